@@ -1,0 +1,427 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 Chimera search path (QPS at Recall@100).
+
+A step is one batch of `--batch` queries through the whole search hot path
+(rotate + LUT, exact centroid probe, stage-1 LUT scoring + aggregation +
+top-k_refine, 1-bit MaxSim refinement, progressive selection, full-bit
+MaxSim, final ordering) over a synthetic corpus with BASELINE config C3's
+shapes (1M docs, ~64M tokens, 262,144 clusters, ex-bits 4, nprobe 128,
+k_refine 3000, k_full_bit 300, 5 chunks, k 100), built on the GPU.
+
+value : queries/s with the queries already in HBM, device-timed (CUDA events
+        on the launching stream, barrier + synchronize on both sides, max over
+        ranks).
+e2e   : queries/s through the public search entry point from pinned host
+        buffers, the query H2D copy and the result D2H copy inside the timed
+        region.
+--impl reference : the CPU implementation (the oracle restatement of the
+        same path with the reference's full-bit scorer order), all host
+        threads, on a bounded sample of the same workload.
+
+The corpus (≈8 GB of index) is larger than L2, so no L2 flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index=0):
+        self.gpu = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q,
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def peaks():
+    try:
+        p = json.load(open(PEAKS))
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def ground_truth(torch, emb, doc_ptrs, queries, k, qsel):
+    """Exact fp32 MaxSim top-k for the selected queries (brute force, GPU)."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n = emb.shape[0]
+    m = doc_ptrs.shape[0] - 1
+    owner = torch.repeat_interleave(torch.arange(m, device=emb.device), doc_ptrs[1:] - doc_ptrs[:-1])
+    out = []
+    chunk = 1 << 23
+    for q in qsel:
+        qt = queries[q]                                    # [32, d]
+        best = torch.full((qt.shape[0], m), -float("inf"), device=emb.device)
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            sc = qt @ emb[s:e].T                           # [32, chunk]
+            best.scatter_reduce_(1, owner[s:e].unsqueeze(0).expand(qt.shape[0], -1), sc, reduce="amax")
+        score = best.sum(0)
+        out.append(torch.topk(score, k).indices.cpu().numpy())
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--recall-queries", type=int, default=32)
+    ap.add_argument("--cpu-sample", type=int, default=4, help="queries timed on the CPU baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    import torch
+    from chimera_b200 import capi, workloads as W
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    if args.impl == "reference" and rank != 0:
+        return
+
+    cfg = W.CONFIGS[args.config]
+    t0 = time.time()
+    # every rank holds a full replica and serves its own query stream
+    emb, doclens, queries = W.generate_torch(cfg, seed=0)
+    log(f"[bench] corpus {cfg.name}: {emb.shape[0]} tokens, {cfg.num_docs} docs ({time.time() - t0:.1f}s)")
+    dl_host = doclens.cpu().numpy()
+    t0 = time.time()
+    index, _ = capi.build_index(emb, dl_host, cfg.n_clusters, cfg.ex_bits)
+    torch.cuda.synchronize()
+    log(f"[bench] index built in {time.time() - t0:.1f}s")
+
+    if args.impl == "reference":
+        run_reference(args, cfg, index, queries, torch)
+        return
+
+    B = args.batch
+    searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
+    nq_total = queries.shape[0]
+    # rank r serves queries offset by r (weak scaling: fixed batch per GPU)
+    def batch_at(i):
+        s = ((i + rank) * B) % nq_total
+        idx = torch.arange(s, s + B, device=queries.device) % nq_total
+        return queries[idx].contiguous()
+
+    stream = torch.cuda.current_stream()
+    res = torch.empty(B, cfg.k, dtype=torch.int64, device="cuda")
+    nres = torch.empty(B, dtype=torch.int32, device="cuda")
+    batches = [batch_at(i) for i in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        searcher.search_device(batches[i], res, nres)
+    torch.cuda.synchronize()
+    if nres.min().item() < 0:
+        raise RuntimeError("stage-1 table overflow during warmup")
+
+    # ---- device-timed value -------------------------------------------------
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        for i in range(args.steps):
+            searcher.search_device(batches[args.warmup + i], res, nres)
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    ms_per_step = ms / args.steps
+    qps = world * B * args.steps / (ms / 1e3)
+
+    # ---- per-stage profile (CUDA events between stage calls) ---------------
+    stages = profile_stages(torch, capi, index, searcher, batches[args.warmup], cfg)
+
+    # ---- end-to-end through the public entry point, host buffers -----------
+    hq = [batches[args.warmup + i].cpu().pin_memory() for i in range(args.steps)]
+    hres = torch.empty(B, cfg.k, dtype=torch.int64).pin_memory()
+    dq = torch.empty_like(batches[0])
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        dq.copy_(hq[i], non_blocking=True)
+        searcher.search_device(dq, res, nres)
+        hres.copy_(res, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    ems = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = t.item()
+    e2e_qps = world * B * args.steps / (ems / 1e3)
+
+    # ---- latency percentiles (single-query batches, as gpu_search times) ---
+    lat = latency_percentiles(torch, capi, index, cfg, queries, n=64)
+
+    # ---- recall ------------------------------------------------------------
+    nrec = min(args.recall_queries, nq_total)
+    qsel = list(range(nrec))
+    r_all, n_all = searcher.search(queries[:nrec].contiguous())
+    gt = ground_truth(torch, emb, index.doc_ptrs, queries, cfg.k, qsel)
+    recall = W.recall_at_k(np.stack(gt), r_all.cpu().numpy(), cfg.k)
+
+    hbm, bf16, kind = peaks()
+    dom = max(stages, key=lambda s: s["ms"])
+    achieved = dom["algo_bytes"] / (dom["ms"] / 1e3) / 1e9 if dom["bound"] == "hbm" else \
+        dom["algo_flops"] / (dom["ms"] / 1e3) / 1e12
+    peak = hbm if dom["bound"] == "hbm" else bf16
+    line = {
+        "metric": "QPS at Recall@100 (C3 passage corpus)",
+        "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32+u8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: {cfg.num_docs} docs, {int(emb.shape[0])} tokens, "
+                               f"{cfg.n_clusters} clusters, ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, "
+                               f"k_refine {cfg.k_refine}, k_full_bit {cfg.k_full_bit}, k {cfg.k}",
+                   "batch_queries": B, "l2": "inputs larger than L2 (index >> 126 MB)",
+                   "recall@100": round(recall, 4), "recall_queries": nrec,
+                   "latency_ms_single_query": lat, "parallelism": f"replica x{world}"},
+        "e2e": {"value": round(e2e_qps, 2), "unit": "queries/s",
+                "h2d_bytes_per_step": int(B * 32 * cfg.dim * 4), "d2h_bytes_per_step": int(B * cfg.k * 8)},
+        "roofline": {"kernel": dom["name"], "bound": dom["bound"], "achieved": round(achieved, 2),
+                     "peak": peak, "unit": "GB/s" if dom["bound"] == "hbm" else "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": kind},
+        "stages_ms_per_step": {s["name"]: round(s["ms"], 3) for s in stages},
+        "gpu_launches": int(sum(s["launches"] for s in stages) * args.steps),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, cfg, index, queries, torch)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def profile_stages(torch, capi, index, searcher, q, cfg):
+    """Runs the pipeline stage by stage on the launching stream with CUDA
+    events between stages (same kernels as chm_search) and returns per-stage
+    device time with each stage's algorithmic bytes / flops."""
+    import ctypes as C
+    L = capi.lib()
+    B = q.shape[0]
+    P = capi._ptr
+    st = capi._stream(torch)
+    dev = q.device
+    p = searcher.params
+    ntok = B * 32
+    rot = torch.empty(ntok, 128, device=dev)
+    cb1 = torch.empty(ntok, device=dev)
+    cbex = torch.empty(ntok, device=dev)
+    lut = torch.empty(ntok, 512, device=dev)
+    labels = torch.empty(ntok, p.nprobe, dtype=torch.int32, device=dev)
+    pb = L.chm_probe_workspace_bytes(ntok, index.n_clusters, p.nprobe)
+    pws = torch.empty(pb, dtype=torch.uint8, device=dev)
+    sb = L.chm_stage1_workspace_bytes(C.byref(index.view), B, p.nprobe, p.k_refine)
+    sws = torch.empty(sb, dtype=torch.uint8, device=dev)
+    rd = torch.empty(B, p.k_refine, dtype=torch.int32, device=dev)
+    rp = torch.empty(B, p.k_refine, device=dev)
+    nr = torch.empty(B, dtype=torch.int32, device=dev)
+    ob = torch.empty(B, p.k_refine, device=dev)
+    fd = torch.empty(B, p.k_refine, dtype=torch.int32, device=dev)
+    nf = torch.empty(B, dtype=torch.int32, device=dev)
+    fs = torch.empty(B, p.k_refine, device=dev)
+    res = torch.empty(B, p.k, dtype=torch.int64, device=dev)
+    nres = torch.empty(B, dtype=torch.int32, device=dev)
+    v = C.byref(index.view)
+    stages = [
+        ("prepare", 1, lambda: L.chm_prepare_queries(P(index.flips), index.dim, index.ex_bits, P(q), ntok, P(rot),
+                                                    P(cb1), P(cbex), P(lut), st)),
+        ("probe", 2, lambda: L.chm_probe(P(rot), ntok, P(index.centroids), P(index.centroid_norms), index.n_clusters,
+                                         p.nprobe, P(labels), P(pws), pb, st)),
+        ("stage1", 4, lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe, p.k_refine, P(rd), P(rp),
+                                           P(nr), None, P(sws), sb, st)),
+        ("refine_1bit", 1, lambda: L.chm_refine_1bit(v, B, P(lut), P(cb1), P(rd), P(nr), p.k_refine, P(ob), st)),
+        ("select_fullbit", 1, lambda: L.chm_select_fullbit(B, P(rd), P(ob), P(nr), p.k_refine, p.k_full_bit,
+                                                           p.num_chunks, P(fd), P(nf), p.k_refine, st)),
+        ("fullbit", 1, lambda: L.chm_fullbit_score(v, B, P(rot), P(cbex), P(fd), P(nf), p.k_refine, P(fs), st)),
+        ("final_topk", 1, lambda: L.chm_final_topk(B, P(fd), P(fs), P(nf), p.k_refine, p.k, P(res), P(nres), st)),
+    ]
+    times = {n: 0.0 for n, _, _ in stages}
+    reps = 3
+    stream = torch.cuda.current_stream()
+    for r in range(reps + 1):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)]
+        evs[0].record(stream)
+        for i, (n, _, f) in enumerate(stages):
+            capi.check(f(), n)
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+        if r > 0:
+            for i, (n, _, _) in enumerate(stages):
+                times[n] += evs[i].elapsed_time(evs[i + 1]) / reps
+    # algorithmic work per step
+    cp = index.cluster_pos
+    lens = (cp[1:] - cp[:-1]).to(torch.int64)
+    lab = labels.view(B, 32, p.nprobe).to(torch.int64)
+    uniq_bytes = 0
+    for b in range(B):
+        u = torch.unique(lab[b])
+        uniq_bytes += int(lens[u].sum().item()) * 24
+    nrh = nr.cpu().numpy()
+    dp = index.doc_ptrs
+    ref_tok = 0
+    for b in range(B):
+        d = rd[b, :nrh[b]].to(torch.int64)
+        ref_tok += int((dp[d + 1] - dp[d]).sum().item())
+    nfh = nf.cpu().numpy()
+    fb_tok = 0
+    for b in range(B):
+        d = fd[b, :nfh[b]].to(torch.int64)
+        fb_tok += int((dp[d + 1] - dp[d]).sum().item())
+    w = 1 + index.ex_bits
+    out = []
+    for n, launches, _ in stages:
+        s = {"name": n, "ms": times[n], "launches": launches, "bound": "hbm", "algo_bytes": 0, "algo_flops": 0}
+        if n == "probe":
+            s.update(bound="tensor", algo_flops=2.0 * ntok * index.n_clusters * 128)
+        elif n == "stage1":
+            s["algo_bytes"] = uniq_bytes
+        elif n == "refine_1bit":
+            s["algo_bytes"] = ref_tok * 24
+        elif n == "fullbit":
+            s["algo_bytes"] = fb_tok * (16 * w + 4)
+        out.append(s)
+    return out
+
+
+def latency_percentiles(torch, capi, index, cfg, queries, n=64):
+    s1 = capi.Searcher(index, k=cfg.k, batch=1, **cfg.search_kwargs())
+    res = torch.empty(1, cfg.k, dtype=torch.int64, device="cuda")
+    nres = torch.empty(1, dtype=torch.int32, device="cuda")
+    lat = []
+    for i in range(n + 3):
+        q = queries[i % queries.shape[0]:i % queries.shape[0] + 1].contiguous()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        s1.search_device(q, res, nres)
+        torch.cuda.synchronize()
+        if i >= 3:
+            lat.append((time.perf_counter() - t) * 1e3)
+    lat = np.sort(np.array(lat))
+    pct = lambda p: float(np.interp(p / 100 * (len(lat) - 1), np.arange(len(lat)), lat))
+    return {"p50": round(pct(50), 3), "p99": round(pct(99), 3), "mean": round(float(lat.mean()), 3)}
+
+
+def _host_index(index):
+    from oracle import oracle as O
+    return O.Index(**index.to_host())
+
+
+def cpu_baseline(args, cfg, index, queries, torch, sample=None):
+    """The oracle (plain-C restatement of the path, full-bit stage in the
+    reference's AVX-512 order) on all host cores over a bounded sample."""
+    from oracle import oracle as O
+    sample = sample or args.cpu_sample
+    threads = os.cpu_count()
+    hidx = _host_index(index)
+    q = queries[:sample].contiguous()
+    ntok = sample * 32
+    rot = O.rotate(index.flips.cpu().numpy(), q.reshape(-1, q.shape[-1]).cpu().numpy()).reshape(sample, 32, 128)
+    cb1, cbex = O.query_state(rot, cfg.ex_bits)
+    cents = index.centroids.cpu().numpy()
+    cn = index.centroid_norms.cpu().numpy()
+    t0 = time.perf_counter()
+    labels = O.probe(rot.reshape(ntok, 128), cents, cn, cfg.nprobe, threads).reshape(sample, 32, cfg.nprobe)
+    t1 = time.perf_counter()
+    hidx.search_batch(rot, cb1, cbex, labels, cfg.nprobe, cfg.k_refine, cfg.k_full_bit, cfg.num_chunks, cfg.k,
+                      threads)
+    t2 = time.perf_counter()
+    return {"value": round(sample / (t2 - t0), 4), "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} queries of the same workload (probe {t1 - t0:.2f}s + search {t2 - t1:.2f}s)"}
+
+
+def run_reference(args, cfg, index, queries, torch):
+    steps, warm = args.steps, args.warmup
+    per = max(1, args.cpu_sample // 2)
+    vals = []
+    for i in range(warm + steps):
+        r = cpu_baseline(args, cfg, index, queries[(i * per) % queries.shape[0]:], torch, sample=per)
+        if i >= warm:
+            vals.append(r["value"])
+    v = float(np.mean(vals))
+    line = {"impl": "reference", "metric": "QPS at Recall@100 (C3 passage corpus)", "value": round(v, 4),
+            "unit": "queries/s", "n_gpus": 1, "steps": steps, "warmup": warm, "higher_is_better": True,
+            "data": "synthetic", "config": {"workload": cfg.name},
+            "cpu_baseline": {"value": round(v, 4), "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{per} queries per step"},
+            "e2e": {"value": round(v, 4), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,308 @@
+"""ctypes binding of the C ABI (include/chimera_b200.h) plus the device-side
+index container and the GPU index build used by the Python entry points.
+
+Torch is used only as device-memory / stream plumbing: every computation on
+the search path runs in the sm_100a kernels of ``lib/libchimera_b200.so``.
+There is no CPU fallback; importing this module without the built library
+raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libchimera_b200.so")
+CORE_PATH = os.path.join(HERE, "lib", "libchimera_core.so")
+HOST_RNG_PATH = os.path.join(HERE, "lib", "libchimera_hostrng.so")
+
+DIM = 128
+QLEN = 32
+
+CHM_OK, CHM_ERR_INVALID, CHM_ERR_CAPACITY, CHM_ERR_CUDA, CHM_ERR_TIMEOUT, CHM_ERR_UNSUPPORTED = range(6)
+_STATUS = {1: "invalid argument", 2: "capacity", 3: "CUDA error", 4: "timeout", 5: "unsupported"}
+
+
+class ChmError(RuntimeError):
+    def __init__(self, status, where):
+        msg = f"{where}: {_STATUS.get(status, status)}"
+        err = _lib_handle.chm_last_error().decode() if _lib_handle is not None else ""
+        if status == CHM_ERR_CUDA and err:
+            msg += f" ({err})"
+        super().__init__(msg)
+        self.status = status
+
+
+class ChmIndex(C.Structure):
+    _fields_ = [
+        ("n_tokens", C.c_int64), ("num_docs", C.c_int64), ("n_clusters", C.c_int64),
+        ("ex_bits", C.c_int32), ("dim", C.c_int32), ("max_list_len", C.c_int32), ("reserved", C.c_int32),
+        ("cluster_pos", C.c_void_p), ("codes1", C.c_void_p), ("factor1", C.c_void_p),
+        ("doc_ids", C.c_void_p), ("tok2pos", C.c_void_p), ("doc_ptrs", C.c_void_p),
+        ("full_codes", C.c_void_p), ("full_factors", C.c_void_p), ("centroids", C.c_void_p),
+        ("centroid_norms", C.c_void_p), ("flips", C.c_void_p),
+    ]
+
+
+class SearchParams(C.Structure):
+    _fields_ = [("nprobe", C.c_int32), ("k_refine", C.c_int32), ("k_full_bit", C.c_int32),
+                ("num_chunks", C.c_int32), ("k", C.c_int32), ("batch", C.c_int32),
+                ("table_log2_extra", C.c_int32)]
+
+
+_lib_handle = None
+_rng_handle = None
+V = C.c_void_p
+I64 = C.c_int64
+I32 = C.c_int32
+SZ = C.c_size_t
+
+EXPORTS = {
+    "chm_version": ([], C.c_char_p),
+    "chm_last_error": ([], C.c_char_p),
+    "chm_search_workspace_bytes": ([V, V], SZ),
+    "chm_search": ([V, V, V, I64, V, V, V, SZ, V], C.c_int),
+    "chm_prepare_queries": ([V, I32, I32, V, I64, V, V, V, V, V], C.c_int),
+    "chm_probe_workspace_bytes": ([I64, I64, I32], SZ),
+    "chm_probe": ([V, I64, V, V, I64, I32, V, V, SZ, V], C.c_int),
+    "chm_stage1_workspace_bytes": ([V, I32, I32, I32], SZ),
+    "chm_stage1": ([V, I32, V, V, V, I32, I32, V, V, V, V, V, SZ, V], C.c_int),
+    "chm_refine_1bit": ([V, I32, V, V, V, V, I32, V, V], C.c_int),
+    "chm_select_fullbit": ([I32, V, V, V, I32, I32, I32, V, V, I32, V], C.c_int),
+    "chm_fullbit_score": ([V, I32, V, V, V, V, I32, V, V], C.c_int),
+    "chm_final_topk": ([I32, V, V, V, I32, I32, V, V, V], C.c_int),
+    "chm_merge_topk": ([I32, I32, I32, V, V, V, V, V, V, V], C.c_int),
+    "chm_build_assign_workspace_bytes": ([I64], SZ),
+    "chm_build_assign": ([V, I64, I32, V, V, I64, V, V, SZ, V], C.c_int),
+    "chm_build_encode": ([V, V, I64, I32, I32, V, V, V, V, V, V], C.c_int),
+    "chm_row_norms": ([V, I64, V, V], C.c_int),
+}
+
+
+def lib():
+    """The CUDA library; raises if it has not been built."""
+    global _lib_handle
+    if _lib_handle is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"chimera_b200 CUDA library missing: {LIB_PATH} "
+                               "(run `python -m chimera_b200.build`)")
+        L = C.CDLL(LIB_PATH)
+        for name, (args, res) in EXPORTS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib_handle = L
+    return _lib_handle
+
+
+def host_rng():
+    global _rng_handle
+    if _rng_handle is None:
+        R = C.CDLL(HOST_RNG_PATH)
+        R.chm_host_fhtkac_flips.argtypes = [C.c_uint64, V, SZ]
+        R.chm_host_sample_centroids.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, V]
+        _rng_handle = R
+    return _rng_handle
+
+
+def check(status, where):
+    if status != CHM_OK:
+        raise ChmError(status, where)
+
+
+def fhtkac_flips(seed: int = 42) -> np.ndarray:
+    out = np.zeros(64, np.uint8)
+    host_rng().chm_host_fhtkac_flips(seed, out.ctypes.data, 64)
+    return out
+
+
+def sample_centroids(num_embeddings: int, n_clusters: int, seed: int = 42) -> np.ndarray:
+    ids = np.zeros(n_clusters, np.uint64)
+    host_rng().chm_host_sample_centroids(num_embeddings, n_clusters, seed, ids.ctypes.data)
+    return ids.astype(np.int64)
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+
+def _stream(torch, stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+class DeviceIndex:
+    """Device-resident index arrays (torch tensors) + the chm_index view."""
+
+    FIELDS = ("cluster_pos", "codes1", "factor1", "doc_ids", "tok2pos", "doc_ptrs", "full_codes",
+              "full_factors", "centroids", "centroid_norms", "flips")
+
+    def __init__(self, *, dim, ex_bits, **arrays):
+        import torch
+        self.torch = torch
+        self.dim = int(dim)
+        self.ex_bits = int(ex_bits)
+        for k in self.FIELDS:
+            setattr(self, k, arrays[k])
+        self.n_tokens = int(self.factor1.shape[0])
+        self.num_docs = int(self.doc_ptrs.shape[0] - 1)
+        self.n_clusters = int(self.cluster_pos.shape[0] - 1)
+        lens = self.cluster_pos[1:] - self.cluster_pos[:-1]
+        self.max_list_len = int(lens.max().item()) if self.n_clusters else 0
+        self.view = ChmIndex(self.n_tokens, self.num_docs, self.n_clusters, self.ex_bits, self.dim,
+                             self.max_list_len, 0, *[self._p(getattr(self, k)) for k in self.FIELDS])
+
+    @staticmethod
+    def _p(t):
+        return t.data_ptr()
+
+    @classmethod
+    def from_host(cls, *, cluster_pos, codes1, factor1, doc_ids, tok2pos, doc_ptrs, full_codes,
+                  full_factors, centroids_rot, flips, dim, ex_bits, device="cuda"):
+        """Upload host arrays in the reference layout (oracle.Index fields)."""
+        import torch
+        dev = torch.device(device)
+        t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).astype(dt, copy=False)).to(dev)
+        cents = t(centroids_rot, np.float32)
+        norms = torch.empty(cents.shape[0], dtype=torch.float32, device=dev)
+        check(lib().chm_row_norms(_ptr(cents), cents.shape[0], _ptr(norms), _stream(torch)), "row_norms")
+        return cls(dim=dim, ex_bits=ex_bits, cluster_pos=t(cluster_pos, np.int64),
+                   codes1=t(codes1, np.uint8), factor1=t(factor1, np.float32),
+                   doc_ids=t(doc_ids, np.int32), tok2pos=t(tok2pos, np.int32),
+                   doc_ptrs=t(doc_ptrs, np.int64), full_codes=t(full_codes, np.uint8),
+                   full_factors=t(full_factors, np.float32), centroids=cents, centroid_norms=norms,
+                   flips=t(flips, np.uint8))
+
+    def to_host(self):
+        """Host copies in the reference layout (for the oracle)."""
+        g = lambda x: x.cpu().numpy()
+        return dict(cluster_pos=g(self.cluster_pos), codes1=g(self.codes1), factor1=g(self.factor1),
+                    doc_ids=g(self.doc_ids), tok2pos=g(self.tok2pos).view(np.uint32),
+                    doc_ptrs=g(self.doc_ptrs), full_codes=g(self.full_codes),
+                    full_factors=g(self.full_factors), ex_bits=self.ex_bits)
+
+
+def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, stream=None):
+    """GPU index build (chimera_index::build, build_index.cu:394-501) from a
+    device tensor of raw embeddings [N, dim] and host doc lengths.
+
+    Reservoir-sampled centroids (host, std::mt19937_64) -> exact nearest
+    centroid on the GPU -> stable cluster order -> GPU rotation + RaBitQ
+    encoding -> cluster-ordered 1-bit arrays."""
+    import torch
+    dev = emb.device
+    st = _stream(torch, stream)
+    n, dim = int(emb.shape[0]), int(emb.shape[1])
+    doclens = np.asarray(doclens, np.int64)
+    if doclens.sum() != n:
+        raise ValueError("Document lengths do not sum to the number of embeddings")
+    flips_np = fhtkac_flips(seed)
+    flips = torch.from_numpy(flips_np).to(dev)
+    ids = torch.from_numpy(sample_centroids(n, n_clusters, 42)).to(dev)
+    if dim < DIM:
+        x128 = torch.zeros(n, DIM, dtype=torch.float32, device=dev)
+        x128[:, :dim] = emb
+    else:
+        x128 = emb.contiguous()
+    cent_raw = x128[ids].contiguous()
+    cn_raw = torch.empty(n_clusters, dtype=torch.float32, device=dev)
+    L = lib()
+    check(L.chm_row_norms(_ptr(cent_raw), n_clusters, _ptr(cn_raw), st), "row_norms")
+    assign = torch.empty(n, dtype=torch.int32, device=dev)
+    wsb = L.chm_build_assign_workspace_bytes(n)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+    check(L.chm_build_assign(_ptr(x128), n, dim, _ptr(cent_raw), _ptr(cn_raw), n_clusters, _ptr(assign),
+                             _ptr(ws), wsb, st), "build_assign")
+    del ws
+    # rotated centroids (padded dim) for the probe
+    rot_c = torch.empty(n_clusters, DIM, dtype=torch.float32, device=dev)
+    cb1_c = torch.empty(n_clusters, dtype=torch.float32, device=dev)
+    cbex_c = torch.empty(n_clusters, dtype=torch.float32, device=dev)
+    cent_in = emb[ids].contiguous()
+    check(L.chm_prepare_queries(_ptr(flips), dim, ex_bits, _ptr(cent_in), n_clusters,
+                                _ptr(rot_c), _ptr(cb1_c), _ptr(cbex_c), None, st), "rotate centroids")
+    cnorm = torch.empty(n_clusters, dtype=torch.float32, device=dev)
+    check(L.chm_row_norms(_ptr(rot_c), n_clusters, _ptr(cnorm), st), "row_norms")
+    # IVF_PG::build_from_assignments: stable counting sort (ivf_pg.cpp:110-126)
+    a64 = assign.to(torch.int64)
+    inv = torch.sort(a64, stable=True).indices
+    counts = torch.bincount(a64, minlength=n_clusters)
+    cluster_pos = torch.zeros(n_clusters + 1, dtype=torch.int64, device=dev)
+    cluster_pos[1:] = torch.cumsum(counts, 0)
+    # rotation + RaBitQ encoding
+    fb = DIM * (1 + ex_bits) // 8
+    codes1 = torch.empty(n, 16, dtype=torch.uint8, device=dev)
+    f1 = torch.empty(n, dtype=torch.float32, device=dev)
+    full = torch.empty(n, fb, dtype=torch.uint8, device=dev)
+    ff = torch.empty(n, dtype=torch.float32, device=dev)
+    check(L.chm_build_encode(_ptr(flips), _ptr(emb.contiguous()), n, dim, ex_bits, _ptr(codes1), _ptr(f1),
+                             _ptr(full), _ptr(ff), None, st), "build_encode")
+    dl = torch.from_numpy(doclens).to(dev)
+    doc_ptrs = torch.zeros(len(doclens) + 1, dtype=torch.int64, device=dev)
+    doc_ptrs[1:] = torch.cumsum(dl, 0)
+    owner = torch.repeat_interleave(torch.arange(len(doclens), device=dev, dtype=torch.int32), dl)
+    tok2pos = torch.empty(n, dtype=torch.int32, device=dev)
+    tok2pos[inv] = torch.arange(n, dtype=torch.int32, device=dev)
+    return DeviceIndex(dim=dim, ex_bits=ex_bits, cluster_pos=cluster_pos,
+                       codes1=codes1[inv].contiguous(), factor1=f1[inv].contiguous(),
+                       doc_ids=owner[inv].contiguous(), tok2pos=tok2pos, doc_ptrs=doc_ptrs,
+                       full_codes=full, full_factors=ff, centroids=rot_c, centroid_norms=cnorm,
+                       flips=flips), dict(assign=assign, inv=inv, token_codes1=codes1, token_f1=f1)
+
+
+class Searcher:
+    """Batched GPU search over a DeviceIndex through chm_search."""
+
+    def __init__(self, index: DeviceIndex, *, nprobe=128, k_refine=3000, k_full_bit=300, num_chunks=5,
+                 k=100, batch=16):
+        import torch
+        self.torch = torch
+        self.index = index
+        self.params = SearchParams(nprobe, k_refine, k_full_bit, num_chunks, k, batch, 0)
+        self._ws = None
+        self._alloc()
+
+    def _alloc(self):
+        L = lib()
+        nb = L.chm_search_workspace_bytes(C.byref(self.index.view), C.byref(self.params))
+        if nb == 0:
+            raise ValueError("invalid search parameters")
+        self._ws = self.torch.empty(nb, dtype=self.torch.uint8, device=self.index.factor1.device)
+        self.ws_bytes = nb
+
+    def search_device(self, queries, results=None, num_results=None, stream=None):
+        """queries: [Q, 32, dim] float32 device tensor."""
+        torch = self.torch
+        q = queries.contiguous()
+        nq = int(q.shape[0])
+        k = self.params.k
+        if results is None:
+            results = torch.empty(nq, k, dtype=torch.int64, device=q.device)
+        if num_results is None:
+            num_results = torch.empty(nq, dtype=torch.int32, device=q.device)
+        check(lib().chm_search(C.byref(self.index.view), C.byref(self.params), _ptr(q), nq, _ptr(results),
+                               _ptr(num_results), _ptr(self._ws), self.ws_bytes, _stream(torch, stream)),
+              "search")
+        return results, num_results
+
+    def search(self, queries, stream=None):
+        """Search with automatic retry of queries whose stage-1 table overflowed."""
+        torch = self.torch
+        res, nres = self.search_device(queries, stream=stream)
+        bad = (nres < 0).nonzero().flatten()
+        extra = 0
+        while bad.numel() > 0 and extra < 6:
+            extra += 1
+            saved = self.params.table_log2_extra
+            self.params.table_log2_extra = extra
+            self._alloc()
+            r2, n2 = self.search_device(queries[bad], stream=stream)
+            res[bad], nres[bad] = r2, n2
+            self.params.table_log2_extra = saved
+            self._alloc()
+            bad = (nres < 0).nonzero().flatten()
+        if bad.numel() > 0:
+            raise ChmError(CHM_ERR_CAPACITY, "search")
+        return res, nres

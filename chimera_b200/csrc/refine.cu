@@ -1,0 +1,371 @@
+// Refinement: segmented 1-bit MaxSim of the refined docs, the reference's
+// progressive chunked selection of docs to full-bit score, the
+// (1+ex_bits)-bit MaxSim itself (moved from the reference's AVX-512 host
+// loop onto the GPU with the same arithmetic order), and the final ordering.
+#include "codes.cuh"
+#include "common.cuh"
+
+namespace chm {
+
+constexpr int kRefineWarps = 8;
+
+// One warp per refined document; all 32 query-token LUTs in shared memory.
+// Replaces gather_refined_doc_lengths/positions, one_bit_token_score and
+// one_bit_document_score (kernels.cu:430-617) without materialising the
+// [32 x tokens] score matrix.
+__global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
+    const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
+    const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
+    const float* __restrict__ lut, const float* __restrict__ cb1,
+    const int32_t* __restrict__ refined_docs, const int32_t* __restrict__ num_refined, int k_refine,
+    float* __restrict__ scores) {
+    extern __shared__ float s_lut[];  // [32][512]
+    __shared__ float s_cb1[kQ];
+    const int q = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int R = num_refined[q];
+    if ((int)blockIdx.x * kRefineWarps >= R) return;
+    const float4* src = reinterpret_cast<const float4*>(lut + (size_t)q * kQ * kLutPerQ);
+    for (int i = threadIdx.x; i < kQ * kLutPerQ / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(s_lut)[i] = src[i];
+    if (threadIdx.x < kQ) s_cb1[threadIdx.x] = cb1[q * kQ + threadIdx.x];
+    __syncthreads();
+    const int r = blockIdx.x * kRefineWarps + warp;
+    if (r >= R) return;
+    const int64_t doc = refined_docs[(size_t)q * k_refine + r];
+    const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
+    float m[kQ];
+#pragma unroll
+    for (int t = 0; t < kQ; ++t) m[t] = -FLT_MAX;
+    for (int64_t tok = t0 + lane; tok < t1; tok += 32) {
+        const uint32_t pos = tok2pos[tok];
+        const uint4 code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
+        const float f = __ldg(factor1 + pos);
+#pragma unroll
+        for (int t = 0; t < kQ; ++t) {
+            const float ip = lut_ip(s_lut + t * kLutPerQ, code);
+            m[t] = fmaxf(m[t], fmul(fsub(ip, s_cb1[t]), f));
+        }
+    }
+    float mine = 0.0f;
+#pragma unroll
+    for (int t = 0; t < kQ; ++t) {
+        float x = m[t];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+        if (lane == t) mine = x;
+    }
+    // one_bit_document_score_kernel's 128-thread tree (kernels.cu:557-570):
+    // 0.0f + max, two zero strides, then 16, 8, 4, 2, 1.
+    float x = fadd(fadd(fadd(0.0f, mine), 0.0f), 0.0f);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+    if (lane == 0) scores[(size_t)q * k_refine + r] = x;
+}
+
+__device__ uint32_t excl_scan_1024(uint32_t v, uint32_t* s_warp, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t w = (lane < (int)(blockDim.x >> 5)) ? s_warp[lane] : 0;
+        uint32_t z = w;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, z, off);
+            if (lane >= off) z += y;
+        }
+        s_warp[lane] = z - w;
+        if (lane == 31) s_warp[32] = z;
+    }
+    __syncthreads();
+    const uint32_t r = s_warp[warp] + x - v;
+    *total = s_warp[32];
+    __syncthreads();
+    return r;
+}
+
+__device__ void sort_desc_u64(uint64_t* a, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint64_t x = a[i], y = a[l];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (x < y) : (x > y)) { a[i] = y; a[l] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// search_impl.cu:341-494.  After chunk c the reference has full-bit scored
+// the top min(T*(c+1)/nch, min(T, end_c)) docs (by 1-bit score) of the
+// refined prefix [0, end_c); the union over chunks is what gets scored.
+// Ties in the 1-bit score resolve to the lower refined index.
+__global__ void __launch_bounds__(1024) select_fullbit_kernel(
+    const int32_t* __restrict__ refined_docs, const float* __restrict__ onebit,
+    const int32_t* __restrict__ num_refined, int k_refine, int k_full_bit, int num_chunks,
+    int32_t* __restrict__ fb_docs, int32_t* __restrict__ num_fb, int fb_cap) {
+    extern __shared__ uint64_t s_keys[];   // [sort_n]
+    __shared__ uint8_t s_chosen[CHM_MAX_K_REFINE];
+    __shared__ uint32_t s_warp[33];
+    const int q = blockIdx.x;
+    const int R = num_refined[q];
+    int sort_n = 1;
+    while (sort_n < R) sort_n <<= 1;
+    for (int i = threadIdx.x; i < sort_n; i += blockDim.x) {
+        if (i < R) {
+            const float s = onebit[(size_t)q * k_refine + i];
+            s_keys[i] = ((uint64_t)float_key_asc(s) << 32) | (uint32_t)(~(uint32_t)i);
+            s_chosen[i] = 0;
+        } else {
+            s_keys[i] = 0;
+        }
+    }
+    __syncthreads();
+    if (R == 0) {
+        if (threadIdx.x == 0) num_fb[q] = 0;
+        return;
+    }
+    sort_desc_u64(s_keys, sort_n);
+    const int T = min(k_full_bit, R);
+    const int nch = min(num_chunks, R);
+    const int cs = (R + nch - 1) / nch;
+    const int per = (R + blockDim.x - 1) / blockDim.x;  // sorted entries per thread
+    for (int c = 0; c < nch; ++c) {
+        const int end = min((c + 1) * cs, R);
+        const int carry = min(T, end);
+        const int cum = min(T * (c + 1) / nch, carry);
+        uint32_t cnt = 0;
+        const int i0 = threadIdx.x * per, i1 = min(R, i0 + per);
+        for (int i = i0; i < i1; ++i) cnt += ((int)(~(uint32_t)s_keys[i]) < end);
+        uint32_t tot;
+        uint32_t rank = excl_scan_1024(cnt, s_warp, &tot);
+        for (int i = i0; i < i1 && (int)rank < cum; ++i) {
+            const int idx = (int)(~(uint32_t)s_keys[i]);
+            if (idx < end) { s_chosen[idx] = 1; ++rank; }
+        }
+        __syncthreads();
+    }
+    // compact chosen refined indices in ascending order
+    const int i0 = threadIdx.x * per, i1 = min(R, i0 + per);
+    uint32_t cnt = 0;
+    for (int i = i0; i < i1; ++i) cnt += s_chosen[i];
+    uint32_t tot;
+    uint32_t at = excl_scan_1024(cnt, s_warp, &tot);
+    for (int i = i0; i < i1; ++i)
+        if (s_chosen[i] && (int)at < fb_cap) fb_docs[(size_t)q * fb_cap + at++] = refined_docs[(size_t)q * k_refine + i];
+    if (threadIdx.x == 0) num_fb[q] = min((int)tot, fb_cap);
+}
+
+// (1+ex_bits)-bit MaxSim, one warp per selected doc.  Lane l = 16h + L
+// computes, for query token 2p + h, the AVX-512 lane-L accumulator of
+// gemv_batch8_avx512 (space.hpp:806-851): fma(decoded[16b + L], q[16b + L])
+// over b = 0..7; shuffles 8, 4, 2, 1 then reproduce _mm512_reduce_add_ps.
+// combined = (ip - cbex) * factor; max over tokens; final sum of the two
+// 16-lane halves reduced the same way (search_impl.cu:538-572).
+__global__ void __launch_bounds__(kRefineWarps * 32) fullbit_kernel(
+    const int64_t* __restrict__ doc_ptrs, const uint8_t* __restrict__ full_codes,
+    const float* __restrict__ full_factors, int w, const float* __restrict__ rot,
+    const float* __restrict__ cbex, const int32_t* __restrict__ fb_docs,
+    const int32_t* __restrict__ num_fb, int fb_cap, float* __restrict__ scores) {
+    __shared__ float s_q[kQ * kDim];
+    __shared__ float s_cbex[kQ];
+    __shared__ float s_m[kRefineWarps][kQ];
+    const int q = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int F = num_fb[q];
+    if ((int)blockIdx.x * kRefineWarps >= F) return;
+    for (int i = threadIdx.x; i < kQ * kDim; i += blockDim.x) s_q[i] = rot[(size_t)q * kQ * kDim + i];
+    if (threadIdx.x < kQ) s_cbex[threadIdx.x] = cbex[q * kQ + threadIdx.x];
+    __syncthreads();
+    const int i = blockIdx.x * kRefineWarps + warp;
+    if (i >= F) return;
+    const int64_t doc = fb_docs[(size_t)q * fb_cap + i];
+    const int half = lane >> 4, L = lane & 15;
+    const size_t stride = (size_t)kDim * w / 8;
+    float m[kQ / 2];
+#pragma unroll
+    for (int p = 0; p < kQ / 2; ++p) m[p] = -INFINITY;
+    for (int64_t tok = doc_ptrs[doc]; tok < doc_ptrs[doc + 1]; ++tok) {
+        const uint8_t* code = full_codes + (size_t)tok * stride;
+        float dec[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) dec[b] = (float)code_at(code, 16 * b + L, w);
+        const float f = full_factors[tok];
+#pragma unroll
+        for (int p = 0; p < kQ / 2; ++p) {
+            const int t = 2 * p + half;
+            const float* qt = s_q + t * kDim;
+            float s = 0.0f;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) s = __fmaf_rn(dec[b], qt[16 * b + L], s);
+#pragma unroll
+            for (int off = 8; off >= 1; off >>= 1) s = fadd(s, __shfl_down_sync(0xffffffffu, s, off, 16));
+            const float comb = fmul(fsub(s, s_cbex[t]), f);
+            m[p] = fmaxf(m[p], comb);
+        }
+    }
+    if (L == 0) {
+#pragma unroll
+        for (int p = 0; p < kQ / 2; ++p) s_m[warp][2 * p + half] = m[p];
+    }
+    __syncwarp();
+    float x = 0.0f;
+    if (lane < 16) x = fadd(s_m[warp][lane], s_m[warp][16 + lane]);
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
+    if (lane == 0) scores[(size_t)q * fb_cap + i] = x;
+}
+
+// std::priority_queue<std::pair<float, size_t>> pop order: score desc, doc
+// desc (search_impl.cu:409, 496-500).
+__global__ void __launch_bounds__(1024) final_topk_kernel(
+    const int32_t* __restrict__ fb_docs, const float* __restrict__ fb_scores,
+    const int32_t* __restrict__ num_fb, int fb_cap, int k, int64_t* __restrict__ results,
+    int32_t* __restrict__ num_results) {
+    extern __shared__ uint64_t s_keys[];
+    const int q = blockIdx.x;
+    const int F = num_fb[q];
+    int sort_n = 1;
+    while (sort_n < F) sort_n <<= 1;
+    for (int i = threadIdx.x; i < sort_n; i += blockDim.x) {
+        if (i < F) {
+            const float s = fb_scores[(size_t)q * fb_cap + i];
+            s_keys[i] = ((uint64_t)float_key_asc(s) << 32) | (uint32_t)fb_docs[(size_t)q * fb_cap + i];
+        } else {
+            s_keys[i] = 0;
+        }
+    }
+    __syncthreads();
+    sort_desc_u64(s_keys, sort_n);
+    const int nk = min(k, F);
+    for (int i = threadIdx.x; i < k; i += blockDim.x)
+        results[(size_t)q * k + i] = i < nk ? (int64_t)(uint32_t)s_keys[i] : -1;
+    if (threadIdx.x == 0) num_results[q] = nk;
+}
+
+// Merge of per-shard top-k lists gathered across GPUs (same ordering rule).
+__global__ void __launch_bounds__(1024) merge_topk_kernel(
+    int shards, int k, const float* __restrict__ scores, const int64_t* __restrict__ docs,
+    const int32_t* __restrict__ counts, int64_t* __restrict__ results,
+    float* __restrict__ result_scores, int32_t* __restrict__ num_results) {
+    extern __shared__ uint64_t s_keys[];
+    const int q = blockIdx.x;
+    const int n = shards * k;
+    int sort_n = 1;
+    while (sort_n < n) sort_n <<= 1;
+    for (int i = threadIdx.x; i < sort_n; i += blockDim.x) {
+        uint64_t key = 0;
+        if (i < n) {
+            const int s = i / k, j = i % k;
+            const size_t at = ((size_t)s * gridDim.x + q) * k + j;
+            if (j < counts[(size_t)s * gridDim.x + q])
+                key = ((uint64_t)float_key_asc(scores[at]) << 32) | (uint32_t)docs[at];
+        }
+        s_keys[i] = key;
+    }
+    __syncthreads();
+    sort_desc_u64(s_keys, sort_n);
+    __shared__ int s_n;
+    if (threadIdx.x == 0) {
+        int c = 0;
+        while (c < k && c < n && s_keys[c] != 0) ++c;
+        s_n = c;
+        num_results[q] = c;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const bool ok = i < s_n;
+        results[(size_t)q * k + i] = ok ? (int64_t)(uint32_t)s_keys[i] : -1;
+        if (result_scores) result_scores[(size_t)q * k + i] = ok ? key_to_float_asc((uint32_t)(s_keys[i] >> 32)) : -INFINITY;
+    }
+}
+
+static size_t pow2_bytes(int n) {
+    int s = 1;
+    while (s < n) s <<= 1;
+    return sizeof(uint64_t) * (size_t)s;
+}
+
+template <typename K>
+static chm_status set_smem(K kernel, size_t bytes) {
+    if (bytes > 48 * 1024)
+        CHM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    return CHM_OK;
+}
+
+}  // namespace chm
+
+extern "C" chm_status chm_refine_1bit(const chm_index* idx, int32_t nq, const float* lut,
+                                      const float* cb1, const int32_t* refined_docs,
+                                      const int32_t* num_refined, int32_t k_refine, float* scores,
+                                      void* stream) {
+    if (nq <= 0) return CHM_OK;
+    const size_t smem = sizeof(float) * chm::kQ * chm::kLutPerQ;
+    CHM_TRY(chm::set_smem(chm::refine_1bit_kernel, smem));
+    dim3 g((k_refine + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
+    chm::refine_1bit_kernel<<<g, chm::kRefineWarps * 32, smem, (cudaStream_t)stream>>>(
+        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
+        k_refine, scores);
+    return chm::launch_status("refine_1bit_kernel");
+}
+
+extern "C" chm_status chm_select_fullbit(int32_t nq, const int32_t* refined_docs,
+                                         const float* onebit, const int32_t* num_refined,
+                                         int32_t k_refine, int32_t k_full_bit, int32_t num_chunks,
+                                         int32_t* fb_docs, int32_t* num_fb, int32_t fb_cap,
+                                         void* stream) {
+    if (nq <= 0) return CHM_OK;
+    if (k_refine > CHM_MAX_K_REFINE || k_full_bit <= 0 || num_chunks <= 0) return CHM_ERR_INVALID;
+    const size_t smem = chm::pow2_bytes(k_refine);
+    CHM_TRY(chm::set_smem(chm::select_fullbit_kernel, smem));
+    chm::select_fullbit_kernel<<<nq, 1024, smem, (cudaStream_t)stream>>>(
+        refined_docs, onebit, num_refined, k_refine, k_full_bit, num_chunks, fb_docs, num_fb, fb_cap);
+    return chm::launch_status("select_fullbit_kernel");
+}
+
+extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const float* rot,
+                                        const float* cbex, const int32_t* fb_docs,
+                                        const int32_t* num_fb, int32_t fb_cap, float* scores,
+                                        void* stream) {
+    if (nq <= 0) return CHM_OK;
+    dim3 g((fb_cap + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
+    chm::fullbit_kernel<<<g, chm::kRefineWarps * 32, 0, (cudaStream_t)stream>>>(
+        idx->doc_ptrs, idx->full_codes, idx->full_factors, 1 + idx->ex_bits, rot, cbex, fb_docs,
+        num_fb, fb_cap, scores);
+    return chm::launch_status("fullbit_kernel");
+}
+
+extern "C" chm_status chm_final_topk(int32_t nq, const int32_t* fb_docs, const float* fb_scores,
+                                     const int32_t* num_fb, int32_t fb_cap, int32_t k,
+                                     int64_t* results, int32_t* num_results, void* stream) {
+    if (nq <= 0) return CHM_OK;
+    if (fb_cap > CHM_MAX_K_REFINE || k <= 0) return CHM_ERR_INVALID;
+    const size_t smem = chm::pow2_bytes(fb_cap);
+    CHM_TRY(chm::set_smem(chm::final_topk_kernel, smem));
+    chm::final_topk_kernel<<<nq, 1024, smem, (cudaStream_t)stream>>>(fb_docs, fb_scores, num_fb, fb_cap,
+                                                                     k, results, num_results);
+    return chm::launch_status("final_topk_kernel");
+}
+
+extern "C" chm_status chm_merge_topk(int32_t nq, int32_t shards, int32_t k, const float* scores,
+                                     const int64_t* docs, const int32_t* counts, int64_t* results,
+                                     float* result_scores, int32_t* num_results, void* stream) {
+    if (nq <= 0) return CHM_OK;
+    if (shards <= 0 || k <= 0 || (int64_t)shards * k > 16384) return CHM_ERR_INVALID;
+    const size_t smem = chm::pow2_bytes(shards * k);
+    CHM_TRY(chm::set_smem(chm::merge_topk_kernel, smem));
+    chm::merge_topk_kernel<<<nq, 1024, smem, (cudaStream_t)stream>>>(shards, k, scores, docs, counts,
+                                                                     results, result_scores, num_results);
+    return chm::launch_status("merge_topk_kernel");
+}

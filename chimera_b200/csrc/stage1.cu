@@ -1,0 +1,561 @@
+// Stage 1: candidate generation and partial scoring.
+//
+// Replaces, for a batch of queries and with no host round trip, the
+// reference's mark -> count -> ExclusiveSum -> host sync -> materialize ->
+// partial_score -> sum_partial_scores -> full radix sort pipeline
+// (kernels.cu:117-400, search_impl.cu:118-262).
+//
+//  score   : one CTA per (query token t, split, query); streams t's probed
+//            lists in cluster order (coalesced 16 B code + 4 B factor + 4 B
+//            doc id per element), 1-bit LUT inner product in the reference
+//            order, and for dist > 0 inserts (doc, t, dist) into the query's
+//            open-addressing table with max semantics.
+//  combine : one warp per table bin; the entries homed at a bin are grouped
+//            by doc and summed over the 32 query tokens with the reference's
+//            shuffle-down tree (kernels.cu:192-198), giving 64-bit keys
+//            (partial score bits << 32 | ~doc).
+//  select  : one CTA per query; exact radix select of the top k_refine keys
+//            and a bitonic sort (score desc, doc asc == stable descending
+//            sort of ascending doc ids, search_impl.cu:245-261).
+//  mark    : only for queries with fewer positive docs than k_refine: marks
+//            every visited doc so zero-score candidates fill the refined list
+//            in ascending doc order, as the reference's bitmap does.
+//
+// Table layout: u64 slots, key (doc << 5 | t) in the high word and the
+// float bits of the max positive distance in the low word (positive floats
+// order like their bit patterns, so a 64-bit atomicMax on a slot holding the
+// same key keeps the larger distance).  A doc's entries are homed in one
+// 8-slot bin (slot = bin * 8 + (t & 7)) with linear probing, so every entry
+// homed at bin b lies between slot 8b and the first empty slot at or after
+// slot 8b + 7.
+#include "common.cuh"
+
+namespace chm {
+
+constexpr uint64_t kEmpty = ~0ull;
+constexpr int kScoreThreads = 256;
+constexpr int kSelectThreads = 1024;
+
+__device__ __forceinline__ uint32_t bin_of(uint32_t doc, uint32_t nbins_mask) {
+    return (doc * 0x9E3779B1u) >> 7 & nbins_mask;
+}
+
+struct Stage1Ctx {
+    const int64_t* cluster_pos;
+    const uint8_t* codes1;
+    const float* factor1;
+    const int32_t* doc_ids;
+    int64_t n_clusters;
+    int64_t num_docs;
+    const float* lut;       // [nq][32][512]
+    const float* cb1;       // [nq][32]
+    const uint32_t* labels; // [nq][32][nprobe]
+    int nprobe;
+    uint64_t* tables;       // [nq][H]
+    int log2h;
+    uint32_t* flags;        // [nq] bit0: table overflow
+};
+
+// Exclusive prefix over list lengths of one query token's probed lists.
+__device__ void probe_prefix(const Stage1Ctx& c, const uint32_t* labels, int64_t* s_start,
+                             int* s_prefix) {
+    for (int p = threadIdx.x; p < c.nprobe; p += blockDim.x) {
+        const uint32_t label = labels[p];
+        if ((int64_t)label < c.n_clusters) {
+            const int64_t st = c.cluster_pos[label];
+            s_start[p] = st;
+            s_prefix[p + 1] = (int)(c.cluster_pos[label + 1] - st);
+        } else {
+            s_start[p] = 0;
+            s_prefix[p + 1] = 0;
+        }
+    }
+    if (threadIdx.x == 0) s_prefix[0] = 0;
+    __syncthreads();
+    // Block-wide inclusive scan of s_prefix[1..nprobe] (nprobe <= 1024).
+    for (int off = 1; off < c.nprobe; off <<= 1) {
+        int add[4];
+        int n = 0;
+        for (int p = threadIdx.x; p < c.nprobe; p += blockDim.x, ++n)
+            add[n] = (p >= off) ? s_prefix[p + 1 - off] : 0;
+        __syncthreads();
+        n = 0;
+        for (int p = threadIdx.x; p < c.nprobe; p += blockDim.x, ++n) s_prefix[p + 1] += add[n];
+        __syncthreads();
+    }
+}
+
+__device__ __forceinline__ void table_insert(uint64_t* table, uint32_t hmask, uint32_t nbins_mask,
+                                             uint32_t doc, int t, float dist, uint32_t* flag) {
+    const uint32_t key = (doc << 5) | (uint32_t)t;
+    const uint64_t val = ((uint64_t)key << 32) | __float_as_uint(dist);
+    uint32_t slot = bin_of(doc, nbins_mask) * 8 + (t & 7);
+    for (uint32_t probe = 0; probe <= hmask; ++probe, slot = (slot + 1) & hmask) {
+        uint64_t cur = table[slot];
+        if (cur == kEmpty) {
+            cur = atomicCAS((unsigned long long*)&table[slot], kEmpty, val);
+            if (cur == kEmpty) return;
+        }
+        if ((uint32_t)(cur >> 32) == key) {
+            if (val > cur) atomicMax((unsigned long long*)&table[slot], val);
+            return;
+        }
+    }
+    atomicOr(flag, 1u);
+}
+
+__global__ void __launch_bounds__(kScoreThreads) stage1_score_kernel(Stage1Ctx c, int splits) {
+    __shared__ float s_lut[kLutPerQ];
+    __shared__ int64_t s_start[CHM_MAX_NPROBE];
+    __shared__ int s_prefix[CHM_MAX_NPROBE + 1];
+    const int t = blockIdx.x / splits;
+    const int split = blockIdx.x % splits;
+    const int q = blockIdx.y;
+    const float* lut = c.lut + ((size_t)q * kQ + t) * kLutPerQ;
+    for (int i = threadIdx.x; i < kLutPerQ; i += blockDim.x) s_lut[i] = lut[i];
+    probe_prefix(c, c.labels + ((size_t)q * kQ + t) * c.nprobe, s_start, s_prefix);
+    const int total = s_prefix[c.nprobe];
+    const int per = (total + splits - 1) / splits;
+    const int lo = split * per;
+    const int hi = min(total, lo + per);
+    const float cb1 = c.cb1[q * kQ + t];
+    uint64_t* table = c.tables + ((size_t)q << c.log2h);
+    const uint32_t hmask = (1u << c.log2h) - 1;
+    const uint32_t nbins_mask = (1u << (c.log2h - 3)) - 1;
+    for (int v = lo + threadIdx.x; v < hi; v += blockDim.x) {
+        // upper_bound over the prefix (lists are visited in label order)
+        int a = 0, b = c.nprobe;
+        while (a < b) {
+            const int mid = (a + b) >> 1;
+            if (s_prefix[mid + 1] <= v) a = mid + 1; else b = mid;
+        }
+        const int64_t pos = s_start[a] + (v - s_prefix[a]);
+        const uint4 code = __ldg(reinterpret_cast<const uint4*>(c.codes1) + pos);
+        const float f = __ldg(c.factor1 + pos);
+        const int32_t doc = __ldg(c.doc_ids + pos);
+        const float ip = lut_ip(s_lut, code);
+        const float dist = fmul(fsub(ip, cb1), f);
+        if (dist > 0.0f && doc >= 0 && (int64_t)doc < c.num_docs)
+            table_insert(table, hmask, nbins_mask, (uint32_t)doc, t, dist, c.flags + q);
+    }
+}
+
+// Marks every visited document (reference mark_candidate_documents_kernel,
+// kernels.cu:206-278) for queries whose positive candidates fall short of
+// k_refine.
+__global__ void __launch_bounds__(kScoreThreads) stage1_mark_kernel(
+    Stage1Ctx c, int splits, const uint32_t* n_pos, int k_refine, uint32_t* bitmaps,
+    int64_t words) {
+    __shared__ int64_t s_start[CHM_MAX_NPROBE];
+    __shared__ int s_prefix[CHM_MAX_NPROBE + 1];
+    const int t = blockIdx.x / splits;
+    const int split = blockIdx.x % splits;
+    const int q = blockIdx.y;
+    if ((int)n_pos[q] >= k_refine) return;
+    probe_prefix(c, c.labels + ((size_t)q * kQ + t) * c.nprobe, s_start, s_prefix);
+    const int total = s_prefix[c.nprobe];
+    const int per = (total + splits - 1) / splits;
+    const int lo = split * per;
+    const int hi = min(total, lo + per);
+    uint32_t* bm = bitmaps + (size_t)q * words;
+    for (int v = lo + threadIdx.x; v < hi; v += blockDim.x) {
+        int a = 0, b = c.nprobe;
+        while (a < b) {
+            const int mid = (a + b) >> 1;
+            if (s_prefix[mid + 1] <= v) a = mid + 1; else b = mid;
+        }
+        const int64_t pos = s_start[a] + (v - s_prefix[a]);
+        const int32_t doc = c.doc_ids[pos];
+        if (doc >= 0 && (int64_t)doc < c.num_docs) atomicOr(bm + (doc >> 5), 1u << (doc & 31));
+    }
+}
+
+constexpr int kCombineWarps = 8;
+constexpr int kBinCap = 256;   // entries homed at one bin (<= 32 per doc)
+constexpr int kOutCap = 128;   // per-warp output staging
+
+__global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
+    const uint64_t* __restrict__ tables, int log2h, int bins_per_warp, uint64_t* __restrict__ keys,
+    int64_t key_cap, uint32_t* __restrict__ n_pos, uint32_t* __restrict__ flags) {
+    __shared__ uint64_t s_bin[kCombineWarps][kBinCap];
+    __shared__ float s_vals[kCombineWarps][32];
+    __shared__ uint64_t s_out[kCombineWarps][kOutCap];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.y;
+    const uint64_t* table = tables + ((size_t)q << log2h);
+    const uint32_t hmask = (1u << log2h) - 1;
+    const uint32_t nbins = 1u << (log2h - 3);
+    const uint32_t nbins_mask = nbins - 1;
+    uint64_t* out = keys + (size_t)q * key_cap;
+    int n_out = 0;
+    const uint32_t bin0 = ((uint32_t)blockIdx.x * kCombineWarps + warp) * bins_per_warp;
+    for (int bi = 0; bi < bins_per_warp; ++bi) {
+        const uint32_t bin = bin0 + bi;
+        if (bin >= nbins) break;
+        // 1) collect the entries homed at `bin`
+        int n_bin = 0;
+        const uint32_t first = bin * 8;
+        for (uint32_t base = 0; base <= hmask; base += 32) {
+            const uint32_t slot = (first + base + lane) & hmask;
+            const uint64_t e = table[slot];
+            const bool empty = (e == kEmpty);
+            bool mine = false;
+            if (!empty) mine = bin_of((uint32_t)(e >> 37), nbins_mask) == bin;
+            const uint32_t mb = __ballot_sync(0xffffffffu, mine);
+            if (mine) {
+                const int at = n_bin + __popc(mb & ((1u << lane) - 1));
+                if (at < kBinCap) s_bin[warp][at] = e;
+            }
+            n_bin += __popc(mb);
+            // chain end: an empty slot at or after slot 8*bin + 7
+            const uint32_t stop = __ballot_sync(0xffffffffu, empty && (base + lane) >= 7);
+            if (stop) break;
+        }
+        if (n_bin > kBinCap) {
+            if (lane == 0) atomicOr(flags + q, 2u);
+            n_bin = kBinCap;
+        }
+        __syncwarp();
+        // 2) group by doc, tree-sum over t
+        for (int i0 = 0; i0 < n_bin; ++i0) {
+            const uint64_t lead = s_bin[warp][i0];
+            if (lead == kEmpty) continue;               // already grouped
+            const uint32_t doc = (uint32_t)(lead >> 37);
+            s_vals[warp][lane] = 0.0f;
+            __syncwarp();
+            for (int j = i0 + lane; j < n_bin; j += 32) {
+                const uint64_t e = s_bin[warp][j];
+                if (e != kEmpty && (uint32_t)(e >> 37) == doc) {
+                    s_vals[warp][(e >> 32) & 31] = __uint_as_float((uint32_t)e);
+                    s_bin[warp][j] = kEmpty;
+                }
+            }
+            __syncwarp();
+            float x = s_vals[warp][lane];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+            if (lane == 0) {
+                s_out[warp][n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~doc);
+            }
+            ++n_out;
+            if (n_out == kOutCap) {
+                __syncwarp();
+                uint32_t at = 0;
+                if (lane == 0) at = atomicAdd(n_pos + q, (uint32_t)n_out);
+                at = __shfl_sync(0xffffffffu, at, 0);
+                for (int j = lane; j < n_out; j += 32)
+                    if (at + j < key_cap) out[at + j] = s_out[warp][j];
+                n_out = 0;
+            }
+            __syncwarp();
+        }
+    }
+    __syncwarp();
+    if (n_out > 0) {
+        uint32_t at = 0;
+        if (lane == 0) at = atomicAdd(n_pos + q, (uint32_t)n_out);
+        at = __shfl_sync(0xffffffffu, at, 0);
+        for (int j = lane; j < n_out; j += 32)
+            if (at + j < key_cap) out[at + j] = s_out[warp][j];
+    }
+}
+
+// ---- block helpers for the select kernel ---------------------------------
+// Exclusive scan over one value per thread (blockDim 1024), in thread order.
+__device__ uint32_t block_excl_scan(uint32_t v, uint32_t* s_warp, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = s_warp[lane];
+        uint32_t z = w;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, z, off);
+            if (lane >= off) z += y;
+        }
+        s_warp[lane] = z - w;  // exclusive warp offsets
+        if (lane == 31) s_warp[32] = z;
+    }
+    __syncthreads();
+    const uint32_t r = s_warp[warp] + x - v;
+    *total = s_warp[32];
+    __syncthreads();
+    return r;
+}
+
+// Bitonic sort, descending, of n (power of two) 64-bit keys in shared memory.
+__device__ void block_sort_desc(uint64_t* a, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint64_t x = a[i], y = a[l];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (x < y) : (x > y)) { a[i] = y; a[l] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Is `doc` present in the query's table (any query token)?
+__device__ bool table_has_doc(const uint64_t* table, uint32_t hmask, uint32_t nbins_mask,
+                              uint32_t doc) {
+    const uint32_t first = bin_of(doc, nbins_mask) * 8;
+    for (uint32_t i = 0; i <= hmask; ++i) {
+        const uint64_t e = table[(first + i) & hmask];
+        if (e == kEmpty) { if (i >= 7) return false; else continue; }
+        if ((uint32_t)(e >> 37) == doc) return true;
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
+    const uint64_t* __restrict__ keys, int64_t key_cap, const uint32_t* __restrict__ n_pos,
+    int k_refine, const uint32_t* __restrict__ bitmaps, int64_t words,
+    const uint64_t* __restrict__ tables, int log2h, int marks_all,
+    int32_t* __restrict__ refined_docs, float* __restrict__ refined_partial,
+    int32_t* __restrict__ num_refined, int64_t* __restrict__ num_candidates,
+    uint32_t* __restrict__ flags) {
+    extern __shared__ uint64_t s_dyn[];
+    uint64_t* s_out = s_dyn;                                   // [sort_n]
+    __shared__ uint32_t s_hist[4096];
+    __shared__ uint32_t s_warp[33];
+    __shared__ uint32_t s_cnt;
+    __shared__ uint64_t s_prefix, s_pmask;
+    __shared__ int s_need, s_done;
+    const int q = blockIdx.x;
+    const uint64_t* qk = keys + (size_t)q * key_cap;
+    const int64_t n = min((int64_t)n_pos[q], key_cap);
+    if ((int64_t)n_pos[q] > key_cap && threadIdx.x == 0) atomicOr(flags + q, 4u);
+    const int k_eff = (int)min((int64_t)k_refine, n);
+    if (threadIdx.x == 0) { s_cnt = 0; s_prefix = 0; s_pmask = 0; s_need = k_eff; s_done = 0; }
+    __syncthreads();
+    if (n <= k_refine) {
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s_out[i] = qk[i];
+        if (threadIdx.x == 0) s_cnt = (uint32_t)n;
+        __syncthreads();
+    } else {
+        // radix select of the k_eff largest keys: 12-bit digits from the top
+        const int shifts[6] = {52, 40, 28, 16, 4, 0};
+        const int widths[6] = {12, 12, 12, 12, 12, 4};
+        for (int lv = 0; lv < 6; ++lv) {
+            if (s_done) break;
+            const int sh = shifts[lv];
+            const uint32_t dmask = (1u << widths[lv]) - 1;
+            for (int i = threadIdx.x; i < 4096; i += blockDim.x) s_hist[i] = 0;
+            __syncthreads();
+            const uint64_t prefix = s_prefix, pmask = s_pmask;
+            for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+                const uint64_t key = qk[i];
+                if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> sh) & dmask], 1u);
+            }
+            __syncthreads();
+            // thread t owns digits [4095-4t-3, 4095-4t] (descending order)
+            uint32_t mine = 0;
+            const int top = 4095 - 4 * threadIdx.x;
+            for (int j = 0; j < 4; ++j) mine += s_hist[top - j];
+            uint32_t total;
+            const uint32_t before = block_excl_scan(mine, s_warp, &total);
+            const int need = s_need;
+            if ((int)before < need && need <= (int)(before + mine)) {
+                uint32_t cum = before;
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t h = s_hist[top - j];
+                    if ((int)(cum + h) >= need) {
+                        const uint32_t d = (uint32_t)(top - j);
+                        s_prefix = prefix | ((uint64_t)d << sh);
+                        s_pmask = pmask | ((uint64_t)dmask << sh);
+                        s_need = need - (int)cum;
+                        if ((int)h == need - (int)cum) s_done = 1;
+                        break;
+                    }
+                    cum += h;
+                }
+            }
+            __syncthreads();
+        }
+        const uint64_t prefix = s_prefix, pmask = s_pmask;
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint64_t key = qk[i];
+            if ((key & pmask) >= prefix) {
+                const uint32_t at = atomicAdd(&s_cnt, 1u);
+                if (at < (uint32_t)k_eff) s_out[at] = key;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && s_cnt != (uint32_t)k_eff) atomicOr(flags + q, 8u);
+        if (threadIdx.x == 0) s_cnt = (uint32_t)k_eff;
+        __syncthreads();
+    }
+    // zero-score fill in ascending doc order (only when positives < k_refine)
+    int64_t n_cand = -1;
+    const bool short_list = (int64_t)n_pos[q] < k_refine;
+    if ((short_list || marks_all) && bitmaps != nullptr) {
+        const uint32_t* bm = bitmaps + (size_t)q * words;
+        const uint64_t* table = tables + ((size_t)q << log2h);
+        const uint32_t hmask = (1u << log2h) - 1;
+        const uint32_t nbins_mask = (1u << (log2h - 3)) - 1;
+        const int64_t per = (words + blockDim.x - 1) / blockDim.x;
+        const int64_t w0 = threadIdx.x * per, w1 = min(words, w0 + per);
+        uint32_t zeros = 0, marked = 0;
+        for (int64_t w = w0; w < w1; ++w) {
+            uint32_t bits = bm[w];
+            marked += __popc(bits);
+            while (bits) {
+                const int b = __ffs(bits) - 1;
+                bits &= bits - 1;
+                if (!table_has_doc(table, hmask, nbins_mask, (uint32_t)(w * 32 + b))) ++zeros;
+            }
+        }
+        uint32_t tot_marked;
+        block_excl_scan(marked, s_warp, &tot_marked);
+        uint32_t tot_zero;
+        uint32_t at = block_excl_scan(zeros, s_warp, &tot_zero);
+        const int base = (int)s_cnt;
+        const int room = short_list ? k_refine - base : 0;
+        for (int64_t w = w0; w < w1 && (int)at < room; ++w) {
+            uint32_t bits = bm[w];
+            while (bits && (int)at < room) {
+                const int b = __ffs(bits) - 1;
+                bits &= bits - 1;
+                const uint32_t doc = (uint32_t)(w * 32 + b);
+                if (!table_has_doc(table, hmask, nbins_mask, doc)) s_out[base + at++] = (uint32_t)(~doc);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && short_list) s_cnt = (uint32_t)min(k_refine, base + (int)tot_zero);
+        n_cand = tot_marked;
+        __syncthreads();
+    }
+    const int cnt = (int)s_cnt;
+    int sort_n = 1;
+    while (sort_n < cnt) sort_n <<= 1;
+    for (int i = cnt + threadIdx.x; i < sort_n; i += blockDim.x) s_out[i] = 0;
+    __syncthreads();
+    block_sort_desc(s_out, sort_n);
+    for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+        const uint64_t key = s_out[i];
+        refined_docs[(size_t)q * k_refine + i] = (int32_t)(~(uint32_t)key);
+        refined_partial[(size_t)q * k_refine + i] = __uint_as_float((uint32_t)(key >> 32));
+    }
+    if (threadIdx.x == 0) {
+        num_refined[q] = cnt;
+        if (num_candidates) num_candidates[q] = n_cand;
+    }
+}
+
+}  // namespace chm
+
+namespace chm {
+int stage1_log2h(const chm_index* idx, int nprobe, int extra) {
+    const double mean_list = idx->n_clusters > 0 ? (double)idx->n_tokens / (double)idx->n_clusters : 0;
+    double want = 2.0 * kQ * (double)nprobe * (mean_list > 1 ? mean_list : 1);
+    if (want < 4096) want = 4096;
+    int l = 12;
+    while ((double)(1ull << l) < want && l < 30) ++l;
+    l += extra;
+    return l > 31 ? 31 : l;
+}
+int64_t stage1_key_cap(const chm_index* idx) { return idx->num_docs; }
+int64_t stage1_words(const chm_index* idx) { return (idx->num_docs + 31) / 32; }
+}  // namespace chm
+
+namespace chm {
+size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra) {
+    Sizer s;
+    const int l = stage1_log2h(idx, nprobe, extra);
+    s.take<uint64_t>((size_t)nq << l);
+    s.take<uint64_t>((size_t)nq * stage1_key_cap(idx));
+    s.take<uint32_t>((size_t)nq * stage1_words(idx));
+    s.take<uint32_t>((size_t)nq);
+    s.take<uint32_t>((size_t)nq);
+    return s.off;
+}
+}  // namespace chm
+
+extern "C" size_t chm_stage1_workspace_bytes(const chm_index* idx, int32_t nq, int32_t nprobe,
+                                             int32_t k_refine) {
+    (void)k_refine;
+    return chm::stage1_bytes(idx, nq, nprobe, 0);
+}
+
+namespace chm {
+// extra_log2h lets the host retry a query batch with a larger table.
+chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
+                      const uint32_t* labels, int32_t nprobe, int32_t k_refine,
+                      int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
+                      int64_t* num_candidates, void* ws, size_t ws_bytes, cudaStream_t st,
+                      bool force_marks, uint32_t* flags_out, int log2_extra) {
+    if (nq <= 0) return CHM_OK;
+    if (nprobe <= 0 || nprobe > CHM_MAX_NPROBE || k_refine <= 0 || k_refine > CHM_MAX_K_REFINE)
+        return CHM_ERR_INVALID;
+    if (idx->num_docs >= (1ll << 27)) return CHM_ERR_UNSUPPORTED;
+    const int l = stage1_log2h(idx, nprobe, log2_extra);
+    const int64_t key_cap = stage1_key_cap(idx);
+    const int64_t words = stage1_words(idx);
+    Arena a(ws, ws_bytes);
+    uint64_t* tables = a.take<uint64_t>((size_t)nq << l);
+    uint64_t* keys = a.take<uint64_t>((size_t)nq * key_cap);
+    uint32_t* bitmaps = a.take<uint32_t>((size_t)nq * words);
+    uint32_t* n_pos = a.take<uint32_t>((size_t)nq);
+    uint32_t* flags = a.take<uint32_t>((size_t)nq);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_CUDA(cudaMemsetAsync(tables, 0xFF, sizeof(uint64_t) * ((size_t)nq << l), st));
+    CHM_CUDA(cudaMemsetAsync(n_pos, 0, sizeof(uint32_t) * nq, st));
+    CHM_CUDA(cudaMemsetAsync(flags, 0, sizeof(uint32_t) * nq, st));
+    Stage1Ctx c{idx->cluster_pos, idx->codes1, idx->factor1, idx->doc_ids, idx->n_clusters,
+                idx->num_docs, lut, cb1, labels, nprobe, tables, l, flags};
+    const double mean_list = (double)idx->n_tokens / (double)(idx->n_clusters > 0 ? idx->n_clusters : 1);
+    const double visits_per_t = nprobe * mean_list;
+    int splits = (int)(visits_per_t / (kScoreThreads * 8));
+    if (splits < 1) splits = 1;
+    if (splits > 64) splits = 64;
+    dim3 g1(kQ * splits, nq);
+    stage1_score_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits);
+    CHM_TRY(launch_status("stage1_score_kernel"));
+    const int bins_per_warp = 16;
+    const int64_t nbins = 1ll << (l - 3);
+    const int64_t cblocks = (nbins + kCombineWarps * bins_per_warp - 1) / (kCombineWarps * bins_per_warp);
+    dim3 g2((unsigned)cblocks, nq);
+    stage1_combine_kernel<<<g2, kCombineWarps * 32, 0, st>>>(tables, l, bins_per_warp, keys, key_cap,
+                                                             n_pos, flags);
+    CHM_TRY(launch_status("stage1_combine_kernel"));
+    CHM_CUDA(cudaMemsetAsync(bitmaps, 0, sizeof(uint32_t) * (size_t)nq * words, st));
+    // queries whose positives fall short of k_refine get the visited-doc bitmap
+    stage1_mark_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits, n_pos,
+                                                     force_marks ? (1 << 30) : k_refine, bitmaps, words);
+    CHM_TRY(launch_status("stage1_mark_kernel"));
+    int sort_cap = 1;
+    while (sort_cap < k_refine) sort_cap <<= 1;
+    const size_t smem = sizeof(uint64_t) * sort_cap;
+    if (smem > 48 * 1024)
+        CHM_CUDA(cudaFuncSetAttribute(stage1_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+    stage1_select_kernel<<<nq, kSelectThreads, smem, st>>>(
+        keys, key_cap, n_pos, k_refine, bitmaps, words, tables, l, force_marks ? 1 : 0,
+        refined_docs, refined_partial, num_refined, num_candidates, flags);
+    CHM_TRY(launch_status("stage1_select_kernel"));
+    if (flags_out) CHM_CUDA(cudaMemcpyAsync(flags_out, flags, sizeof(uint32_t) * nq, cudaMemcpyDeviceToDevice, st));
+    return CHM_OK;
+}
+}  // namespace chm
+
+extern "C" chm_status chm_stage1(const chm_index* idx, int32_t nq, const float* lut,
+                                 const float* cb1, const uint32_t* labels, int32_t nprobe,
+                                 int32_t k_refine, int32_t* refined_docs, float* refined_partial,
+                                 int32_t* num_refined, int64_t* num_candidates, void* ws,
+                                 size_t ws_bytes, void* stream) {
+    return chm::stage1_run(idx, nq, lut, cb1, labels, nprobe, k_refine, refined_docs,
+                           refined_partial, num_refined, num_candidates, ws, ws_bytes,
+                           (cudaStream_t)stream, num_candidates != nullptr, nullptr, 0);
+}

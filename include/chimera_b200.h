@@ -1,0 +1,191 @@
+/*
+ * chimera_b200 -- C ABI of the B200-native Chimera search path.
+ *
+ * Every entry point takes plain device pointers and sizes, runs
+ * asynchronously on the given CUDA stream, allocates nothing (scratch is a
+ * caller-provided workspace), and returns a chm_status instead of throwing.
+ * The host C++ layer (include/chimera/chimera_index.cuh) turns statuses into
+ * the reference's exception types.
+ *
+ * Each function names the reference interface it replaces (paths inside the
+ * Chimera project, https://github.com/iidyc/Chimera).
+ */
+#ifndef CHIMERA_B200_H
+#define CHIMERA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CHM_PADDED_DIM 128  /* cpp/include/chimera/config.cuh:7 */
+#define CHM_QLEN 32         /* cpp/include/chimera/config.cuh:8 */
+#define CHM_MAX_NPROBE 1024 /* reference: 512 and unchecked (kernels.cuh:64) */
+#define CHM_MAX_K_REFINE 8192
+#define CHM_MAX_K 8192
+
+typedef enum {
+    CHM_OK = 0,
+    CHM_ERR_INVALID = 1,   /* bad argument (reference: std::invalid_argument) */
+    CHM_ERR_CAPACITY = 2,  /* workspace or table too small */
+    CHM_ERR_CUDA = 3,      /* CUDA launch/runtime failure */
+    CHM_ERR_TIMEOUT = 4,   /* a bounded wait ran out */
+    CHM_ERR_UNSUPPORTED = 5
+} chm_status;
+
+/* Device-resident index (all pointers are device memory).
+ * Layouts are the reference's on-disk layouts (build_index.cu:470-498):
+ * 1-bit data in cluster order, full codes in token order. */
+typedef struct {
+    int64_t n_tokens;
+    int64_t num_docs;
+    int64_t n_clusters;
+    int32_t ex_bits;             /* 1..7; full codes use 1 + ex_bits bits/dim */
+    int32_t dim;                 /* raw embedding dimension, 64..128 */
+    int32_t max_list_len;        /* longest inverted list */
+    int32_t reserved;
+    const int64_t* cluster_pos;  /* [n_clusters + 1] list offsets (ivf.bin) */
+    const uint8_t* codes1;       /* [n_tokens * 16] 1-bit codes, cluster order */
+    const float* factor1;        /* [n_tokens] 1-bit factors, cluster order */
+    const int32_t* doc_ids;      /* [n_tokens] owning doc, cluster order */
+    const uint32_t* tok2pos;     /* [n_tokens] token id -> cluster position */
+    const int64_t* doc_ptrs;     /* [num_docs + 1] token offsets of documents */
+    const uint8_t* full_codes;   /* [n_tokens * 16 * (1 + ex_bits)] token order */
+    const float* full_factors;   /* [n_tokens] token order */
+    const float* centroids;      /* [n_clusters * 128] rotated centroids, fp32 */
+    const float* centroid_norms; /* [n_clusters] ||c||^2 (sequential fma) */
+    const uint8_t* flips;        /* [64] FhtKac sign flips (doc_1bit.bin) */
+} chm_index;
+
+typedef struct {
+    int32_t nprobe;      /* SearchOptions::nprobe (chimera_index.cuh:27) */
+    int32_t k_refine;    /* SearchOptions::k_refine */
+    int32_t k_full_bit;  /* SearchOptions::k_full_bit */
+    int32_t num_chunks;  /* SearchOptions::num_chunks */
+    int32_t k;           /* results per query */
+    int32_t batch;       /* queries processed per pipeline pass */
+    int32_t table_log2_extra; /* grow stage-1 tables by 2^x (retry on overflow) */
+} chm_search_params;
+
+/* Library version and the last CUDA error string seen on this thread. */
+const char* chm_version(void);
+const char* chm_last_error(void);
+
+/* Workspace bytes chm_search needs for `params` on `index`. */
+size_t chm_search_workspace_bytes(const chm_index* index, const chm_search_params* params);
+
+/*
+ * Full search of `num_queries` raw queries ([num_queries, 32, index->dim]
+ * fp32, device).  Writes up to k doc ids per query (best first, -1 padded)
+ * into `results` ([num_queries, k] int64, device) and the count into
+ * `num_results` ([num_queries] int32, device).  A query whose stage-1 table
+ * overflowed gets a negative count (-flags); rerun it with a larger
+ * table_log2_extra.
+ * Replaces chimera_index::search / search_one (cpp/src/search_impl.cu:46-116),
+ * one query per call there, `params->batch` queries per pass here.
+ */
+chm_status chm_search(const chm_index* index, const chm_search_params* params,
+                      const float* queries, int64_t num_queries, int64_t* results,
+                      int32_t* num_results, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/*
+ * Stage entry points (each replaces the named reference kernels / calls).
+ */
+
+/* FhtKacRotator::rotate over every query token (rotator.hpp:281-334,
+ * called at search_impl.cu:73-75), QueryState (chimera_index_internal.cuh:
+ * 58-64) and precompute_one_bit_lut_kernel (kernels.cu:402-428).
+ * rot [ntok*128], cb1/cbex [ntok], lut [ntok*512] (lut may be NULL). */
+chm_status chm_prepare_queries(const uint8_t* flips, int32_t dim, int32_t ex_bits,
+                               const float* raw, int64_t ntok, float* rot, float* cb1,
+                               float* cbex, float* lut, void* stream);
+
+/* Exact top-nprobe centroids per rotated query token
+ * (replaces IVF_PG::search_centroids -> cuVS CAGRA, ivf_pg.cpp:37-65, 96-108).
+ * labels [nrows * nprobe], nearest first. */
+size_t chm_probe_workspace_bytes(int64_t nrows, int64_t n_clusters, int32_t nprobe);
+chm_status chm_probe(const float* rot_queries, int64_t nrows, const float* centroids,
+                     const float* centroid_norms, int64_t n_clusters, int32_t nprobe,
+                     uint32_t* labels, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 1 for `nq` queries: candidate scoring of every probed list with the
+ * 1-bit LUT, per-(doc, query token) max aggregation, per-doc partial score
+ * and the ordered top-k_refine
+ * (replaces mark/count/materialize/partial_score/sum_partial_scores kernels
+ * + CUB scan/sort, kernels.cu:117-400, search_impl.cu:118-262).
+ * refined_docs/refined_partial [nq * k_refine]; num_refined [nq];
+ * num_candidates [nq] (may be NULL). */
+size_t chm_stage1_workspace_bytes(const chm_index* index, int32_t nq, int32_t nprobe,
+                                  int32_t k_refine);
+chm_status chm_stage1(const chm_index* index, int32_t nq, const float* lut, const float* cb1,
+                      const uint32_t* labels, int32_t nprobe, int32_t k_refine,
+                      int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
+                      int64_t* num_candidates, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* Segmented 1-bit MaxSim of the refined docs (replaces
+ * gather_refined_doc_lengths/positions + one_bit_token_score +
+ * one_bit_document_score kernels, kernels.cu:430-617,
+ * search_impl.cu:278-403).  scores [nq * k_refine]. */
+chm_status chm_refine_1bit(const chm_index* index, int32_t nq, const float* lut,
+                           const float* cb1, const int32_t* refined_docs,
+                           const int32_t* num_refined, int32_t k_refine, float* scores,
+                           void* stream);
+
+/* Progressive chunked selection of the docs to full-bit score
+ * (search_impl.cu:341-494).  fb_docs [nq * fb_cap], num_fb [nq]. */
+chm_status chm_select_fullbit(int32_t nq, const int32_t* refined_docs, const float* onebit,
+                              const int32_t* num_refined, int32_t k_refine, int32_t k_full_bit,
+                              int32_t num_chunks, int32_t* fb_docs, int32_t* num_fb,
+                              int32_t fb_cap, void* stream);
+
+/* (1+ex_bits)-bit MaxSim of the selected docs (replaces the AVX-512
+ * compute_full_bit_scores, search_impl.cu:510-574).
+ * rot [nq*32*128], cbex [nq*32], scores [nq * fb_cap]. */
+chm_status chm_fullbit_score(const chm_index* index, int32_t nq, const float* rot,
+                             const float* cbex, const int32_t* fb_docs, const int32_t* num_fb,
+                             int32_t fb_cap, float* scores, void* stream);
+
+/* Final ordering of the full-bit scored docs, best first, ties to the larger
+ * doc id (std::priority_queue<pair<float,size_t>> pops, search_impl.cu:
+ * 496-500).  results [nq * k] (-1 padded), num_results [nq]. */
+chm_status chm_final_topk(int32_t nq, const int32_t* fb_docs, const float* fb_scores,
+                          const int32_t* num_fb, int32_t fb_cap, int32_t k, int64_t* results,
+                          int32_t* num_results, void* stream);
+
+/* Merge per-shard top-k lists (score, global doc id) into a global top-k with
+ * the same ordering rule (document-sharded multi-GPU search; no reference
+ * counterpart).  scores/docs [nq * shards * k] as gathered by NCCL. */
+chm_status chm_merge_topk(int32_t nq, int32_t shards, int32_t k, const float* scores,
+                          const int64_t* docs, const int32_t* counts, int64_t* results,
+                          float* result_scores, int32_t* num_results, void* stream);
+
+/*
+ * Index build (replaces build_index.cu:186-363 and quantization.cpp).
+ */
+
+/* Exact nearest centroid for n vectors stored as [n, 128] rows (raw dims
+ * first, zero padded; stand-in for the CAGRA k=1 assignment,
+ * build_index.cu:186-230).  assign [n]. */
+size_t chm_build_assign_workspace_bytes(int64_t n);
+chm_status chm_build_assign(const float* x, int64_t n, int32_t dim, const float* centroids,
+                            const float* centroid_norms, int64_t n_clusters, uint32_t* assign,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Rotate + RaBitQ-encode n raw vectors (encode_embeddings,
+ * build_index.cu:258-303; quantization.cpp:47-193).
+ * codes1 [n*16], f1 [n], full [n*16*(1+ex_bits)], ff [n]; rot may be NULL. */
+chm_status chm_build_encode(const uint8_t* flips, const float* x, int64_t n, int32_t dim,
+                            int32_t ex_bits, uint8_t* codes1, float* f1, uint8_t* full,
+                            float* ff, float* rot, void* stream);
+
+/* ||x||^2 of n rows of width 128 as a sequential fma chain. */
+chm_status chm_row_norms(const float* x, int64_t n, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHIMERA_B200_H */
