@@ -33,7 +33,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 CU_SOURCES = ["capi.cu", "query_prep.cu", "probe.cu", "stage1.cu", "refine.cu", "build.cu"]
-HOST_SOURCES = ["host/chimera_index.cpp", "host/io.cpp"]
+HOST_SOURCES = ["host/chimera_index.cpp", "host/io.cpp", "host/rng.cpp"]
 
 
 def _cxx():
@@ -57,7 +57,8 @@ def _stale(target, deps):
 
 def _headers():
     out = []
-    for d in (CSRC, os.path.join(CSRC, "host"), INCLUDE, os.path.join(INCLUDE, "chimera")):
+    for d in (CSRC, os.path.join(CSRC, "host"), os.path.join(CSRC, "apps"), INCLUDE,
+              os.path.join(INCLUDE, "chimera")):
         if os.path.isdir(d):
             out += [os.path.join(d, f) for f in os.listdir(d) if f.endswith((".h", ".cuh", ".hpp"))]
     return out

@@ -1,0 +1,116 @@
+"""The reference-facing surfaces: pybind11 module ``chimera`` (build / search
+/ save / load), the gpu_build / gpu_search CLIs and their flag handling."""
+import os
+import struct
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from chimera_b200 import build as B
+from tests import _corpus
+
+BIN = B.BIN
+
+
+def _chimera():
+    sys.path.insert(0, B.HERE)
+    import chimera  # noqa: E402
+    return chimera
+
+
+def run(args, **kw):
+    return subprocess.run(args, capture_output=True, text=True, timeout=600, **kw)
+
+
+def test_cli_help_and_bad_args():
+    for tool in ("gpu_build", "gpu_search"):
+        exe = os.path.join(BIN, tool)
+        r = run([exe])
+        assert r.returncode == 0 and "Usage:" in r.stdout
+        r = run([exe, "--help"])
+        assert r.returncode == 0 and "Usage:" in r.stdout
+        r = run([exe, "--bogus"])
+        assert r.returncode == 1 and "Argument error: Unknown argument: --bogus" in r.stderr
+    r = run([os.path.join(BIN, "gpu_search"), "--query", "q", "--gt", "g", "--index", "/nonexistent"])
+    assert r.returncode == 1 and "--index must point to a Chimera index directory" in r.stderr
+
+
+def test_module_imports_and_signature():
+    chimera = _chimera()
+    doc = chimera.ChimeraIndex.build.__doc__
+    for kw in ("nprobe", "k_refine", "k_full_bit", "cagra_itopk_size", "num_chunks"):
+        assert kw in doc
+
+
+@pytest.mark.gpu
+def test_pybind_build_search_save_load(tmp_path):
+    chimera = _chimera()
+    c = _corpus.corpus("small")
+    cfg = c["cfg"]
+    kw = dict(nprobe=cfg.nprobe, k_refine=cfg.k_refine, k_full_bit=cfg.k_full_bit, num_chunks=cfg.num_chunks)
+    idx = chimera.ChimeraIndex.build(np.ascontiguousarray(c["emb"]), [int(x) for x in c["doclens"]],
+                                     cfg.n_clusters, cfg.ex_bits, **kw)
+    one = idx.search(np.ascontiguousarray(c["queries"][0]), k=cfg.k)
+    many = idx.search(np.ascontiguousarray(c["queries"]), k=cfg.k)
+    for q in range(c["queries"].shape[0]):
+        want = list(_corpus.oracle_search(c, q)["result"])
+        assert many[q] == want, q
+    assert one == many[0]
+    idx.save(str(tmp_path / "ix"))
+    names = sorted(os.listdir(tmp_path / "ix"))
+    assert names == sorted(["doclens.bin", "doc_1bit.bin", "doc_full.bin", "cluster_1bit.bin", "ivf.bin",
+                            "centroids.f32"])
+    # on-disk payloads equal the oracle-built index arrays
+    raw = open(tmp_path / "ix" / "cluster_1bit.bin", "rb").read()
+    n = c["emb"].shape[0]
+    assert len(raw) == n * 28
+    np.testing.assert_array_equal(np.frombuffer(raw[:n * 16], np.uint8).reshape(n, 16), c["index"].codes1)
+    np.testing.assert_array_equal(np.frombuffer(raw[n * 20:n * 24], np.int32), c["index"].doc_ids)
+    idx2 = chimera.ChimeraIndex.load(str(tmp_path / "ix"), **kw)
+    assert idx2.search(np.ascontiguousarray(c["queries"]), k=cfg.k) == many
+    with pytest.raises(ValueError):
+        idx2.search(np.zeros((31, 128), np.float32), k=10)
+    with pytest.raises(ValueError):
+        idx2.search(np.ascontiguousarray(c["queries"][0]), k=0)
+    with pytest.raises(ValueError):
+        chimera.ChimeraIndex.load(str(tmp_path / "ix"), nprobe=cfg.n_clusters + 1)
+    with pytest.raises(ValueError):
+        chimera.ChimeraIndex.load(str(tmp_path / "ix"), k_refine=10, k_full_bit=20)
+    with pytest.raises(RuntimeError):
+        chimera.ChimeraIndex.load(str(tmp_path / "missing"))
+
+
+@pytest.mark.gpu
+def test_cli_build_and_search(tmp_path):
+    c = _corpus.corpus("mini")
+    cfg = c["cfg"]
+    emb, dl, qs = c["emb"], c["doclens"], c["queries"]
+    with open(tmp_path / "emb.bin", "wb") as f:
+        f.write(struct.pack("ii", emb.shape[0], emb.shape[1]))
+        f.write(np.ascontiguousarray(emb, np.float32).tobytes())
+    with open(tmp_path / "doclens.bin", "wb") as f:
+        f.write(struct.pack("i", len(dl)))
+        f.write(np.asarray(dl, np.int32).tobytes())
+    with open(tmp_path / "q.bin", "wb") as f:
+        f.write(struct.pack("iii", qs.shape[0], qs.shape[1], qs.shape[2]))
+        f.write(np.ascontiguousarray(qs, np.float32).tobytes())
+    res = [list(_corpus.oracle_search(c, q)["result"]) for q in range(qs.shape[0])]
+    with open(tmp_path / "gt.tsv", "w") as f:
+        for q, r in enumerate(res):
+            for rank, doc in enumerate(r):
+                f.write(f"{q}\t{doc}\t{rank + 1}\n")
+    r = run([os.path.join(BIN, "gpu_build"), "--index", str(tmp_path / "ix"), "--doclens", str(tmp_path / "doclens.bin"),
+             "--data", str(tmp_path / "emb.bin"), "--n-clusters", str(cfg.n_clusters), "--ex-bits", str(cfg.ex_bits)])
+    assert r.returncode == 0, r.stderr
+    r = run([os.path.join(BIN, "gpu_search"), "--query", str(tmp_path / "q.bin"), "--gt", str(tmp_path / "gt.tsv"),
+             "--index", str(tmp_path / "ix"), "--k", str(cfg.k), "--nprobe", str(cfg.nprobe), "--k-refine",
+             str(cfg.k_refine), "--k-full-bit", str(cfg.k_full_bit), "--num-chunks", str(cfg.num_chunks),
+             "--cagra-itopk-size", "64", "--warmup", "2", "--batch", "4"])
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.splitlines()
+    assert lines[0].startswith("[SEARCH] latency_ms mean=") and " p99=" in lines[0]
+    # results equal the oracle's, so recall against them is exactly 1
+    assert lines[1] == f"[SEARCH] recall@{cfg.k}=1"
+    assert any(l.startswith("[SEARCH] batched qps=") for l in lines)

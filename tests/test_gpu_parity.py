@@ -21,6 +21,9 @@ torch = pytest.importorskip("torch")
 
 
 def T(a, dtype=None):
+    """Device copy of a host array.  Bind the result to a name before taking
+    its pointer: a temporary can be recycled by torch's allocator before an
+    asynchronous kernel reads it."""
     return torch.from_numpy(np.ascontiguousarray(a if dtype is None else a.astype(dtype))).cuda()
 
 
@@ -54,7 +57,8 @@ def test_prepare_queries_bit_exact(small):
     cb1 = torch.empty(ntok, device="cuda")
     cbex = torch.empty(ntok, device="cuda")
     lut = torch.empty(ntok, 512, device="cuda")
-    capi.check(capi.lib().chm_prepare_queries(P(T(c["flips"])), c["dim"], c["cfg"].ex_bits, P(q), ntok, P(rot),
+    flips = T(c["flips"])
+    capi.check(capi.lib().chm_prepare_queries(P(flips), c["dim"], c["cfg"].ex_bits, P(q), ntok, P(rot),
                                               P(cb1), P(cbex), P(lut), S()), "prepare")
     torch.cuda.synchronize()
     np.testing.assert_array_equal(bits(rot.cpu().numpy()), bits(c["qrot"].reshape(-1, 128)))
@@ -72,7 +76,8 @@ def test_probe_labels_exact(small, dsmall):
     L = capi.lib()
     nb = L.chm_probe_workspace_bytes(rows.shape[0], dsmall.n_clusters, nprobe)
     ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
-    capi.check(L.chm_probe(P(T(rows)), rows.shape[0], P(dsmall.centroids), P(dsmall.centroid_norms),
+    rows_d = T(rows)
+    capi.check(L.chm_probe(P(rows_d), rows.shape[0], P(dsmall.centroids), P(dsmall.centroid_norms),
                            dsmall.n_clusters, nprobe, P(labels), P(ws), nb, S()), "probe")
     got = labels.cpu().numpy().view(np.uint32)
     np.testing.assert_array_equal(got, c["labels"].reshape(rows.shape[0], nprobe))
@@ -193,7 +198,8 @@ def test_build_encode_bit_exact(ex_bits, dim):
     full = torch.empty(n, fb, dtype=torch.uint8, device="cuda")
     ff = torch.empty(n, device="cuda")
     rot = torch.empty(n, 128, device="cuda")
-    capi.check(capi.lib().chm_build_encode(P(T(flips)), P(T(x)), n, dim, ex_bits, P(c1), P(f1), P(full), P(ff),
+    flips_d, x_d = T(flips), T(x)
+    capi.check(capi.lib().chm_build_encode(P(flips_d), P(x_d), n, dim, ex_bits, P(c1), P(f1), P(full), P(ff),
                                            P(rot), S()), "encode")
     torch.cuda.synchronize()
     ref_rot = O.rotate(flips, x)
@@ -233,8 +239,8 @@ def test_merge_topk():
     res = torch.empty(nq, k, dtype=torch.int64, device="cuda")
     rs = torch.empty(nq, k, device="cuda")
     nr = torch.empty(nq, dtype=torch.int32, device="cuda")
-    capi.check(capi.lib().chm_merge_topk(nq, shards, k, P(T(scores)), P(T(docs)), P(T(counts)), P(res), P(rs),
-                                         P(nr), S()), "merge")
+    sd, dd, cd = T(scores), T(docs), T(counts)
+    capi.check(capi.lib().chm_merge_topk(nq, shards, k, P(sd), P(dd), P(cd), P(res), P(rs), P(nr), S()), "merge")
     torch.cuda.synchronize()
     for q in range(nq):
         pairs = [(scores[s, q, j], docs[s, q, j]) for s in range(shards) for j in range(counts[s, q])]
