@@ -191,9 +191,20 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
     Reservoir-sampled centroids (host, std::mt19937_64) -> exact nearest
     centroid on the GPU -> stable cluster order -> GPU rotation + RaBitQ
     encoding -> cluster-ordered 1-bit arrays."""
+    import time
+
     import torch
     dev = emb.device
     st = _stream(torch, stream)
+    verbose = bool(os.environ.get("CHM_VERBOSE"))
+    t0 = [time.time()]
+
+    def phase(name):
+        if verbose:
+            torch.cuda.synchronize()
+            now = time.time()
+            print(f"[build] {name}: {now - t0[0]:.2f}s", flush=True)
+            t0[0] = now
     n, dim = int(emb.shape[0]), int(emb.shape[1])
     doclens = np.asarray(doclens, np.int64)
     if doclens.sum() != n:
@@ -216,6 +227,7 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
     check(L.chm_build_assign(_ptr(x128), n, dim, _ptr(cent_raw), _ptr(cn_raw), n_clusters, _ptr(assign),
                              _ptr(ws), wsb, st), "build_assign")
     del ws
+    phase("assign")
     # rotated centroids (padded dim) for the probe
     rot_c = torch.empty(n_clusters, DIM, dtype=torch.float32, device=dev)
     cb1_c = torch.empty(n_clusters, dtype=torch.float32, device=dev)
@@ -239,6 +251,7 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
     ff = torch.empty(n, dtype=torch.float32, device=dev)
     check(L.chm_build_encode(_ptr(flips), _ptr(emb.contiguous()), n, dim, ex_bits, _ptr(codes1), _ptr(f1),
                              _ptr(full), _ptr(ff), None, st), "build_encode")
+    phase("encode")
     dl = torch.from_numpy(doclens).to(dev)
     doc_ptrs = torch.zeros(len(doclens) + 1, dtype=torch.int64, device=dev)
     doc_ptrs[1:] = torch.cumsum(dl, 0)

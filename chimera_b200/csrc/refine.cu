@@ -167,61 +167,75 @@ __global__ void __launch_bounds__(1024) select_fullbit_kernel(
     if (threadIdx.x == 0) num_fb[q] = min((int)tot, fb_cap);
 }
 
-// (1+ex_bits)-bit MaxSim, one warp per selected doc.  Lane l = 16h + L
-// computes, for query token 2p + h, the AVX-512 lane-L accumulator of
-// gemv_batch8_avx512 (space.hpp:806-851): fma(decoded[16b + L], q[16b + L])
-// over b = 0..7; shuffles 8, 4, 2, 1 then reproduce _mm512_reduce_add_ps.
-// combined = (ip - cbex) * factor; max over tokens; final sum of the two
-// 16-lane halves reduced the same way (search_impl.cu:538-572).
+// (1+ex_bits)-bit MaxSim, one warp per selected doc, lane t = query token t
+// with its 128 rotated query values held in registers.  For every token the
+// warp decodes the packed code once into shared memory; each lane then forms
+// the 16 AVX-512 lane accumulators of gemv_batch8_avx512
+// (space.hpp:806-851), s[l] = fma(decoded[16b + l], q[16b + l], s[l]) over
+// b = 0..7, reduces them in _mm512_reduce_add_ps order (8+8, 4+4, (0+2)+(1+3)),
+// and keeps max((ip - cbex) * factor) (search_impl.cu:538-566).  The doc
+// score adds the two 16-lane halves of the maxima and reduces them the same
+// way (:569-572).
+__device__ __forceinline__ float reduce16_avx512(const float (&s)[16]) {
+    float t3[8], t6[4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t3[i] = fadd(s[8 + i], s[i]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) t6[i] = fadd(t3[4 + i], t3[i]);
+    return fadd(fadd(t6[0], t6[2]), fadd(t6[1], t6[3]));
+}
+
 __global__ void __launch_bounds__(kRefineWarps * 32) fullbit_kernel(
     const int64_t* __restrict__ doc_ptrs, const uint8_t* __restrict__ full_codes,
     const float* __restrict__ full_factors, int w, const float* __restrict__ rot,
     const float* __restrict__ cbex, const int32_t* __restrict__ fb_docs,
     const int32_t* __restrict__ num_fb, int fb_cap, float* __restrict__ scores) {
-    __shared__ float s_q[kQ * kDim];
-    __shared__ float s_cbex[kQ];
-    __shared__ float s_m[kRefineWarps][kQ];
+    __shared__ __align__(16) float s_dec[kRefineWarps][kDim];
+    __shared__ __align__(16) uint8_t s_code[kRefineWarps][kDim];
     const int q = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int F = num_fb[q];
-    if ((int)blockIdx.x * kRefineWarps >= F) return;
-    for (int i = threadIdx.x; i < kQ * kDim; i += blockDim.x) s_q[i] = rot[(size_t)q * kQ * kDim + i];
-    if (threadIdx.x < kQ) s_cbex[threadIdx.x] = cbex[q * kQ + threadIdx.x];
-    __syncthreads();
     const int i = blockIdx.x * kRefineWarps + warp;
     if (i >= F) return;
+    float qr[kDim];
+    const float4* qsrc = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + lane) * kDim);
+#pragma unroll
+    for (int j = 0; j < kDim / 4; ++j) {
+        const float4 v = qsrc[j];
+        qr[4 * j] = v.x; qr[4 * j + 1] = v.y; qr[4 * j + 2] = v.z; qr[4 * j + 3] = v.w;
+    }
+    const float cb = cbex[q * kQ + lane];
     const int64_t doc = fb_docs[(size_t)q * fb_cap + i];
-    const int half = lane >> 4, L = lane & 15;
-    const size_t stride = (size_t)kDim * w / 8;
-    float m[kQ / 2];
-#pragma unroll
-    for (int p = 0; p < kQ / 2; ++p) m[p] = -INFINITY;
+    const int bytes = kDim * w / 8;
+    float m = -INFINITY;
     for (int64_t tok = doc_ptrs[doc]; tok < doc_ptrs[doc + 1]; ++tok) {
-        const uint8_t* code = full_codes + (size_t)tok * stride;
-        float dec[8];
+        const uint8_t* code = full_codes + (size_t)tok * bytes;
+        for (int b = lane; b < bytes; b += 32) s_code[warp][b] = code[b];
+        __syncwarp();
 #pragma unroll
-        for (int b = 0; b < 8; ++b) dec[b] = (float)code_at(code, 16 * b + L, w);
-        const float f = full_factors[tok];
+        for (int k = 0; k < 4; ++k) s_dec[warp][32 * k + lane] = (float)code_at(s_code[warp], 32 * k + lane, w);
+        __syncwarp();
+        float s[16];
 #pragma unroll
-        for (int p = 0; p < kQ / 2; ++p) {
-            const int t = 2 * p + half;
-            const float* qt = s_q + t * kDim;
-            float s = 0.0f;
+        for (int l = 0; l < 16; ++l) s[l] = 0.0f;
 #pragma unroll
-            for (int b = 0; b < 8; ++b) s = __fmaf_rn(dec[b], qt[16 * b + L], s);
+        for (int b = 0; b < 8; ++b) {
+            const float4* dv = reinterpret_cast<const float4*>(&s_dec[warp][16 * b]);
 #pragma unroll
-            for (int off = 8; off >= 1; off >>= 1) s = fadd(s, __shfl_down_sync(0xffffffffu, s, off, 16));
-            const float comb = fmul(fsub(s, s_cbex[t]), f);
-            m[p] = fmaxf(m[p], comb);
+            for (int j = 0; j < 4; ++j) {
+                const float4 d4 = dv[j];
+                s[4 * j + 0] = __fmaf_rn(d4.x, qr[16 * b + 4 * j + 0], s[4 * j + 0]);
+                s[4 * j + 1] = __fmaf_rn(d4.y, qr[16 * b + 4 * j + 1], s[4 * j + 1]);
+                s[4 * j + 2] = __fmaf_rn(d4.z, qr[16 * b + 4 * j + 2], s[4 * j + 2]);
+                s[4 * j + 3] = __fmaf_rn(d4.w, qr[16 * b + 4 * j + 3], s[4 * j + 3]);
+            }
         }
+        const float ip = reduce16_avx512(s);
+        m = fmaxf(m, fmul(fsub(ip, cb), full_factors[tok]));
+        __syncwarp();
     }
-    if (L == 0) {
-#pragma unroll
-        for (int p = 0; p < kQ / 2; ++p) s_m[warp][2 * p + half] = m[p];
-    }
-    __syncwarp();
-    float x = 0.0f;
-    if (lane < 16) x = fadd(s_m[warp][lane], s_m[warp][16 + lane]);
+    // sum = max[0:16] + max[16:32] lane-wise, then the 16-lane reduction
+    float x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
 #pragma unroll
     for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
     if (lane == 0) scores[(size_t)q * fb_cap + i] = x;
@@ -297,10 +311,11 @@ static size_t pow2_bytes(int n) {
     return sizeof(uint64_t) * (size_t)s;
 }
 
+// Always raise the dynamic limit: static + dynamic shared memory together
+// may pass the 48 KB default even when the dynamic part alone does not.
 template <typename K>
 static chm_status set_smem(K kernel, size_t bytes) {
-    if (bytes > 48 * 1024)
-        CHM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    CHM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     return CHM_OK;
 }
 

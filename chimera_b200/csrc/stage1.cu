@@ -538,9 +538,8 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     int sort_cap = 1;
     while (sort_cap < k_refine) sort_cap <<= 1;
     const size_t smem = sizeof(uint64_t) * sort_cap;
-    if (smem > 48 * 1024)
-        CHM_CUDA(cudaFuncSetAttribute(stage1_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
+    // static (histogram) + dynamic (sort buffer) can exceed the 48 KB default
+    CHM_CUDA(cudaFuncSetAttribute(stage1_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     stage1_select_kernel<<<nq, kSelectThreads, smem, st>>>(
         keys, key_cap, n_pos, k_refine, bitmaps, words, tables, l, force_marks ? 1 : 0,
         refined_docs, refined_partial, num_refined, num_candidates, flags);
