@@ -32,7 +32,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE,
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
-CU_SOURCES = ["capi.cu", "query_prep.cu", "probe.cu", "stage1.cu", "refine.cu", "build.cu"]
+CU_SOURCES = ["capi.cu", "query_prep.cu", "probe.cu", "stage1.cu", "refine.cu", "build.cu", "tcgemm.cu"]
 HOST_SOURCES = ["host/chimera_index.cpp", "host/io.cpp", "host/rng.cpp"]
 
 
@@ -81,7 +81,7 @@ def build_cuda(verbose=False):
                 print(log)
     so = os.path.join(LIB, "libchimera_b200.so")
     if _stale(so, objs):
-        _run([NVCC] + ARCH + ["-shared", "-o", so] + objs + ["-lcudart"])
+        _run([NVCC] + ARCH + ["-shared", "-o", so] + objs + ["-lcudart"])  # driver API via entry points
     return so
 
 

@@ -42,7 +42,8 @@ class ChmIndex(C.Structure):
         ("cluster_pos", C.c_void_p), ("codes1", C.c_void_p), ("factor1", C.c_void_p),
         ("doc_ids", C.c_void_p), ("tok2pos", C.c_void_p), ("doc_ptrs", C.c_void_p),
         ("full_codes", C.c_void_p), ("full_factors", C.c_void_p), ("centroids", C.c_void_p),
-        ("centroid_norms", C.c_void_p), ("flips", C.c_void_p),
+        ("centroid_norms", C.c_void_p), ("flips", C.c_void_p), ("centroids_bf16", C.c_void_p),
+        ("centroid_norm_max", C.c_void_p),
     ]
 
 
@@ -74,7 +75,11 @@ EXPORTS = {
     "chm_fullbit_score": ([V, I32, V, V, V, V, I32, V, V], C.c_int),
     "chm_final_topk": ([I32, V, V, V, I32, I32, V, V, V], C.c_int),
     "chm_merge_topk": ([I32, I32, I32, V, V, V, V, V, V, V], C.c_int),
-    "chm_build_assign_workspace_bytes": ([I64], SZ),
+    "chm_build_assign_workspace_bytes": ([I64, I64], SZ),
+    "chm_probe_tc_workspace_bytes": ([I64, I64, I32], SZ),
+    "chm_probe_tc": ([V, I64, V, V, V, V, I64, I32, V, V, SZ, V], C.c_int),
+    "chm_to_bf16": ([V, I64, V, V], C.c_int),
+    "chm_max_value": ([V, I64, V, V], C.c_int),
     "chm_build_assign": ([V, I64, I32, V, V, I64, V, V, SZ, V], C.c_int),
     "chm_build_encode": ([V, V, I64, I32, I32, V, V, V, V, V, V], C.c_int),
     "chm_row_norms": ([V, I64, V, V], C.c_int),
@@ -137,22 +142,43 @@ class DeviceIndex:
     """Device-resident index arrays (torch tensors) + the chm_index view."""
 
     FIELDS = ("cluster_pos", "codes1", "factor1", "doc_ids", "tok2pos", "doc_ptrs", "full_codes",
-              "full_factors", "centroids", "centroid_norms", "flips")
+              "full_factors", "centroids", "centroid_norms", "flips", "centroids_bf16", "centroid_norm_max")
 
-    def __init__(self, *, dim, ex_bits, **arrays):
+    def __init__(self, *, dim, ex_bits, tensor_core_probe=True, **arrays):
         import torch
         self.torch = torch
         self.dim = int(dim)
         self.ex_bits = int(ex_bits)
-        for k in self.FIELDS:
+        for k in self.FIELDS[:11]:
             setattr(self, k, arrays[k])
+        dev = self.centroids.device
+        st = _stream(torch)
+        self.centroids_bf16 = torch.empty(self.centroids.shape, dtype=torch.bfloat16, device=dev)
+        check(lib().chm_to_bf16(_ptr(self.centroids), self.centroids.numel(), _ptr(self.centroids_bf16), st),
+              "to_bf16")
+        self.centroid_norm_max = torch.empty(1, dtype=torch.float32, device=dev)
+        check(lib().chm_max_value(_ptr(self.centroid_norms), self.centroid_norms.numel(),
+                                  _ptr(self.centroid_norm_max), st), "max")
         self.n_tokens = int(self.factor1.shape[0])
         self.num_docs = int(self.doc_ptrs.shape[0] - 1)
         self.n_clusters = int(self.cluster_pos.shape[0] - 1)
         lens = self.cluster_pos[1:] - self.cluster_pos[:-1]
         self.max_list_len = int(lens.max().item()) if self.n_clusters else 0
+        ptrs = [self._p(getattr(self, k)) for k in self.FIELDS]
+        if not tensor_core_probe:
+            ptrs[-2] = ptrs[-1] = 0
         self.view = ChmIndex(self.n_tokens, self.num_docs, self.n_clusters, self.ex_bits, self.dim,
-                             self.max_list_len, 0, *[self._p(getattr(self, k)) for k in self.FIELDS])
+                             self.max_list_len, 0, *ptrs)
+
+    def with_probe(self, tensor_core: bool):
+        """The same arrays with the tensor-core (True) or SIMT (False) probe."""
+        v = ChmIndex.from_buffer_copy(self.view)
+        v.centroids_bf16 = self._p(self.centroids_bf16) if tensor_core else 0
+        v.centroid_norm_max = self._p(self.centroid_norm_max) if tensor_core else 0
+        clone = object.__new__(DeviceIndex)
+        clone.__dict__.update(self.__dict__)
+        clone.view = v
+        return clone
 
     @staticmethod
     def _p(t):
@@ -160,7 +186,7 @@ class DeviceIndex:
 
     @classmethod
     def from_host(cls, *, cluster_pos, codes1, factor1, doc_ids, tok2pos, doc_ptrs, full_codes,
-                  full_factors, centroids_rot, flips, dim, ex_bits, device="cuda"):
+                  full_factors, centroids_rot, flips, dim, ex_bits, device="cuda", tensor_core_probe=True):
         """Upload host arrays in the reference layout (oracle.Index fields)."""
         import torch
         dev = torch.device(device)
@@ -168,7 +194,8 @@ class DeviceIndex:
         cents = t(centroids_rot, np.float32)
         norms = torch.empty(cents.shape[0], dtype=torch.float32, device=dev)
         check(lib().chm_row_norms(_ptr(cents), cents.shape[0], _ptr(norms), _stream(torch)), "row_norms")
-        return cls(dim=dim, ex_bits=ex_bits, cluster_pos=t(cluster_pos, np.int64),
+        return cls(dim=dim, ex_bits=ex_bits, tensor_core_probe=tensor_core_probe,
+                   cluster_pos=t(cluster_pos, np.int64),
                    codes1=t(codes1, np.uint8), factor1=t(factor1, np.float32),
                    doc_ids=t(doc_ids, np.int32), tok2pos=t(tok2pos, np.int32),
                    doc_ptrs=t(doc_ptrs, np.int64), full_codes=t(full_codes, np.uint8),
@@ -222,7 +249,7 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
     L = lib()
     check(L.chm_row_norms(_ptr(cent_raw), n_clusters, _ptr(cn_raw), st), "row_norms")
     assign = torch.empty(n, dtype=torch.int32, device=dev)
-    wsb = L.chm_build_assign_workspace_bytes(n)
+    wsb = L.chm_build_assign_workspace_bytes(n, n_clusters)
     ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
     check(L.chm_build_assign(_ptr(x128), n, dim, _ptr(cent_raw), _ptr(cn_raw), n_clusters, _ptr(assign),
                              _ptr(ws), wsb, st), "build_assign")

@@ -53,11 +53,18 @@ struct SearchBuffers {
     uint32_t* flags;
 };
 
+// The tensor-core probe is used when the index carries the bf16 centroids.
+static bool use_tc_probe(const chm_index* idx, const chm_search_params* p) {
+    return idx->centroids_bf16 != nullptr && idx->centroid_norm_max != nullptr && p->nprobe <= 448;
+}
+
 template <typename A>
 static void layout(A& a, const chm_index* idx, const chm_search_params* p, SearchBuffers* b) {
     const size_t B = (size_t)p->batch;
     const size_t ntok = B * kQ;
-    const size_t probe_bytes = chm_probe_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe);
+    const size_t probe_bytes = use_tc_probe(idx, p)
+                                   ? chm_probe_tc_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe)
+                                   : chm_probe_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe);
     const size_t s1_bytes = stage1_bytes(idx, p->batch, p->nprobe, p->table_log2_extra);
     auto rot = a.template take<float>(ntok * kDim);
     auto cb1 = a.template take<float>(ntok);
@@ -134,8 +141,13 @@ extern "C" chm_status chm_search(const chm_index* idx, const chm_search_params* 
         CHM_TRY(chm_prepare_queries(idx->flips, idx->dim, idx->ex_bits,
                                     queries + q0 * chm::kQ * idx->dim, ntok, b.rot, b.cb1, b.cbex,
                                     b.lut, st));
-        CHM_TRY(chm_probe(b.rot, ntok, idx->centroids, idx->centroid_norms, idx->n_clusters,
-                          p->nprobe, b.labels, b.probe_ws, b.probe_bytes, st));
+        if (chm::use_tc_probe(idx, p))
+            CHM_TRY(chm_probe_tc(b.rot, ntok, idx->centroids, idx->centroids_bf16, idx->centroid_norms,
+                                 idx->centroid_norm_max, idx->n_clusters, p->nprobe, b.labels, b.probe_ws,
+                                 b.probe_bytes, st));
+        else
+            CHM_TRY(chm_probe(b.rot, ntok, idx->centroids, idx->centroid_norms, idx->n_clusters,
+                              p->nprobe, b.labels, b.probe_ws, b.probe_bytes, st));
         CHM_TRY(chm::stage1_run(idx, nq, b.lut, b.cb1, b.labels, p->nprobe, p->k_refine,
                                 b.refined_docs, b.refined_partial, b.num_refined, nullptr, b.s1_ws,
                                 b.s1_bytes, st, false, b.flags, p->table_log2_extra));

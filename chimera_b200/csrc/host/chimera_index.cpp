@@ -148,7 +148,7 @@ struct chimera_index::Impl {
     bool ready = false;
 
     DevBuf d_cluster_pos, d_codes1, d_factor1, d_doc_ids, d_tok2pos, d_doc_ptrs, d_full, d_ff, d_cent,
-        d_cnorm, d_flips, d_ws, d_q, d_res, d_nres;
+        d_cnorm, d_flips, d_cent_bf16, d_cnmax, d_ws, d_q, d_res, d_nres;
     size_t ws_bytes = 0;
     int ws_batch = 0;
     int table_extra = 0;
@@ -165,7 +165,8 @@ struct chimera_index::Impl {
             stream = nullptr;
         }
         for (DevBuf* b : {&d_cluster_pos, &d_codes1, &d_factor1, &d_doc_ids, &d_tok2pos, &d_doc_ptrs, &d_full,
-                          &d_ff, &d_cent, &d_cnorm, &d_flips, &d_ws, &d_q, &d_res, &d_nres})
+                          &d_ff, &d_cent, &d_cnorm, &d_flips, &d_cent_bf16, &d_cnmax, &d_ws, &d_q, &d_res,
+                          &d_nres})
             b->reset();
         ready = false;
         ws_bytes = 0;
@@ -250,6 +251,12 @@ struct chimera_index::Impl {
         check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
         throw_status(chm_row_norms(d_cent.as<float>(), static_cast<int64_t>(n_clusters), d_cnorm.as<float>(), stream),
                      "centroid norms");
+        d_cent_bf16.alloc(n_clusters * kPadded * 2);
+        d_cnmax.alloc(sizeof(float));
+        throw_status(chm_to_bf16(d_cent.as<float>(), static_cast<int64_t>(n_clusters * kPadded), d_cent_bf16.p, stream),
+                     "centroid bf16 copy");
+        throw_status(chm_max_value(d_cnorm.as<float>(), static_cast<int64_t>(n_clusters), d_cnmax.as<float>(), stream),
+                     "centroid norm max");
         int32_t max_list = 0;
         for (size_t c = 0; c < n_clusters; ++c)
             max_list = std::max<int32_t>(max_list, static_cast<int32_t>(cluster_pos[c + 1] - cluster_pos[c]));
@@ -258,7 +265,7 @@ struct chimera_index::Impl {
                          d_cluster_pos.as<int64_t>(), d_codes1.as<uint8_t>(), d_factor1.as<float>(),
                          d_doc_ids.as<int32_t>(), d_tok2pos.as<uint32_t>(), d_doc_ptrs.as<int64_t>(),
                          d_full.as<uint8_t>(), d_ff.as<float>(), d_cent.as<float>(), d_cnorm.as<float>(),
-                         d_flips.as<uint8_t>()};
+                         d_flips.as<uint8_t>(), d_cent_bf16.p, d_cnmax.as<float>()};
         check_cuda(cudaStreamSynchronize(stream), "index upload");
         ready = true;
     }
@@ -363,7 +370,7 @@ void chimera_index::build(const std::vector<float>& embeddings, size_t dimension
     cn_raw.alloc(n_clusters * sizeof(float));
     throw_status(chm_row_norms(c128.as<float>(), static_cast<int64_t>(n_clusters), cn_raw.as<float>(), st), "norms");
     assign_d.alloc(n * sizeof(uint32_t));
-    const size_t wsb = chm_build_assign_workspace_bytes(static_cast<int64_t>(n));
+    const size_t wsb = chm_build_assign_workspace_bytes(static_cast<int64_t>(n), static_cast<int64_t>(n_clusters));
     ws.alloc(wsb);
     throw_status(chm_build_assign(x_pad, static_cast<int64_t>(n), static_cast<int32_t>(d), c128.as<float>(),
                                   cn_raw.as<float>(), static_cast<int64_t>(n_clusters), assign_d.as<uint32_t>(),

@@ -8,10 +8,12 @@
 //  probe  : GEMM -> dist matrix [rows x n_clusters] -> one CTA per row does
 //           an exact radix select of the nprobe smallest (dist, id) and a
 //           bitonic sort, nearest first, ties to the lower id.
-//  assign : GEMM with a fused arg-min (packed (key, id) 64-bit atomicMin).
+#include <cuda_bf16.h>
+
 #include <algorithm>
 
 #include "common.cuh"
+#include "select.cuh"
 
 namespace chm {
 
@@ -20,11 +22,9 @@ constexpr int kGemmThreads = 256;  // 16 x 16 threads, 4 x 8 outputs each
 
 // Loads a BK-wide k-slab of A (rows) and B (cols) into shared memory,
 // transposed so the inner loop reads contiguous rows/cols.
-template <bool kArgmin>
 __global__ void __launch_bounds__(kGemmThreads) dist_gemm_kernel(
     const float* __restrict__ A, int64_t rows, const float* __restrict__ B,
-    const float* __restrict__ bnorm, int64_t cols, int lda, int kdim, float* __restrict__ dist,
-    unsigned long long* __restrict__ best) {
+    const float* __restrict__ bnorm, int64_t cols, int lda, int kdim, float* __restrict__ dist) {
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[BK][BN + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -67,150 +67,30 @@ __global__ void __launch_bounds__(kGemmThreads) dist_gemm_kernel(
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int64_t gr = row0 + ty * 4 + i;
-        unsigned long long mn = ~0ull;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int64_t gc = col0 + tx * 8 + j;
-            if (gr < rows && gc < cols) {
-                const float d = fsub(bnorm[gc], fmul(2.0f, acc[i][j]));
-                if (kArgmin) {
-                    const unsigned long long key = ((unsigned long long)float_key_asc(d) << 32) | (uint32_t)gc;
-                    mn = key < mn ? key : mn;
-                } else {
-                    dist[gr * cols + gc] = d;
-                }
-            }
-        }
-        if (kArgmin) {
-            // the 16 threads sharing a row are 16 consecutive lanes
-#pragma unroll
-            for (int off = 8; off >= 1; off >>= 1) {
-                const unsigned long long o = __shfl_xor_sync(0xffffffffu, mn, off, 16);
-                mn = o < mn ? o : mn;
-            }
-            if (tx == 0 && gr < rows) atomicMin(best + gr, mn);
+            if (gr < rows && gc < cols) dist[gr * cols + gc] = fsub(bnorm[gc], fmul(2.0f, acc[i][j]));
         }
     }
 }
 
 constexpr int kSelThreads = 1024;
 
-__device__ uint32_t scan_excl(uint32_t v, uint32_t* s_warp, uint32_t* total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t x = v;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
-        if (lane >= off) x += y;
-    }
-    if (lane == 31) s_warp[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        const uint32_t w = s_warp[lane];
-        uint32_t z = w;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, z, off);
-            if (lane >= off) z += y;
-        }
-        s_warp[lane] = z - w;
-        if (lane == 31) s_warp[32] = z;
-    }
-    __syncthreads();
-    const uint32_t r = s_warp[warp] + x - v;
-    *total = s_warp[32];
-    __syncthreads();
-    return r;
-}
-
-// Exact k smallest (dist, id) per row; 8-bit digits over the ordered key,
-// then an id-ordered collection (ties keep the lowest ids) and a sort.
 __global__ void __launch_bounds__(kSelThreads) row_select_kernel(
     const float* __restrict__ dist, int64_t cols, int k, uint32_t* __restrict__ labels) {
-    __shared__ uint32_t s_hist[256];
-    __shared__ uint32_t s_warp[33];
-    __shared__ uint32_t s_prefix, s_need;
-    __shared__ uint64_t s_out[CHM_MAX_NPROBE];
-    __shared__ uint32_t s_nl, s_ne;
     const int64_t row = blockIdx.x;
-    const float* d = dist + row * cols;
-    if (threadIdx.x == 0) { s_prefix = 0; s_need = (uint32_t)k; s_nl = 0; s_ne = 0; }
-    uint32_t pmask = 0;
-    for (int sh = 24; sh >= 0; sh -= 8) {
-        if (threadIdx.x < 256) s_hist[threadIdx.x] = 0;
-        __syncthreads();
-        const uint32_t prefix = s_prefix;
-        for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
-            const uint32_t key = float_key_asc(d[i]);
-            if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> sh) & 255], 1u);
-        }
-        __syncthreads();
-        if (threadIdx.x < 32) {
-            // smallest digit whose cumulative count reaches need (lane owns 8 digits)
-            uint32_t c = 0;
-            for (int j = 0; j < 8; ++j) c += s_hist[threadIdx.x * 8 + j];
-            uint32_t x = c;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
-                if ((int)threadIdx.x >= off) x += y;
-            }
-            const uint32_t before = x - c;
-            const uint32_t need = s_need;
-            if (before < need && need <= before + c) {
-                uint32_t cum = before;
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t h = s_hist[threadIdx.x * 8 + j];
-                    if (cum + h >= need) {
-                        s_prefix = prefix | ((uint32_t)(threadIdx.x * 8 + j) << sh);
-                        s_need = need - cum;
-                        break;
-                    }
-                    cum += h;
-                }
-            }
-        }
-        pmask |= 255u << sh;
-        __syncthreads();
-    }
-    const uint32_t kth = s_prefix;
-    const uint32_t need_eq = s_need;   // equal keys to take, lowest ids first
-    // id-ordered pass: every key < kth, and the first need_eq keys == kth
-    for (int64_t base = 0; base < cols; base += blockDim.x) {
-        const int64_t i = base + threadIdx.x;
-        uint32_t key = 0xFFFFFFFFu;
-        if (i < cols) key = float_key_asc(d[i]);
-        const uint32_t lt = (i < cols) && key < kth;
-        const uint32_t eq = (i < cols) && key == kth;
-        uint32_t tl, te;
-        const uint32_t rl = scan_excl(lt, s_warp, &tl);
-        const uint32_t re = scan_excl(eq, s_warp, &te);
-        const uint32_t nl = s_nl, ne = s_ne;
-        if (lt) s_out[nl + rl] = ((uint64_t)key << 32) | (uint32_t)i;
-        if (eq && ne + re < need_eq) s_out[(uint32_t)k - need_eq + ne + re] = ((uint64_t)key << 32) | (uint32_t)i;
-        __syncthreads();
-        if (threadIdx.x == 0) { s_nl = nl + tl; s_ne = ne + te; }
-        __syncthreads();
-    }
-    int n = 1;
-    while (n < k) n <<= 1;
-    for (int i = k + threadIdx.x; i < n; i += blockDim.x) s_out[i] = ~0ull;
-    __syncthreads();
-    // ascending bitonic sort
-    for (int kk = 2; kk <= n; kk <<= 1) {
-        for (int j = kk >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                const int l = i ^ j;
-                if (l > i) {
-                    const uint64_t x = s_out[i], y = s_out[l];
-                    const bool asc = (i & kk) == 0;
-                    if (asc ? (x > y) : (x < y)) { s_out[i] = y; s_out[l] = x; }
-                }
-            }
-            __syncthreads();
-        }
-    }
-    for (int i = threadIdx.x; i < k; i += blockDim.x) labels[row * k + i] = (uint32_t)s_out[i];
+    block_select_smallest(dist + row * cols, cols, k, labels + row * k);
+}
+
+// k-th smallest value per row (the tensor-core probe's filter threshold).
+__global__ void __launch_bounds__(kSelThreads) row_kth_kernel(const float* __restrict__ dist, int64_t cols, int k,
+                                                              float* __restrict__ kth) {
+    __shared__ KthState s;
+    const int64_t row = blockIdx.x;
+    uint32_t key, need;
+    block_kth_key(dist + row * cols, cols, k, s, &key, &need);
+    if (threadIdx.x == 0) kth[row] = key_to_float_asc(key);
 }
 
 __global__ void row_norms_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
@@ -220,12 +100,6 @@ __global__ void row_norms_kernel(const float* __restrict__ x, int64_t n, float* 
     float acc = 0.0f;
     for (int k = 0; k < kDim; ++k) acc = __fmaf_rn(r[k], r[k], acc);
     out[i] = acc;
-}
-
-__global__ void unpack_argmin_kernel(const unsigned long long* __restrict__ best, int64_t n,
-                                     uint32_t* __restrict__ assign) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) assign[i] = (uint32_t)best[i];
 }
 
 }  // namespace chm
@@ -247,11 +121,19 @@ extern "C" chm_status chm_probe(const float* rot_queries, int64_t nrows, const f
     if (a.overflow) return CHM_ERR_CAPACITY;
     cudaStream_t st = (cudaStream_t)stream;
     dim3 g((unsigned)((n_clusters + chm::BN - 1) / chm::BN), (unsigned)((nrows + chm::BM - 1) / chm::BM));
-    chm::dist_gemm_kernel<false><<<g, chm::kGemmThreads, 0, st>>>(
-        rot_queries, nrows, centroids, centroid_norms, n_clusters, chm::kDim, chm::kDim, dist, nullptr);
+    chm::dist_gemm_kernel<<<g, chm::kGemmThreads, 0, st>>>(rot_queries, nrows, centroids, centroid_norms,
+                                                           n_clusters, chm::kDim, chm::kDim, dist);
     CHM_TRY(chm::launch_status("dist_gemm_kernel"));
     chm::row_select_kernel<<<(unsigned)nrows, chm::kSelThreads, 0, st>>>(dist, n_clusters, nprobe, labels);
     return chm::launch_status("row_select_kernel");
+}
+
+chm_status chm_row_kth(const float* dist, int64_t rows, int64_t cols, int k, float* kth, uint32_t* labels,
+                       void* stream) {
+    (void)labels;
+    if (rows <= 0) return CHM_OK;
+    chm::row_kth_kernel<<<(unsigned)rows, chm::kSelThreads, 0, (cudaStream_t)stream>>>(dist, cols, k, kth);
+    return chm::launch_status("row_kth_kernel");
 }
 
 extern "C" chm_status chm_row_norms(const float* x, int64_t n, float* out, void* stream) {
@@ -261,12 +143,20 @@ extern "C" chm_status chm_row_norms(const float* x, int64_t n, float* out, void*
 }
 
 // x and centroids are [*, 128] rows with the raw dims first and zeros after
-// (zero padding leaves every fma chain unchanged).
+// (zero padding leaves every fma chain unchanged).  Rows go through the
+// tensor-core top-16 pass with exact re-ranking, in slabs.
+size_t chm_tc_assign_workspace_bytes(int64_t rows, int64_t nc);
+chm_status chm_tc_assign(const float* x128, int64_t rows, const float* centroids, const __nv_bfloat16* cent_bf16,
+                         const float* cn, const float* cnmax, int64_t nc, uint32_t* assign, void* ws,
+                         size_t ws_bytes, cudaStream_t st);
+
 namespace chm { constexpr int64_t kAssignSlab = 1 << 20; }
 
-extern "C" size_t chm_build_assign_workspace_bytes(int64_t n) {
+extern "C" size_t chm_build_assign_workspace_bytes(int64_t n, int64_t nc) {
     chm::Sizer s;
-    s.take<unsigned long long>((size_t)std::min<int64_t>(n, chm::kAssignSlab));
+    s.take<__nv_bfloat16>((size_t)nc * chm::kDim);
+    s.take<float>(4);
+    s.take<char>(chm_tc_assign_workspace_bytes(std::min<int64_t>(n, chm::kAssignSlab), nc));
     return s.off;
 }
 
@@ -277,17 +167,17 @@ extern "C" chm_status chm_build_assign(const float* x, int64_t n, int32_t dim, c
     if (dim <= 0 || dim > CHM_PADDED_DIM || n_clusters <= 0) return CHM_ERR_INVALID;
     cudaStream_t st = (cudaStream_t)stream;
     chm::Arena a(ws, ws_bytes);
-    unsigned long long* best = a.take<unsigned long long>((size_t)std::min<int64_t>(n, chm::kAssignSlab));
+    auto* cb = a.take<__nv_bfloat16>((size_t)n_clusters * chm::kDim);
+    auto* cnmax = a.take<float>(4);
+    const size_t inner = chm_tc_assign_workspace_bytes(std::min<int64_t>(n, chm::kAssignSlab), n_clusters);
+    auto* iws = a.take<char>(inner);
     if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_TRY(chm_to_bf16(centroids, n_clusters * chm::kDim, cb, st));
+    CHM_TRY(chm_max_value(centroid_norms, n_clusters, cnmax, st));
     for (int64_t r0 = 0; r0 < n; r0 += chm::kAssignSlab) {
         const int64_t rows = std::min<int64_t>(chm::kAssignSlab, n - r0);
-        CHM_CUDA(cudaMemsetAsync(best, 0xFF, sizeof(unsigned long long) * rows, st));
-        dim3 g((unsigned)((n_clusters + chm::BN - 1) / chm::BN), (unsigned)((rows + chm::BM - 1) / chm::BM));
-        chm::dist_gemm_kernel<true><<<g, chm::kGemmThreads, 0, st>>>(
-            x + r0 * chm::kDim, rows, centroids, centroid_norms, n_clusters, chm::kDim, chm::kDim, nullptr, best);
-        CHM_TRY(chm::launch_status("dist_gemm_kernel<argmin>"));
-        chm::unpack_argmin_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(best, rows, assign + r0);
-        CHM_TRY(chm::launch_status("unpack_argmin_kernel"));
+        CHM_TRY(chm_tc_assign(x + r0 * chm::kDim, rows, centroids, cb, centroid_norms, cnmax, n_clusters,
+                              assign + r0, iws, inner, st));
     }
     return CHM_OK;
 }

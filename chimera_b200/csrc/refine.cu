@@ -185,17 +185,23 @@ __device__ __forceinline__ float reduce16_avx512(const float (&s)[16]) {
     return fadd(fadd(t6[0], t6[2]), fadd(t6[1], t6[3]));
 }
 
-__global__ void __launch_bounds__(kRefineWarps * 32) fullbit_kernel(
+constexpr int kFbWarps = 4;
+constexpr int kFbChunkTokens = 32;   // tokens staged in shared memory at a time
+
+__global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
     const int64_t* __restrict__ doc_ptrs, const uint8_t* __restrict__ full_codes,
     const float* __restrict__ full_factors, int w, const float* __restrict__ rot,
     const float* __restrict__ cbex, const int32_t* __restrict__ fb_docs,
     const int32_t* __restrict__ num_fb, int fb_cap, float* __restrict__ scores) {
-    __shared__ __align__(16) float s_dec[kRefineWarps][kDim];
-    __shared__ __align__(16) uint8_t s_code[kRefineWarps][kDim];
+    // per warp: up to 32 tokens' packed codes (<= 128 B each) and factors,
+    // plus one decoded token (128 floats)
+    __shared__ __align__(16) uint8_t s_code[kFbWarps][kFbChunkTokens * 128];
+    __shared__ float s_fac[kFbWarps][kFbChunkTokens];
+    __shared__ __align__(16) float s_dec[kFbWarps][kDim];
     const int q = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int F = num_fb[q];
-    const int i = blockIdx.x * kRefineWarps + warp;
+    const int i = blockIdx.x * kFbWarps + warp;
     if (i >= F) return;
     float qr[kDim];
     const float4* qsrc = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + lane) * kDim);
@@ -206,33 +212,41 @@ __global__ void __launch_bounds__(kRefineWarps * 32) fullbit_kernel(
     }
     const float cb = cbex[q * kQ + lane];
     const int64_t doc = fb_docs[(size_t)q * fb_cap + i];
-    const int bytes = kDim * w / 8;
+    const int bytes = kDim * w / 8;       // 16 * w, a multiple of 16
+    const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
     float m = -INFINITY;
-    for (int64_t tok = doc_ptrs[doc]; tok < doc_ptrs[doc + 1]; ++tok) {
-        const uint8_t* code = full_codes + (size_t)tok * bytes;
-        for (int b = lane; b < bytes; b += 32) s_code[warp][b] = code[b];
+    for (int64_t c0 = t0; c0 < t1; c0 += kFbChunkTokens) {
+        const int nt = (int)min((int64_t)kFbChunkTokens, t1 - c0);
+        // one coalesced burst: the chunk's codes are contiguous in token order
+        const uint4* src = reinterpret_cast<const uint4*>(full_codes + (size_t)c0 * bytes);
+        uint4* dst = reinterpret_cast<uint4*>(s_code[warp]);
+        for (int v = lane; v < nt * bytes / 16; v += 32) dst[v] = __ldg(src + v);
+        if (lane < nt) s_fac[warp][lane] = __ldg(full_factors + c0 + lane);
         __syncwarp();
+        for (int t = 0; t < nt; ++t) {
+            const uint8_t* code = s_code[warp] + t * bytes;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) s_dec[warp][32 * k + lane] = (float)code_at(s_code[warp], 32 * k + lane, w);
-        __syncwarp();
-        float s[16];
+            for (int k = 0; k < 4; ++k) s_dec[warp][32 * k + lane] = (float)code_at(code, 32 * k + lane, w);
+            __syncwarp();
+            float s[16];
 #pragma unroll
-        for (int l = 0; l < 16; ++l) s[l] = 0.0f;
+            for (int l = 0; l < 16; ++l) s[l] = 0.0f;
 #pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            const float4* dv = reinterpret_cast<const float4*>(&s_dec[warp][16 * b]);
+            for (int b = 0; b < 8; ++b) {
+                const float4* dv = reinterpret_cast<const float4*>(&s_dec[warp][16 * b]);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 d4 = dv[j];
-                s[4 * j + 0] = __fmaf_rn(d4.x, qr[16 * b + 4 * j + 0], s[4 * j + 0]);
-                s[4 * j + 1] = __fmaf_rn(d4.y, qr[16 * b + 4 * j + 1], s[4 * j + 1]);
-                s[4 * j + 2] = __fmaf_rn(d4.z, qr[16 * b + 4 * j + 2], s[4 * j + 2]);
-                s[4 * j + 3] = __fmaf_rn(d4.w, qr[16 * b + 4 * j + 3], s[4 * j + 3]);
+                for (int j = 0; j < 4; ++j) {
+                    const float4 d4 = dv[j];
+                    s[4 * j + 0] = __fmaf_rn(d4.x, qr[16 * b + 4 * j + 0], s[4 * j + 0]);
+                    s[4 * j + 1] = __fmaf_rn(d4.y, qr[16 * b + 4 * j + 1], s[4 * j + 1]);
+                    s[4 * j + 2] = __fmaf_rn(d4.z, qr[16 * b + 4 * j + 2], s[4 * j + 2]);
+                    s[4 * j + 3] = __fmaf_rn(d4.w, qr[16 * b + 4 * j + 3], s[4 * j + 3]);
+                }
             }
+            const float ip = reduce16_avx512(s);
+            m = fmaxf(m, fmul(fsub(ip, cb), s_fac[warp][t]));
+            __syncwarp();
         }
-        const float ip = reduce16_avx512(s);
-        m = fmaxf(m, fmul(fsub(ip, cb), full_factors[tok]));
-        __syncwarp();
     }
     // sum = max[0:16] + max[16:32] lane-wise, then the 16-lane reduction
     float x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
@@ -354,8 +368,8 @@ extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const 
                                         const int32_t* num_fb, int32_t fb_cap, float* scores,
                                         void* stream) {
     if (nq <= 0) return CHM_OK;
-    dim3 g((fb_cap + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
-    chm::fullbit_kernel<<<g, chm::kRefineWarps * 32, 0, (cudaStream_t)stream>>>(
+    dim3 g((fb_cap + chm::kFbWarps - 1) / chm::kFbWarps, nq);
+    chm::fullbit_kernel<<<g, chm::kFbWarps * 32, 0, (cudaStream_t)stream>>>(
         idx->doc_ptrs, idx->full_codes, idx->full_factors, 1 + idx->ex_bits, rot, cbex, fb_docs,
         num_fb, fb_cap, scores);
     return chm::launch_status("fullbit_kernel");

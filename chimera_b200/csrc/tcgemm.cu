@@ -1,0 +1,631 @@
+// Tensor-core (tcgen05 / TMEM / TMA) distance GEMM for the centroid probe
+// and the build-time assignment, with exact fp32 re-ranking.
+//
+// Contract (same as the SIMT path in probe.cu): dist(q, c) = ||c||^2 - 2<q, c>
+// with <q, c> a sequential fp32 fma chain; top-k by (dist, id).  The bf16
+// tensor-core pass only proposes candidates:
+//   1. threshold : tensor-core dists to a prefix of the centroids, exact
+//                  radix select of the K'-th smallest per row -> tau_row, so at
+//                  least K' centroids pass the filter below;
+//   2. filter    : tensor-core dists to every centroid, rows keep the
+//                  (dist, id) pairs with dist <= tau_row (per-split buffers);
+//   3. re-rank   : the K' best survivors get exact fp32 dists; the row is
+//                  accepted only when its k-th exact dist is below the
+//                  smallest approximate dist left out minus the bf16 error
+//                  bound E, which proves no excluded centroid can enter.
+//                  Rows that fail (or overflow a buffer) are recomputed
+//                  exactly over all centroids.
+// The assignment keeps the 16 best approximate centroids per row in
+// registers instead of a threshold, with the same certificate.
+//
+// GEMM kernel: one CTA = 128 query rows x a range of 128-centroid tiles.
+// Warp 0 issues TMA loads (A once, B through a 4-stage ring), warp 1 owns
+// TMEM and issues tcgen05.mma (M=128, N=128, K=16 x 8) into two TMEM
+// accumulators, warps 4-7 drain TMEM with tcgen05.ld.  No cluster multicast
+// is used anywhere.
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "common.cuh"
+#include "select.cuh"
+#include "sm100.cuh"
+
+namespace chm {
+
+constexpr int kTM = 128, kTN = 128, kK = 128;
+constexpr int kStages = 4;
+constexpr int kTcThreads = 256;
+constexpr int kBoxBytes = 128 * 64 * 2;             // one 128 x 64 bf16 TMA box
+constexpr int kTileBytes = 2 * kBoxBytes;           // 128 x 128 bf16
+constexpr int kTopA = 16;                           // assignment candidates per row
+constexpr int kFallbackRows = 16;                   // rows recomputed exactly at a time
+constexpr uint32_t kIdesc = sm100::idesc_bf16_f32(kTM, kTN);
+
+enum TcMode { kStore = 0, kFilter = 1, kTop16 = 2 };
+
+struct TcArgs {
+    int64_t rows, cols;
+    const float* cn;          // exact ||c||^2
+    int tiles_per_split;
+    int splits;
+    float* dist;              // kStore: [rows x ld]
+    int64_t ld;
+    const float* tau;         // kFilter: per-row threshold
+    uint64_t* surv;           // kFilter: [rows][splits][cap]
+    int32_t* surv_cnt;        // kFilter: [rows][splits]
+    int cap;
+    uint64_t* top;            // kTop16: [rows][splits][16]
+    uint32_t* err;
+};
+
+struct TcSmem {
+    alignas(1024) uint8_t a[kTileBytes];
+    alignas(1024) uint8_t b[kStages][kTileBytes];
+    uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, mma_done;
+    uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint64_t dist_key(float d, uint32_t col) {
+    return ((uint64_t)float_key_asc(d) << 32) | col;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                               const __grid_constant__ CUtensorMap tmB,
+                                                               TcArgs p) {
+    extern __shared__ uint8_t smem_raw[];
+    TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row0 = (int64_t)blockIdx.y * kTM;
+    const int n_tiles_total = (int)((p.cols + kTN - 1) / kTN);
+    const int t_begin = blockIdx.x * p.tiles_per_split;
+    const int t_end = min(n_tiles_total, t_begin + p.tiles_per_split);
+    const int n_tiles = max(0, t_end - t_begin);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            sm100::mbar_init(&s.full[i], 1);
+            sm100::mbar_init(&s.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            sm100::mbar_init(&s.acc_full[i], 1);
+            sm100::mbar_init(&s.acc_empty[i], 128);
+        }
+        sm100::mbar_init(&s.a_full, 1);
+        sm100::mbar_init(&s.mma_done, 1);
+        sm100::fence_mbar_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&s.tmem_base, 256);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+    bool failed = false;
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer ----
+        sm100::prefetch_tmap(&tmA);
+        sm100::prefetch_tmap(&tmB);
+        sm100::mbar_expect_tx(&s.a_full, kTileBytes);
+        sm100::tma_load_2d(s.a, &tmA, 0, (int)row0, &s.a_full);
+        sm100::tma_load_2d(s.a + kBoxBytes, &tmA, 64, (int)row0, &s.a_full);
+        for (int it = 0; it < n_tiles; ++it) {
+            const int st = it % kStages;
+            const uint32_t round = it / kStages;
+            if (!sm100::mbar_wait(&s.empty[st], (round & 1) ^ 1)) { failed = true; break; }
+            const int n0 = (t_begin + it) * kTN;
+            sm100::mbar_expect_tx(&s.full[st], kTileBytes);
+            sm100::tma_load_2d(s.b[st], &tmB, 0, n0, &s.full[st]);
+            sm100::tma_load_2d(s.b[st] + kBoxBytes, &tmB, 64, n0, &s.full[st]);
+        }
+        // drain: every issued load has landed before the CTA may exit
+        const int issued = failed ? 0 : n_tiles;
+        for (int it = max(0, issued - kStages); it < issued; ++it)
+            if (!sm100::mbar_wait(&s.full[it % kStages], (it / kStages) & 1)) failed = true;
+        if (!sm100::mbar_wait(&s.a_full, 0)) failed = true;
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        bool ok = sm100::mbar_wait(&s.a_full, 0);
+        const uint32_t a_base = sm100::smem_addr(s.a);
+        int it = 0;
+        for (; ok && it < n_tiles; ++it) {
+            const int st = it % kStages;
+            const int buf = it & 1;
+            if (!sm100::mbar_wait(&s.acc_empty[buf], ((it >> 1) & 1) ^ 1)) { ok = false; break; }
+            if (!sm100::mbar_wait(&s.full[st], (it / kStages) & 1)) { ok = false; break; }
+            sm100::tc_fence_after();
+            const uint32_t b_base = sm100::smem_addr(s.b[st]);
+            const uint32_t d_tmem = tmem + buf * kTN;
+#pragma unroll
+            for (int kk = 0; kk < kK / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                sm100::mma_bf16(d_tmem, sm100::smem_desc_sw128(a_base + off), sm100::smem_desc_sw128(b_base + off),
+                                kIdesc, kk > 0 ? 1u : 0u);
+            }
+            sm100::mma_commit(&s.empty[st]);
+            sm100::mma_commit(&s.acc_full[buf]);
+        }
+        failed = !ok;
+        // all issued MMAs complete before TMEM is released
+        sm100::mma_commit(&s.mma_done);
+        if (!sm100::mbar_wait(&s.mma_done, 0)) failed = true;
+    } else if (warp >= 4) {
+        // ---- epilogue: TMEM -> registers -> filter / store / top-16 ----
+        const int q4 = warp - 4;
+        const int64_t row = row0 + q4 * 32 + lane;
+        const bool vrow = row < p.rows;
+        float tau = -INFINITY;
+        if (MODE == kFilter && vrow) tau = p.tau[row];
+        int cnt = 0;
+        uint64_t best[kTopA];
+        if (MODE == kTop16) {
+#pragma unroll
+            for (int j = 0; j < kTopA; ++j) best[j] = ~0ull;
+        }
+        for (int it = 0; it < n_tiles; ++it) {
+            const int buf = it & 1;
+            // warp-uniform wait: the tcgen05.ld below needs every lane
+            const bool ok = __all_sync(0xffffffffu, sm100::mbar_wait(&s.acc_full[buf], (it >> 1) & 1));
+            if (!ok) { failed = true; break; }
+            sm100::tc_fence_after();
+            const int64_t n0 = (int64_t)(t_begin + it) * kTN;
+#pragma unroll 1
+            for (int c = 0; c < kTN / 32; ++c) {
+                float v[32];
+                sm100::tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + buf * kTN + c * 32, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int64_t col = n0 + c * 32 + j;
+                    if (col < p.cols && vrow) {
+                        const float d = fsub(__ldg(p.cn + col), fmul(2.0f, v[j]));
+                        if (MODE == kStore) {
+                            p.dist[row * p.ld + col] = d;
+                        } else if (MODE == kFilter) {
+                            if (d <= tau) {
+                                if (cnt < p.cap)
+                                    p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + cnt] =
+                                        dist_key(d, (uint32_t)col);
+                                ++cnt;
+                            }
+                        } else {
+                            const uint64_t key = dist_key(d, (uint32_t)col);
+                            if (key < best[kTopA - 1]) {
+                                best[kTopA - 1] = key;
+#pragma unroll
+                                for (int q = kTopA - 1; q > 0; --q) {
+                                    if (best[q] < best[q - 1]) {
+                                        const uint64_t t = best[q];
+                                        best[q] = best[q - 1];
+                                        best[q - 1] = t;
+                                    }
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&s.acc_empty[buf]);
+        }
+        if (vrow) {
+            if (MODE == kFilter) p.surv_cnt[(size_t)row * p.splits + blockIdx.x] = cnt;
+            if (MODE == kTop16) {
+#pragma unroll
+                for (int j = 0; j < kTopA; ++j) p.top[((size_t)row * p.splits + blockIdx.x) * kTopA + j] = best[j];
+            }
+        }
+    }
+    if (failed) atomicOr(p.err, 1u);
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem, 256);
+}
+
+// ---- helpers ---------------------------------------------------------------
+__global__ void to_bf16_kernel(const float* __restrict__ x, int64_t n, __nv_bfloat16* __restrict__ y) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// Bound on |approx - exact| for dist = ||c||^2 - 2<q,c> with bf16 operands
+// (relative rounding 2^-9 on each operand, fp32 accumulation) against the
+// sequential fp32 chain: 2 * (2^-8 + 2^-16 + accumulation slack) * ||q|| *
+// max||c|| plus fp32 slack on the subtraction.
+__device__ __forceinline__ float err_bound(float qnorm, float cnmax) {
+    const float cmax = sqrtf(cnmax);
+    return 2.0f * (0.00390625f + 0.0000153f + 0.00025f) * 1.05f * cmax * qnorm +
+           4e-6f * (cnmax + 2.0f * cmax * qnorm) + 1e-6f;
+}
+
+// Exact (sequential fma) dist of row q to centroid c.
+__device__ __forceinline__ float exact_dist(const float* q, const float* c, float cn) {
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int k = 0; k < kDim; ++k) acc = __fmaf_rn(q[k], c[k], acc);
+    return fsub(cn, fmul(2.0f, acc));
+}
+
+__device__ void bitonic_asc(uint64_t* a, int n) {
+    for (int k = 2; k <= n; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint64_t x = a[i], y = a[l];
+                    const bool asc = (i & k) == 0;
+                    if (asc ? (x > y) : (x < y)) { a[i] = y; a[l] = x; }
+                }
+            }
+            __syncthreads();
+        }
+}
+
+constexpr int kRerankThreads = 256;
+constexpr int kSurvMax = 4096;  // survivors a row can hold in the re-rank sort
+
+// Probe re-rank: one CTA per row (see the file comment for the certificate).
+__global__ void __launch_bounds__(kRerankThreads) probe_rerank_kernel(
+    const float* __restrict__ q_rows, const float* __restrict__ centroids, const float* __restrict__ cn,
+    const uint64_t* __restrict__ surv, const int32_t* __restrict__ surv_cnt, int splits, int cap,
+    const float* __restrict__ tau, int kc, int nprobe, const float* __restrict__ cnmax,
+    uint32_t* __restrict__ labels, int32_t* __restrict__ fallback_list, uint32_t* __restrict__ fallback_cnt) {
+    __shared__ uint64_t s_keys[kSurvMax];
+    __shared__ uint64_t s_ex[512];
+    __shared__ float s_q[kDim];
+    __shared__ int s_total, s_bad;
+    const int64_t row = blockIdx.x;
+    if (threadIdx.x == 0) { s_total = 0; s_bad = 0; }
+    if (threadIdx.x < kDim) s_q[threadIdx.x] = q_rows[row * kDim + threadIdx.x];
+    __syncthreads();
+    // gather survivors of every split
+    for (int sp = 0; sp < splits; ++sp) {
+        const int c = surv_cnt[(size_t)row * splits + sp];
+        if (c > cap) s_bad = 1;
+        const int n = min(c, cap);
+        const int base = s_total;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+            if (base + i < kSurvMax) s_keys[base + i] = surv[((size_t)row * splits + sp) * cap + i];
+        __syncthreads();
+        if (threadIdx.x == 0) s_total = base + n;
+        __syncthreads();
+    }
+    const int total = s_total;
+    if (total > kSurvMax || total < nprobe) s_bad = 1;
+    __syncthreads();
+    if (s_bad) {
+        if (threadIdx.x == 0) fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
+        return;
+    }
+    int n = 1;
+    while (n < total) n <<= 1;
+    for (int i = total + threadIdx.x; i < n; i += blockDim.x) s_keys[i] = ~0ull;
+    __syncthreads();
+    bitonic_asc(s_keys, n);
+    const int m = min(kc, total);
+    // the smallest approximate dist left out of the candidate set
+    const float a_star = (total > m) ? key_to_float_asc((uint32_t)(s_keys[m] >> 32)) : tau[row];
+    float qn = 0.0f;
+    for (int k = 0; k < kDim; ++k) qn = fmaf(s_q[k], s_q[k], qn);
+    const float e = err_bound(sqrtf(qn), *cnmax);
+    int ne = 1;
+    while (ne < m) ne <<= 1;
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) {
+        uint64_t key = ~0ull;
+        if (i < m) {
+            const uint32_t col = (uint32_t)s_keys[i];
+            const float d = exact_dist(s_q, centroids + (size_t)col * kDim, cn[col]);
+            key = dist_key(d, col);
+        }
+        s_ex[i] = key;
+    }
+    __syncthreads();
+    bitonic_asc(s_ex, ne);
+    const float kth = key_to_float_asc((uint32_t)(s_ex[nprobe - 1] >> 32));
+    const bool certified = kth < a_star - e;
+    if (!certified) {
+        if (threadIdx.x == 0) fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
+        return;
+    }
+    for (int i = threadIdx.x; i < nprobe; i += blockDim.x) labels[row * nprobe + i] = (uint32_t)s_ex[i];
+}
+
+// Assignment re-rank: one warp per row over its 16 x splits candidates.
+__global__ void assign_rerank_kernel(const float* __restrict__ x, int64_t rows, const float* __restrict__ centroids,
+                                     const float* __restrict__ cn, const uint64_t* __restrict__ top, int splits,
+                                     const float* __restrict__ cnmax, uint32_t* __restrict__ assign,
+                                     int32_t* __restrict__ fallback_list, uint32_t* __restrict__ fallback_cnt) {
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* q = x + row * kDim;
+    float qn = 0.0f;
+    for (int k = lane; k < kDim; k += 32) qn = fmaf(q[k], q[k], qn);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) qn += __shfl_xor_sync(0xffffffffu, qn, off);
+    const float e = err_bound(sqrtf(qn), *cnmax);
+    uint64_t best = ~0ull;
+    float a_star = INFINITY;
+    const int ncand = kTopA * splits;
+    for (int i = lane; i < ncand; i += 32) {
+        const uint64_t k = top[(size_t)row * ncand + i];
+        if ((i % kTopA) == kTopA - 1) a_star = fminf(a_star, key_to_float_asc((uint32_t)(k >> 32)));
+        if (k == ~0ull) continue;
+        const uint32_t col = (uint32_t)k;
+        const float d = exact_dist(q, centroids + (size_t)col * kDim, cn[col]);
+        const uint64_t key = dist_key(d, col);
+        best = key < best ? key : best;
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const uint64_t o = __shfl_xor_sync(0xffffffffu, best, off);
+        best = o < best ? o : best;
+        a_star = fminf(a_star, __shfl_xor_sync(0xffffffffu, a_star, off));
+    }
+    if (lane == 0) {
+        const float b = key_to_float_asc((uint32_t)(best >> 32));
+        if (best != ~0ull && b < a_star - e) {
+            assign[row] = (uint32_t)best;
+        } else {
+            fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
+        }
+    }
+}
+
+// Exact fallback: one CTA per listed row computes every dist with the
+// sequential fma chain into `scratch` and selects the k smallest (dist, id).
+
+__global__ void __launch_bounds__(1024) exact_rows_kernel(const float* __restrict__ x, const float* __restrict__ centroids,
+                                                          const float* __restrict__ cn, int64_t cols, int k,
+                                                          const int32_t* __restrict__ list,
+                                                          const uint32_t* __restrict__ count, float* __restrict__ scratch,
+                                                          uint32_t* __restrict__ out_labels) {
+    __shared__ float s_q[kDim];
+    const uint32_t n = *count;
+    float* d = scratch + (size_t)blockIdx.x * cols;
+    for (uint32_t r = blockIdx.x; r < n; r += gridDim.x) {
+        const int64_t row = list[r];
+        __syncthreads();
+        if (threadIdx.x < kDim) s_q[threadIdx.x] = x[row * kDim + threadIdx.x];
+        __syncthreads();
+        for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) d[c] = exact_dist(s_q, centroids + c * kDim, cn[c]);
+        __syncthreads();
+        block_select_smallest(d, cols, k, out_labels + row * k);
+    }
+}
+
+// ---- host side ---------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// [rows x 128] bf16 row-major, 128 x 64 boxes with 128-byte swizzle.
+static bool make_map(CUtensorMap* m, const void* base, int64_t rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)kK, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kK * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static size_t tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
+
+template <int MODE>
+static chm_status launch_tc(const __nv_bfloat16* a, int64_t rows, const __nv_bfloat16* b, int64_t cols,
+                            int splits, TcArgs args, cudaStream_t st) {
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, a, rows) || !make_map(&mb, b, cols)) return CHM_ERR_UNSUPPORTED;
+    const int n_tiles = (int)((cols + kTN - 1) / kTN);
+    splits = std::max(1, std::min(splits, n_tiles));
+    args.tiles_per_split = (n_tiles + splits - 1) / splits;
+    args.splits = splits;
+    const size_t smem = tc_smem_bytes();
+    CHM_CUDA(cudaFuncSetAttribute(tc_dist_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid(splits, (unsigned)((rows + kTM - 1) / kTM));
+    tc_dist_kernel<MODE><<<grid, kTcThreads, smem, st>>>(ma, mb, args);
+    return launch_status("tc_dist_kernel");
+}
+
+}  // namespace chm
+
+
+namespace chm {
+
+struct ProbePlan {
+    int64_t rows, nc;
+    int nprobe, kc, prefix, splits, cap;
+};
+
+static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
+    ProbePlan p;
+    p.rows = rows;
+    p.nc = nc;
+    p.nprobe = nprobe;
+    p.kc = std::min<int64_t>(nc, std::min(512, nprobe + 64));
+    // prefix sample large enough that ~8x kc centroids survive on average
+    p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, nc / 8));
+    p.prefix = (int)std::min<int64_t>(nc, ((p.prefix + kTN - 1) / kTN) * kTN);
+    const int64_t row_tiles = (rows + kTM - 1) / kTM;
+    const int n_tiles = (int)((nc + kTN - 1) / kTN);
+    int splits = (int)std::max<int64_t>(1, (2 * 148 + row_tiles - 1) / row_tiles);
+    splits = std::min(splits, n_tiles);
+    splits = std::min(splits, 16);
+    p.splits = splits;
+    const double expect = (double)p.kc * nc / std::max(1, p.prefix);
+    p.cap = (int)std::min<double>(kSurvMax, std::max(64.0, 4.0 * expect / splits + 64));
+    return p;
+}
+
+}  // namespace chm
+
+namespace chm {
+__global__ void max_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
+    __shared__ float s[32];
+    float m = -INFINITY;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, x[i]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        m = threadIdx.x < (blockDim.x >> 5) ? s[threadIdx.x] : -INFINITY;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        if (threadIdx.x == 0) *out = m;
+    }
+}
+}  // namespace chm
+
+extern "C" chm_status chm_to_bf16(const float* x, int64_t n, void* out, void* stream) {
+    if (n <= 0) return CHM_OK;
+    chm::to_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        x, n, static_cast<__nv_bfloat16*>(out));
+    return chm::launch_status("to_bf16_kernel");
+}
+
+extern "C" chm_status chm_max_value(const float* x, int64_t n, float* out, void* stream) {
+    if (n <= 0) return CHM_ERR_INVALID;
+    chm::max_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, out);
+    return chm::launch_status("max_kernel");
+}
+
+size_t chm_tc_probe_workspace_bytes(int64_t rows, int64_t nc, int nprobe) {
+    const chm::ProbePlan p = chm::probe_plan(rows, nc, nprobe);
+    chm::Sizer s;
+    s.take<__nv_bfloat16>((size_t)rows * chm::kK);          // bf16 rows
+    s.take<float>((size_t)rows * p.prefix);                  // threshold dists
+    s.take<float>((size_t)rows);                             // tau
+    s.take<uint64_t>((size_t)rows * p.splits * p.cap);       // survivors
+    s.take<int32_t>((size_t)rows * p.splits);                // survivor counts
+    s.take<uint32_t>((size_t)rows * p.kc);                   // threshold select labels
+    s.take<int32_t>((size_t)rows);                           // fallback list
+    s.take<uint32_t>(4);                                     // counters
+    s.take<float>((size_t)chm::kFallbackRows * nc);        // fallback scratch rows
+    return s.off;
+}
+
+// Row k-th key of the prefix dists (shared radix select in probe.cu).
+chm_status chm_row_kth(const float* dist, int64_t rows, int64_t cols, int k, float* kth, uint32_t* labels,
+                       void* stream);
+
+chm_status chm_tc_probe(const float* rot, int64_t rows, const float* centroids, const __nv_bfloat16* cent_bf16,
+                        const float* cn, const float* cnmax, int64_t nc, int nprobe, uint32_t* labels, void* ws,
+                        size_t ws_bytes, cudaStream_t st) {
+    using namespace chm;
+    const ProbePlan p = probe_plan(rows, nc, nprobe);
+    Arena a(ws, ws_bytes);
+    auto* qb = a.take<__nv_bfloat16>((size_t)rows * kK);
+    auto* pdist = a.take<float>((size_t)rows * p.prefix);
+    auto* tau = a.take<float>((size_t)rows);
+    auto* surv = a.take<uint64_t>((size_t)rows * p.splits * p.cap);
+    auto* scnt = a.take<int32_t>((size_t)rows * p.splits);
+    auto* tlab = a.take<uint32_t>((size_t)rows * p.kc);
+    auto* fl = a.take<int32_t>((size_t)rows);
+    auto* cnt = a.take<uint32_t>(4);
+    auto* scratch = a.take<float>((size_t)kFallbackRows * nc);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_CUDA(cudaMemsetAsync(cnt, 0, 16, st));
+    const int64_t nel = rows * kK;
+    to_bf16_kernel<<<(unsigned)((nel + 255) / 256), 256, 0, st>>>(rot, nel, qb);
+    CHM_TRY(launch_status("to_bf16_kernel"));
+    // 1) threshold from a prefix of the centroids
+    TcArgs t1{};
+    t1.rows = rows;
+    t1.cols = p.prefix;
+    t1.cn = cn;
+    t1.dist = pdist;
+    t1.ld = p.prefix;
+    t1.err = cnt + 1;
+    CHM_TRY(launch_tc<kStore>(qb, rows, cent_bf16, p.prefix, p.splits, t1, st));
+    CHM_TRY(chm_row_kth(pdist, rows, p.prefix, p.kc, tau, tlab, st));
+    // 2) filter over all centroids
+    TcArgs t2{};
+    t2.rows = rows;
+    t2.cols = nc;
+    t2.cn = cn;
+    t2.tau = tau;
+    t2.surv = surv;
+    t2.surv_cnt = scnt;
+    t2.cap = p.cap;
+    t2.err = cnt + 1;
+    CHM_TRY(launch_tc<kFilter>(qb, rows, cent_bf16, nc, p.splits, t2, st));
+    // 3) exact re-rank with the certificate, exact fallback for the rest
+    probe_rerank_kernel<<<(unsigned)rows, kRerankThreads, 0, st>>>(rot, centroids, cn, surv, scnt, p.splits, p.cap,
+                                                                   tau, p.kc, nprobe, cnmax, labels, fl, cnt);
+    CHM_TRY(launch_status("probe_rerank_kernel"));
+    exact_rows_kernel<<<kFallbackRows, 1024, 0, st>>>(rot, centroids, cn, nc, nprobe, fl, cnt, scratch, labels);
+    return launch_status("exact_rows_kernel");
+}
+
+size_t chm_tc_assign_workspace_bytes(int64_t rows, int64_t nc) {
+    chm::Sizer s;
+    s.take<__nv_bfloat16>((size_t)rows * chm::kK);
+    s.take<uint64_t>((size_t)rows * chm::kTopA);
+    s.take<int32_t>((size_t)rows);
+    s.take<uint32_t>(4);
+    s.take<float>((size_t)chm::kFallbackRows * nc);
+    return s.off;
+}
+
+chm_status chm_tc_assign(const float* x128, int64_t rows, const float* centroids, const __nv_bfloat16* cent_bf16,
+                         const float* cn, const float* cnmax, int64_t nc, uint32_t* assign, void* ws,
+                         size_t ws_bytes, cudaStream_t st) {
+    using namespace chm;
+    Arena a(ws, ws_bytes);
+    auto* xb = a.take<__nv_bfloat16>((size_t)rows * kK);
+    auto* top = a.take<uint64_t>((size_t)rows * kTopA);
+    auto* fl = a.take<int32_t>((size_t)rows);
+    auto* cnt = a.take<uint32_t>(4);
+    auto* scratch = a.take<float>((size_t)kFallbackRows * nc);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_CUDA(cudaMemsetAsync(cnt, 0, 16, st));
+    const int64_t nel = rows * kK;
+    to_bf16_kernel<<<(unsigned)((nel + 255) / 256), 256, 0, st>>>(x128, nel, xb);
+    CHM_TRY(launch_status("to_bf16_kernel"));
+    TcArgs t{};
+    t.rows = rows;
+    t.cols = nc;
+    t.cn = cn;
+    t.top = top;
+    t.err = cnt + 1;
+    CHM_TRY(launch_tc<kTop16>(xb, rows, cent_bf16, nc, 1, t, st));
+    assign_rerank_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x128, rows, centroids, cn, top, 1,
+                                                                             cnmax, assign, fl, cnt);
+    CHM_TRY(launch_status("assign_rerank_kernel"));
+    exact_rows_kernel<<<kFallbackRows, 1024, 0, st>>>(x128, centroids, cn, nc, 1, fl, cnt, scratch, assign);
+    return launch_status("exact_rows_kernel");
+}
+
+extern "C" size_t chm_probe_tc_workspace_bytes(int64_t nrows, int64_t n_clusters, int32_t nprobe) {
+    return chm_tc_probe_workspace_bytes(nrows, n_clusters, nprobe);
+}
+
+extern "C" chm_status chm_probe_tc(const float* rot, int64_t nrows, const float* centroids, const void* cent_bf16,
+                                   const float* cn, const float* cnmax, int64_t nc, int32_t nprobe, uint32_t* labels,
+                                   void* ws, size_t ws_bytes, void* stream) {
+    if (nrows <= 0) return CHM_OK;
+    if (nprobe <= 0 || nprobe > 448 || nprobe > nc || !cent_bf16 || !cnmax) return CHM_ERR_INVALID;
+    return chm_tc_probe(rot, nrows, centroids, static_cast<const __nv_bfloat16*>(cent_bf16), cn, cnmax, nc, nprobe,
+                        labels, ws, ws_bytes, (cudaStream_t)stream);
+}

@@ -57,6 +57,9 @@ typedef struct {
     const float* centroids;      /* [n_clusters * 128] rotated centroids, fp32 */
     const float* centroid_norms; /* [n_clusters] ||c||^2 (sequential fma) */
     const uint8_t* flips;        /* [64] FhtKac sign flips (doc_1bit.bin) */
+    const void* centroids_bf16;  /* [n_clusters * 128] bf16 copy for the tensor-core
+                                    probe; NULL selects the exact SIMT probe */
+    const float* centroid_norm_max; /* device scalar max ||c||^2 (with centroids_bf16) */
 } chm_index;
 
 typedef struct {
@@ -110,6 +113,19 @@ size_t chm_probe_workspace_bytes(int64_t nrows, int64_t n_clusters, int32_t npro
 chm_status chm_probe(const float* rot_queries, int64_t nrows, const float* centroids,
                      const float* centroid_norms, int64_t n_clusters, int32_t nprobe,
                      uint32_t* labels, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Tensor-core probe with the same exact result: a bf16 tcgen05 pass proposes
+ * candidates and exact fp32 re-ranking with an error-bound certificate (or an
+ * exact recomputation of the row) decides.  nprobe <= 448. */
+size_t chm_probe_tc_workspace_bytes(int64_t nrows, int64_t n_clusters, int32_t nprobe);
+chm_status chm_probe_tc(const float* rot_queries, int64_t nrows, const float* centroids,
+                        const void* centroids_bf16, const float* centroid_norms,
+                        const float* centroid_norm_max, int64_t n_clusters, int32_t nprobe,
+                        uint32_t* labels, void* workspace, size_t workspace_bytes, void* stream);
+
+/* fp32 -> bf16 (round to nearest even) and the max of n values (device). */
+chm_status chm_to_bf16(const float* x, int64_t n, void* out, void* stream);
+chm_status chm_max_value(const float* x, int64_t n, float* out, void* stream);
 
 /* Stage 1 for `nq` queries: candidate scoring of every probed list with the
  * 1-bit LUT, per-(doc, query token) max aggregation, per-doc partial score
@@ -167,10 +183,13 @@ chm_status chm_merge_topk(int32_t nq, int32_t shards, int32_t k, const float* sc
  * Index build (replaces build_index.cu:186-363 and quantization.cpp).
  */
 
-/* Exact nearest centroid for n vectors stored as [n, 128] rows (raw dims
- * first, zero padded; stand-in for the CAGRA k=1 assignment,
- * build_index.cu:186-230).  assign [n]. */
-size_t chm_build_assign_workspace_bytes(int64_t n);
+/* Exact nearest centroid (min ||c||^2 - 2<x,c>, sequential fp32 fma dots,
+ * ties to the lower id) for n vectors stored as [n, 128] rows (raw dims
+ * first, zero padded); a bf16 tcgen05 pass proposes 16 candidates per row,
+ * exact re-ranking with an error-bound certificate decides, uncertified rows
+ * are recomputed exactly.  Stand-in for the CAGRA k=1 assignment
+ * (build_index.cu:186-230).  assign [n]. */
+size_t chm_build_assign_workspace_bytes(int64_t n, int64_t n_clusters);
 chm_status chm_build_assign(const float* x, int64_t n, int32_t dim, const float* centroids,
                             const float* centroid_norms, int64_t n_clusters, uint32_t* assign,
                             void* workspace, size_t workspace_bytes, void* stream);

@@ -256,3 +256,97 @@ def test_invalid_arguments_rejected(small, dsmall):
     assert L.chm_search_workspace_bytes(C.byref(dsmall.view), C.byref(bad)) == 0
     st = L.chm_probe(None, 1, None, None, 10, 2000, None, None, 0, S())
     assert st == capi.CHM_ERR_INVALID
+
+
+# ---- tensor-core probe: same labels as the exact contract -------------------
+def _probe_pair(rows, cents, nprobe):
+    """(tensor-core labels, SIMT labels) for rows/centroids as host arrays."""
+    L = capi.lib()
+    r = T(rows)
+    c = T(cents)
+    nc = cents.shape[0]
+    cn = torch.empty(nc, device="cuda")
+    capi.check(L.chm_row_norms(P(c), nc, P(cn), S()), "norms")
+    cb = torch.empty(nc, 128, dtype=torch.bfloat16, device="cuda")
+    capi.check(L.chm_to_bf16(P(c), nc * 128, P(cb), S()), "bf16")
+    cmax = torch.empty(1, device="cuda")
+    capi.check(L.chm_max_value(P(cn), nc, P(cmax), S()), "max")
+    out = []
+    for tc in (True, False):
+        lab = torch.full((rows.shape[0], nprobe), -1, dtype=torch.int32, device="cuda")
+        if tc:
+            nb = L.chm_probe_tc_workspace_bytes(rows.shape[0], nc, nprobe)
+            ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+            capi.check(L.chm_probe_tc(P(r), rows.shape[0], P(c), P(cb), P(cn), P(cmax), nc, nprobe, P(lab), P(ws), nb,
+                                      S()), "probe_tc")
+        else:
+            nb = L.chm_probe_workspace_bytes(rows.shape[0], nc, nprobe)
+            ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+            capi.check(L.chm_probe(P(r), rows.shape[0], P(c), P(cn), nc, nprobe, P(lab), P(ws), nb, S()), "probe")
+        torch.cuda.synchronize()
+        out.append(lab.cpu().numpy().view(np.uint32))
+    return out
+
+
+def test_probe_tensor_core_matches_oracle(small):
+    c = small
+    rows = c["qrot"].reshape(-1, 128)
+    tc, simt = _probe_pair(rows, c["centroids_rot"], c["cfg"].nprobe)
+    np.testing.assert_array_equal(tc, c["labels"].reshape(rows.shape[0], -1))
+    np.testing.assert_array_equal(simt, tc)
+
+
+@pytest.mark.parametrize("nc,nprobe", [(65536, 128), (20000, 64), (4096, 300)])
+def test_probe_tensor_core_random(nc, nprobe):
+    rng = np.random.default_rng(nc + nprobe)
+    rows = rng.standard_normal((1000, 128)).astype(np.float32)
+    rows /= np.linalg.norm(rows, axis=1, keepdims=True)
+    cents = rng.standard_normal((nc, 128)).astype(np.float32)
+    cents /= np.linalg.norm(cents, axis=1, keepdims=True)
+    tc, simt = _probe_pair(rows, cents, nprobe)
+    np.testing.assert_array_equal(tc, simt)
+
+
+def test_probe_tensor_core_fallback_on_ties():
+    """Duplicated centroids make exact ties at the boundary, so the
+    certificate cannot hold and rows take the exact fallback."""
+    rng = np.random.default_rng(7)
+    base = rng.standard_normal((300, 128)).astype(np.float32)
+    base /= np.linalg.norm(base, axis=1, keepdims=True)
+    cents = np.concatenate([base] * 8)            # every centroid 8 times
+    rows = base[:200] + 0.01 * rng.standard_normal((200, 128)).astype(np.float32)
+    tc, simt = _probe_pair(rows.astype(np.float32), cents, 20)
+    np.testing.assert_array_equal(tc, simt)
+    # ties resolve to the lower id: the first copy of the nearest centroid leads
+    assert (tc[:, 0] < 300).all()
+
+
+def test_build_assign_tensor_core_with_duplicate_centroids():
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((5000, 128)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    cents = np.concatenate([x[:100]] * 3)          # ties everywhere
+    want = O.assign(x, cents)
+    L = capi.lib()
+    xd, cd = T(x), T(cents)
+    cn = torch.empty(cents.shape[0], device="cuda")
+    capi.check(L.chm_row_norms(P(cd), cents.shape[0], P(cn), S()), "norms")
+    nb = L.chm_build_assign_workspace_bytes(x.shape[0], cents.shape[0])
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    out = torch.empty(x.shape[0], dtype=torch.int32, device="cuda")
+    capi.check(L.chm_build_assign(P(xd), x.shape[0], 128, P(cd), P(cn), cents.shape[0], P(out), P(ws), nb, S()),
+               "assign")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), want)
+
+
+def test_search_end_to_end_simt_probe(small, dsmall):
+    c = small
+    cfg = c["cfg"]
+    s = capi.Searcher(dsmall.with_probe(False), k=cfg.k, batch=7, **cfg.search_kwargs())
+    q = T(c["queries"], np.float32)
+    res, nres = s.search(q)
+    res, nres = res.cpu().numpy(), nres.cpu().numpy()
+    for i in range(c["queries"].shape[0]):
+        o = _corpus.oracle_search(c, i)
+        np.testing.assert_array_equal(res[i, :nres[i]], o["result"], err_msg=f"query {i}")
