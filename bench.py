@@ -228,10 +228,12 @@ def main():
 
     # ---- recall ------------------------------------------------------------
     nrec = min(args.recall_queries, nq_total)
-    qsel = list(range(nrec))
-    r_all, n_all = searcher.search(queries[:nrec].contiguous())
-    gt = ground_truth(torch, emb, index.doc_ptrs, queries, cfg.k, qsel)
-    recall = W.recall_at_k(np.stack(gt), r_all.cpu().numpy(), cfg.k)
+    recall = None
+    if nrec > 0:
+        qsel = list(range(nrec))
+        r_all, n_all = searcher.search(queries[:nrec].contiguous())
+        gt = ground_truth(torch, emb, index.doc_ptrs, queries, cfg.k, qsel)
+        recall = round(W.recall_at_k(np.stack(gt), r_all.cpu().numpy(), cfg.k), 4)
 
     hbm, bf16, kind = peaks()
     dom = max(stages, key=lambda s: s["ms"])
@@ -247,7 +249,7 @@ def main():
                                f"{cfg.n_clusters} clusters, ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, "
                                f"k_refine {cfg.k_refine}, k_full_bit {cfg.k_full_bit}, k {cfg.k}",
                    "batch_queries": B, "l2": "inputs larger than L2 (index >> 126 MB)",
-                   "recall@100": round(recall, 4), "recall_queries": nrec,
+                   "recall@100": recall, "recall_queries": nrec,
                    "latency_ms_single_query": lat, "parallelism": f"replica x{world}"},
         "e2e": {"value": round(e2e_qps, 2), "unit": "queries/s",
                 "h2d_bytes_per_step": int(B * 32 * cfg.dim * 4), "d2h_bytes_per_step": int(B * cfg.k * 8)},
@@ -284,8 +286,16 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
     cbex = torch.empty(ntok, device=dev)
     lut = torch.empty(ntok, 512, device=dev)
     labels = torch.empty(ntok, p.nprobe, dtype=torch.int32, device=dev)
-    pb = L.chm_probe_workspace_bytes(ntok, index.n_clusters, p.nprobe)
+    use_tc = bool(index.view.centroids_bf16) and p.nprobe <= 448
+    pb = (L.chm_probe_tc_workspace_bytes if use_tc else L.chm_probe_workspace_bytes)(ntok, index.n_clusters, p.nprobe)
     pws = torch.empty(pb, dtype=torch.uint8, device=dev)
+
+    def probe():
+        if use_tc:
+            return L.chm_probe_tc(P(rot), ntok, P(index.centroids), P(index.centroids_bf16), P(index.centroid_norms),
+                                  P(index.centroid_norm_max), index.n_clusters, p.nprobe, P(labels), P(pws), pb, st)
+        return L.chm_probe(P(rot), ntok, P(index.centroids), P(index.centroid_norms), index.n_clusters, p.nprobe,
+                           P(labels), P(pws), pb, st)
     sb = L.chm_stage1_workspace_bytes(C.byref(index.view), B, p.nprobe, p.k_refine)
     sws = torch.empty(sb, dtype=torch.uint8, device=dev)
     rd = torch.empty(B, p.k_refine, dtype=torch.int32, device=dev)
@@ -301,8 +311,7 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
     stages = [
         ("prepare", 1, lambda: L.chm_prepare_queries(P(index.flips), index.dim, index.ex_bits, P(q), ntok, P(rot),
                                                     P(cb1), P(cbex), P(lut), st)),
-        ("probe", 2, lambda: L.chm_probe(P(rot), ntok, P(index.centroids), P(index.centroid_norms), index.n_clusters,
-                                         p.nprobe, P(labels), P(pws), pb, st)),
+        ("probe", 7 if use_tc else 2, probe),
         ("stage1", 4, lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe, p.k_refine, P(rd), P(rp),
                                            P(nr), None, P(sws), sb, st)),
         ("refine_1bit", 1, lambda: L.chm_refine_1bit(v, B, P(lut), P(cb1), P(rd), P(nr), p.k_refine, P(ob), st)),

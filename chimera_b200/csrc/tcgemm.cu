@@ -67,6 +67,7 @@ struct TcSmem {
     alignas(1024) uint8_t b[kStages][kTileBytes];
     uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, mma_done;
     uint32_t tmem_base;
+    float cn[2][kTN];   // per-tile ||c||^2, double-buffered for the epilogue warps
 };
 
 __device__ __forceinline__ uint64_t dist_key(float d, uint32_t col) {
@@ -169,50 +170,94 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
 #pragma unroll
             for (int j = 0; j < kTopA; ++j) best[j] = ~0ull;
         }
+        const int et = threadIdx.x - 128;                       // 0..127 within the epilogue
+        float thr = INFINITY;                                   // kTop16: float of best[15]
         for (int it = 0; it < n_tiles; ++it) {
             const int buf = it & 1;
+            const int64_t n0 = (int64_t)(t_begin + it) * kTN;
+            // stage this tile's norms (other warps may still read the other buffer)
+            s.cn[buf][et] = (n0 + et < p.cols) ? __ldg(p.cn + n0 + et) : INFINITY;
+            // every epilogue warp passes this barrier once per tile, also after a
+            // failed wait, so the barrier count stays equal across warps
+            sm100::named_bar(1, 128);
+            if (failed) continue;
             // warp-uniform wait: the tcgen05.ld below needs every lane
             const bool ok = __all_sync(0xffffffffu, sm100::mbar_wait(&s.acc_full[buf], (it >> 1) & 1));
-            if (!ok) { failed = true; break; }
+            if (!ok) { failed = true; continue; }
             sm100::tc_fence_after();
-            const int64_t n0 = (int64_t)(t_begin + it) * kTN;
-#pragma unroll 1
-            for (int c = 0; c < kTN / 32; ++c) {
-                float v[32];
-                sm100::tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + buf * kTN + c * 32, v);
+            uint32_t r[4][32];
+            const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + buf * kTN;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int64_t col = n0 + c * 32 + j;
-                    if (col < p.cols && vrow) {
-                        const float d = fsub(__ldg(p.cn + col), fmul(2.0f, v[j]));
-                        if (MODE == kStore) {
-                            p.dist[row * p.ld + col] = d;
-                        } else if (MODE == kFilter) {
-                            if (d <= tau) {
+            for (int c = 0; c < 4; ++c) sm100::tmem_ld32_async(tbase + c * 32, r[c]);
+            sm100::tmem_wait_ld();
+            // the accumulator is in registers: hand TMEM back to the MMA warp
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&s.acc_empty[buf]);
+            if (!vrow) continue;
+            const float* cnb = s.cn[buf];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (MODE == kStore) {
+                    float* out = p.dist + row * p.ld + n0 + c * 32;
+                    if (n0 + c * 32 + 32 <= p.cols && (p.ld & 3) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 o;
+                            o.x = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 0]), cnb[c * 32 + j + 0]);
+                            o.y = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 1]), cnb[c * 32 + j + 1]);
+                            o.z = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 2]), cnb[c * 32 + j + 2]);
+                            o.w = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 3]), cnb[c * 32 + j + 3]);
+                            *reinterpret_cast<float4*>(out + j) = o;
+                        }
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + c * 32 + j < p.cols)
+                                out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[c][j]), cnb[c * 32 + j]);
+                    }
+                } else {
+                    // Branch-free pass over the 32 values: bit j set when column
+                    // j can enter (d <= tau for the filter, d <= the current
+                    // 16th best for the top-16).  d = cn - 2 v is exact in one
+                    // fma because 2 v is exact.  Out-of-range columns carry +inf
+                    // norms and never pass.
+                    const float lim = (MODE == kFilter) ? tau : thr;
+                    uint32_t mask = 0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float d = __fmaf_rn(-2.0f, __uint_as_float(r[c][j]), cnb[c * 32 + j]);
+                        mask |= (d <= lim ? 1u : 0u) << j;
+                    }
+                    if (mask) {
+                        // rare: static register indices keep r[][] out of local memory
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (!(mask & (1u << j))) continue;
+                            const float d = __fmaf_rn(-2.0f, __uint_as_float(r[c][j]), cnb[c * 32 + j]);
+                            const uint32_t col = (uint32_t)(n0 + c * 32 + j);
+                            if (MODE == kFilter) {
                                 if (cnt < p.cap)
-                                    p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + cnt] =
-                                        dist_key(d, (uint32_t)col);
+                                    p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + cnt] = dist_key(d, col);
                                 ++cnt;
-                            }
-                        } else {
-                            const uint64_t key = dist_key(d, (uint32_t)col);
-                            if (key < best[kTopA - 1]) {
-                                best[kTopA - 1] = key;
+                            } else {
+                                const uint64_t key = dist_key(d, col);
+                                if (key < best[kTopA - 1]) {
+                                    best[kTopA - 1] = key;
 #pragma unroll
-                                for (int q = kTopA - 1; q > 0; --q) {
-                                    if (best[q] < best[q - 1]) {
-                                        const uint64_t t = best[q];
-                                        best[q] = best[q - 1];
-                                        best[q - 1] = t;
+                                    for (int q = kTopA - 1; q > 0; --q) {
+                                        if (best[q] < best[q - 1]) {
+                                            const uint64_t t = best[q];
+                                            best[q] = best[q - 1];
+                                            best[q - 1] = t;
+                                        }
                                     }
+                                    if (best[kTopA - 1] != ~0ull)
+                                        thr = key_to_float_asc((uint32_t)(best[kTopA - 1] >> 32));
                                 }
                             }
                         }
                     }
                 }
             }
-            sm100::tc_fence_before();
-            sm100::mbar_arrive(&s.acc_empty[buf]);
         }
         if (vrow) {
             if (MODE == kFilter) p.surv_cnt[(size_t)row * p.splits + blockIdx.x] = cnt;
