@@ -68,6 +68,7 @@ struct TcSmem {
     uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, mma_done;
     uint32_t tmem_base;
     float cn[2][kTN];   // per-tile ||c||^2, double-buffered for the epilogue warps
+    float pass[4][32][33];  // per-lane copy of 32 values whose mask has set bits
 };
 
 __device__ __forceinline__ uint64_t dist_key(float d, uint32_t col) {
@@ -228,11 +229,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
                         mask |= (d <= lim ? 1u : 0u) << j;
                     }
                     if (mask) {
-                        // rare: static register indices keep r[][] out of local memory
+                        // rare: copy the 32 values to this lane's shared row and
+                        // walk the set bits with a runtime index (keeps the hot
+                        // loop small and r[][] in registers)
+                        float* row_vals = s.pass[q4][lane];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (!(mask & (1u << j))) continue;
-                            const float d = __fmaf_rn(-2.0f, __uint_as_float(r[c][j]), cnb[c * 32 + j]);
+                        for (int j = 0; j < 32; ++j) row_vals[j] = __uint_as_float(r[c][j]);
+                        while (mask) {
+                            const int j = __ffs(mask) - 1;
+                            mask &= mask - 1;
+                            const float d = __fmaf_rn(-2.0f, row_vals[j], cnb[c * 32 + j]);
                             const uint32_t col = (uint32_t)(n0 + c * 32 + j);
                             if (MODE == kFilter) {
                                 if (cnt < p.cap)
