@@ -170,93 +170,66 @@ __global__ void __launch_bounds__(kScoreThreads) stage1_mark_kernel(
     }
 }
 
-constexpr int kCombineWarps = 8;
-constexpr int kBinCap = 256;   // entries homed at one bin (<= 32 per doc)
-constexpr int kOutCap = 128;   // per-warp output staging
+constexpr int kCombineThreads = 256;
 
-__global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
-    const uint64_t* __restrict__ tables, int log2h, int bins_per_warp, uint64_t* __restrict__ keys,
-    int64_t key_cap, uint32_t* __restrict__ n_pos, uint32_t* __restrict__ flags) {
-    __shared__ uint64_t s_bin[kCombineWarps][kBinCap];
-    __shared__ float s_vals[kCombineWarps][32];
-    __shared__ uint64_t s_out[kCombineWarps][kOutCap];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// One thread per table slot.  The slot holding the first entry of a doc
+// (counting from the doc's home slot) makes that thread the doc's leader: it
+// gathers the doc's entries from the rest of the probe chain, sums the 32
+// per-query-token maxima with the reference's tree (zeros for absent tokens,
+// kernels.cu:192-198) and emits the 64-bit key (score bits << 32 | ~doc).
+__global__ void __launch_bounds__(kCombineThreads) stage1_combine_kernel(
+    const uint64_t* __restrict__ tables, int log2h, uint64_t* __restrict__ keys, int64_t key_cap,
+    uint32_t* __restrict__ n_pos, uint32_t* __restrict__ flags) {
+    __shared__ uint64_t s_out[kCombineThreads];
+    __shared__ uint32_t s_n, s_base;
     const int q = blockIdx.y;
-    const uint64_t* table = tables + ((size_t)q << log2h);
     const uint32_t hmask = (1u << log2h) - 1;
-    const uint32_t nbins = 1u << (log2h - 3);
-    const uint32_t nbins_mask = nbins - 1;
-    uint64_t* out = keys + (size_t)q * key_cap;
-    int n_out = 0;
-    const uint32_t bin0 = ((uint32_t)blockIdx.x * kCombineWarps + warp) * bins_per_warp;
-    for (int bi = 0; bi < bins_per_warp; ++bi) {
-        const uint32_t bin = bin0 + bi;
-        if (bin >= nbins) break;
-        // 1) collect the entries homed at `bin`
-        int n_bin = 0;
-        const uint32_t first = bin * 8;
-        for (uint32_t base = 0; base <= hmask; base += 32) {
-            const uint32_t slot = (first + base + lane) & hmask;
-            const uint64_t e = table[slot];
-            const bool empty = (e == kEmpty);
-            bool mine = false;
-            if (!empty) mine = bin_of((uint32_t)(e >> 37), nbins_mask) == bin;
-            const uint32_t mb = __ballot_sync(0xffffffffu, mine);
-            if (mine) {
-                const int at = n_bin + __popc(mb & ((1u << lane) - 1));
-                if (at < kBinCap) s_bin[warp][at] = e;
-            }
-            n_bin += __popc(mb);
-            // chain end: an empty slot at or after slot 8*bin + 7
-            const uint32_t stop = __ballot_sync(0xffffffffu, empty && (base + lane) >= 7);
-            if (stop) break;
+    const uint32_t nbins_mask = (1u << (log2h - 3)) - 1;
+    const uint64_t* table = tables + ((size_t)q << log2h);
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    const uint32_t slot = blockIdx.x * kCombineThreads + threadIdx.x;
+    const uint64_t e = (slot <= hmask) ? table[slot] : kEmpty;
+    if (e != kEmpty) {
+        const uint32_t doc = (uint32_t)(e >> 37);
+        const uint32_t home = bin_of(doc, nbins_mask) * 8;
+        // leader test: no earlier entry of this doc between its home and here
+        bool leader = true;
+        for (uint32_t x = home; x != slot; x = (x + 1) & hmask) {
+            const uint64_t o = table[x];
+            if (o != kEmpty && (uint32_t)(o >> 37) == doc) { leader = false; break; }
         }
-        if (n_bin > kBinCap) {
-            if (lane == 0) atomicOr(flags + q, 2u);
-            n_bin = kBinCap;
-        }
-        __syncwarp();
-        // 2) group by doc, tree-sum over t
-        for (int i0 = 0; i0 < n_bin; ++i0) {
-            const uint64_t lead = s_bin[warp][i0];
-            if (lead == kEmpty) continue;               // already grouped
-            const uint32_t doc = (uint32_t)(lead >> 37);
-            s_vals[warp][lane] = 0.0f;
-            __syncwarp();
-            for (int j = i0 + lane; j < n_bin; j += 32) {
-                const uint64_t e = s_bin[warp][j];
-                if (e != kEmpty && (uint32_t)(e >> 37) == doc) {
-                    s_vals[warp][(e >> 32) & 31] = __uint_as_float((uint32_t)e);
-                    s_bin[warp][j] = kEmpty;
-                }
-            }
-            __syncwarp();
-            float x = s_vals[warp][lane];
+        if (leader) {
+            float v[32];
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
-            if (lane == 0) {
-                s_out[warp][n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~doc);
+            for (int t = 0; t < 32; ++t) v[t] = 0.0f;
+            v[(e >> 32) & 31] = __uint_as_float((uint32_t)e);
+            // the doc's other entries lie before the first empty slot at or
+            // after home + 7
+            for (uint32_t x = (slot + 1) & hmask, dist = (slot - home + 1) & hmask; dist <= hmask;
+                 x = (x + 1) & hmask, ++dist) {
+                const uint64_t o = table[x];
+                if (o == kEmpty) {
+                    if (dist >= 7) break;
+                    continue;
+                }
+                if ((uint32_t)(o >> 37) == doc) v[(o >> 32) & 31] = __uint_as_float((uint32_t)o);
             }
-            ++n_out;
-            if (n_out == kOutCap) {
-                __syncwarp();
-                uint32_t at = 0;
-                if (lane == 0) at = atomicAdd(n_pos + q, (uint32_t)n_out);
-                at = __shfl_sync(0xffffffffu, at, 0);
-                for (int j = lane; j < n_out; j += 32)
-                    if (at + j < key_cap) out[at + j] = s_out[warp][j];
-                n_out = 0;
-            }
-            __syncwarp();
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+                for (int i = 0; i < off; ++i) v[i] = fadd(v[i], v[i + off]);
+            const uint32_t at = atomicAdd(&s_n, 1u);
+            s_out[at] = ((uint64_t)__float_as_uint(v[0]) << 32) | (uint32_t)(~doc);
         }
     }
-    __syncwarp();
-    if (n_out > 0) {
-        uint32_t at = 0;
-        if (lane == 0) at = atomicAdd(n_pos + q, (uint32_t)n_out);
-        at = __shfl_sync(0xffffffffu, at, 0);
-        for (int j = lane; j < n_out; j += 32)
-            if (at + j < key_cap) out[at + j] = s_out[warp][j];
+    __syncthreads();
+    if (threadIdx.x == 0 && s_n) s_base = atomicAdd(n_pos + q, s_n);
+    __syncthreads();
+    uint64_t* out = keys + (size_t)q * key_cap;
+    for (uint32_t i = threadIdx.x; i < s_n; i += blockDim.x) {
+        if (s_base + i < key_cap) out[s_base + i] = s_out[i];
+        else atomicOr(flags + q, 4u);
     }
 }
 
@@ -523,12 +496,8 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     dim3 g1(kQ * splits, nq);
     stage1_score_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits);
     CHM_TRY(launch_status("stage1_score_kernel"));
-    const int bins_per_warp = 16;
-    const int64_t nbins = 1ll << (l - 3);
-    const int64_t cblocks = (nbins + kCombineWarps * bins_per_warp - 1) / (kCombineWarps * bins_per_warp);
-    dim3 g2((unsigned)cblocks, nq);
-    stage1_combine_kernel<<<g2, kCombineWarps * 32, 0, st>>>(tables, l, bins_per_warp, keys, key_cap,
-                                                             n_pos, flags);
+    dim3 g2((unsigned)((1ll << l) / kCombineThreads), nq);
+    stage1_combine_kernel<<<g2, kCombineThreads, 0, st>>>(tables, l, keys, key_cap, n_pos, flags);
     CHM_TRY(launch_status("stage1_combine_kernel"));
     CHM_CUDA(cudaMemsetAsync(bitmaps, 0, sizeof(uint32_t) * (size_t)nq * words, st));
     // queries whose positives fall short of k_refine get the visited-doc bitmap

@@ -43,6 +43,7 @@ constexpr int kBoxBytes = 128 * 64 * 2;             // one 128 x 64 bf16 TMA box
 constexpr int kTileBytes = 2 * kBoxBytes;           // 128 x 128 bf16
 constexpr int kTopA = 16;                           // assignment candidates per row
 constexpr int kFallbackRows = 16;                   // rows recomputed exactly at a time
+constexpr int kMaxSplits = 296;                     // centroid-range splits per row tile
 constexpr uint32_t kIdesc = sm100::idesc_bf16_f32(kTM, kTN);
 
 enum TcMode { kStore = 0, kFilter = 1, kTop16 = 2 };
@@ -336,19 +337,29 @@ __global__ void __launch_bounds__(kRerankThreads) probe_rerank_kernel(
     if (threadIdx.x == 0) { s_total = 0; s_bad = 0; }
     if (threadIdx.x < kDim) s_q[threadIdx.x] = q_rows[row * kDim + threadIdx.x];
     __syncthreads();
-    // gather survivors of every split
-    for (int sp = 0; sp < splits; ++sp) {
-        const int c = surv_cnt[(size_t)row * splits + sp];
-        if (c > cap) s_bad = 1;
-        const int n = min(c, cap);
-        const int base = s_total;
-        __syncthreads();
-        for (int i = threadIdx.x; i < n; i += blockDim.x)
-            if (base + i < kSurvMax) s_keys[base + i] = surv[((size_t)row * splits + sp) * cap + i];
-        __syncthreads();
-        if (threadIdx.x == 0) s_total = base + n;
-        __syncthreads();
+    // gather survivors of every split: offsets by one thread, then a flat copy
+    __shared__ int s_off[kMaxSplits + 1];
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        s_off[0] = 0;
+        for (int sp = 0; sp < splits; ++sp) {
+            const int c = surv_cnt[(size_t)row * splits + sp];
+            if (c > cap) s_bad = 1;
+            acc += min(c, cap);
+            s_off[sp + 1] = acc;
+        }
+        s_total = acc;
     }
+    __syncthreads();
+    for (int i = threadIdx.x; i < min(s_total, kSurvMax); i += blockDim.x) {
+        int lo = 0, hi = splits;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (s_off[mid + 1] <= i) lo = mid + 1; else hi = mid;
+        }
+        s_keys[i] = surv[((size_t)row * splits + lo) * cap + (i - s_off[lo])];
+    }
+    __syncthreads();
     const int total = s_total;
     if (total > kSurvMax || total < nprobe) s_bad = 1;
     __syncthreads();
@@ -519,9 +530,11 @@ static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
     p.prefix = (int)std::min<int64_t>(nc, ((p.prefix + kTN - 1) / kTN) * kTN);
     const int64_t row_tiles = (rows + kTM - 1) / kTM;
     const int n_tiles = (int)((nc + kTN - 1) / kTN);
+    // about two CTAs' worth of work per SM: small batches split the centroid
+    // range across many CTAs so a single query still uses the whole GPU
     int splits = (int)std::max<int64_t>(1, (2 * 148 + row_tiles - 1) / row_tiles);
-    splits = std::min(splits, n_tiles);
-    splits = std::min(splits, 16);
+    splits = std::min(splits, std::max(1, n_tiles / 8));
+    splits = std::min(splits, kMaxSplits);
     p.splits = splits;
     const double expect = (double)p.kc * nc / std::max(1, p.prefix);
     p.cap = (int)std::min<double>(kSurvMax, std::max(64.0, 4.0 * expect / splits + 64));
