@@ -12,7 +12,7 @@
 //            open-addressing table with max semantics.
 //  combine : one warp per table bin; the entries homed at a bin are grouped
 //            by doc and summed over the 32 query tokens with the reference's
-//            shuffle-down tree (kernels.cu:192-198), giving 64-bit keys
+//            tree (kernels.cu:192-198), giving 64-bit keys
 //            (partial score bits << 32 | ~doc).
 //  select  : one CTA per query; exact radix select of the top k_refine keys
 //            and a bitonic sort (score desc, doc asc == stable descending
@@ -25,9 +25,9 @@
 // float bits of the max positive distance in the low word (positive floats
 // order like their bit patterns, so a 64-bit atomicMax on a slot holding the
 // same key keeps the larger distance).  A doc's entries are homed in one
-// 8-slot bin (slot = bin * 8 + (t & 7)) with linear probing, so every entry
-// homed at bin b lies between slot 8b and the first empty slot at or after
-// slot 8b + 7.
+// 32-slot bin (slot = bin * 32 + t) with linear probing, so every entry
+// homed at bin b lies between slot 32b and the first empty slot at or after
+// slot 32b + 31.
 #include "common.cuh"
 
 namespace chm {
@@ -35,6 +35,10 @@ namespace chm {
 constexpr uint64_t kEmpty = ~0ull;
 constexpr int kScoreThreads = 256;
 constexpr int kSelectThreads = 1024;
+
+// Docs hash to 32-slot bins; a doc's entry for query token t starts probing
+// at slot bin * 32 + t, so one warp load covers a bin.
+constexpr int kBinShift = 5;
 
 __device__ __forceinline__ uint32_t bin_of(uint32_t doc, uint32_t nbins_mask) {
     return (doc * 0x9E3779B1u) >> 7 & nbins_mask;
@@ -89,7 +93,7 @@ __device__ __forceinline__ void table_insert(uint64_t* table, uint32_t hmask, ui
                                              uint32_t doc, int t, float dist, uint32_t* flag) {
     const uint32_t key = (doc << 5) | (uint32_t)t;
     const uint64_t val = ((uint64_t)key << 32) | __float_as_uint(dist);
-    uint32_t slot = bin_of(doc, nbins_mask) * 8 + (t & 7);
+    uint32_t slot = (bin_of(doc, nbins_mask) << kBinShift) + (uint32_t)t;
     for (uint32_t probe = 0; probe <= hmask; ++probe, slot = (slot + 1) & hmask) {
         uint64_t cur = table[slot];
         if (cur == kEmpty) {
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(kScoreThreads) stage1_score_kernel(Stage1Ctx c
     const float cb1 = c.cb1[q * kQ + t];
     uint64_t* table = c.tables + ((size_t)q << c.log2h);
     const uint32_t hmask = (1u << c.log2h) - 1;
-    const uint32_t nbins_mask = (1u << (c.log2h - 3)) - 1;
+    const uint32_t nbins_mask = (1u << (c.log2h - kBinShift)) - 1;
     for (int v = lo + threadIdx.x; v < hi; v += blockDim.x) {
         // upper_bound over the prefix (lists are visited in label order)
         int a = 0, b = c.nprobe;
@@ -170,66 +174,123 @@ __global__ void __launch_bounds__(kScoreThreads) stage1_mark_kernel(
     }
 }
 
-constexpr int kCombineThreads = 256;
+constexpr int kCombineWarps = 8;
+constexpr int kBinCap = 128;   // entries homed at one bin held in shared memory
 
-// One thread per table slot.  The slot holding the first entry of a doc
-// (counting from the doc's home slot) makes that thread the doc's leader: it
-// gathers the doc's entries from the rest of the probe chain, sums the 32
-// per-query-token maxima with the reference's tree (zeros for absent tokens,
-// kernels.cu:192-198) and emits the 64-bit key (score bits << 32 | ~doc).
-__global__ void __launch_bounds__(kCombineThreads) stage1_combine_kernel(
+// Tree sum (kernels.cu:192-198) of one doc whose entries sit in the warp's
+// staged list: lane t picks the value for query token t (0 when absent) and
+// the shuffle-down tree adds them in the reference order.
+__device__ __forceinline__ float doc_tree_sum(const uint64_t* ent, int n, uint32_t doc, float* scratch) {
+    const int lane = threadIdx.x & 31;
+    scratch[lane] = 0.0f;
+    __syncwarp();
+    for (int j = lane; j < n; j += 32) {
+        const uint64_t e = ent[j];
+        if ((uint32_t)(e >> 37) == doc) scratch[(e >> 32) & 31] = __uint_as_float((uint32_t)e);
+    }
+    __syncwarp();
+    float x = scratch[lane];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+    __syncwarp();
+    return __shfl_sync(0xffffffffu, x, 0);
+}
+
+// One warp per 32-slot bin.  The bin's own entries (homed here; the probe
+// chain may run past the bin) are staged in shared memory and grouped by doc.
+// A doc's partial score is the reference's tree over its 32 per-token maxima
+// with zeros for absent tokens: with one entry that is the entry itself and
+// with two it is their sum (adding zeros is exact), so only docs with three or
+// more entries need the ordered tree.
+__global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
     const uint64_t* __restrict__ tables, int log2h, uint64_t* __restrict__ keys, int64_t key_cap,
     uint32_t* __restrict__ n_pos, uint32_t* __restrict__ flags) {
-    __shared__ uint64_t s_out[kCombineThreads];
-    __shared__ uint32_t s_n, s_base;
+    __shared__ uint64_t s_ent[kCombineWarps][kBinCap];
+    __shared__ uint64_t s_out[kCombineWarps][kBinCap];
+    __shared__ float s_scr[kCombineWarps][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.y;
     const uint32_t hmask = (1u << log2h) - 1;
-    const uint32_t nbins_mask = (1u << (log2h - 3)) - 1;
+    const uint32_t nbins = 1u << (log2h - kBinShift);
+    const uint32_t nbins_mask = nbins - 1;
+    const uint32_t bin = blockIdx.x * kCombineWarps + warp;
+    if (bin >= nbins) return;
     const uint64_t* table = tables + ((size_t)q << log2h);
-    if (threadIdx.x == 0) s_n = 0;
-    __syncthreads();
-    const uint32_t slot = blockIdx.x * kCombineThreads + threadIdx.x;
-    const uint64_t e = (slot <= hmask) ? table[slot] : kEmpty;
-    if (e != kEmpty) {
-        const uint32_t doc = (uint32_t)(e >> 37);
-        const uint32_t home = bin_of(doc, nbins_mask) * 8;
-        // leader test: no earlier entry of this doc between its home and here
-        bool leader = true;
-        for (uint32_t x = home; x != slot; x = (x + 1) & hmask) {
-            const uint64_t o = table[x];
-            if (o != kEmpty && (uint32_t)(o >> 37) == doc) { leader = false; break; }
+    const uint32_t first = bin << kBinShift;
+    uint64_t* ent = s_ent[warp];
+    uint64_t* outb = s_out[warp];
+    // 1) stage the bin's own entries
+    int n = 0;
+    for (uint32_t base = 0; base <= hmask; base += 32) {
+        const uint64_t e = __ldcs(table + ((first + base + lane) & hmask));
+        const bool empty = (e == kEmpty);
+        const bool mine = !empty && bin_of((uint32_t)(e >> 37), nbins_mask) == bin;
+        const uint32_t mb = __ballot_sync(0xffffffffu, mine);
+        if (mine) {
+            const int at = n + __popc(mb & ((1u << lane) - 1));
+            if (at < kBinCap) ent[at] = e;
         }
-        if (leader) {
-            float v[32];
-#pragma unroll
-            for (int t = 0; t < 32; ++t) v[t] = 0.0f;
-            v[(e >> 32) & 31] = __uint_as_float((uint32_t)e);
-            // the doc's other entries lie before the first empty slot at or
-            // after home + 7
-            for (uint32_t x = (slot + 1) & hmask, dist = (slot - home + 1) & hmask; dist <= hmask;
-                 x = (x + 1) & hmask, ++dist) {
-                const uint64_t o = table[x];
-                if (o == kEmpty) {
-                    if (dist >= 7) break;
-                    continue;
-                }
-                if ((uint32_t)(o >> 37) == doc) v[(o >> 32) & 31] = __uint_as_float((uint32_t)o);
-            }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-                for (int i = 0; i < off; ++i) v[i] = fadd(v[i], v[i + off]);
-            const uint32_t at = atomicAdd(&s_n, 1u);
-            s_out[at] = ((uint64_t)__float_as_uint(v[0]) << 32) | (uint32_t)(~doc);
+        n += __popc(mb);
+        // the chain ends at the first empty slot at or after slot 32 * bin + 31
+        if (__ballot_sync(0xffffffffu, empty && (base + lane) >= 31)) break;
+    }
+    if (n > kBinCap) {
+        if (lane == 0) atomicOr(flags + q, 2u);
+        n = kBinCap;
+    }
+    __syncwarp();
+    int n_out = 0;
+    if (n <= 32) {
+        const bool act = lane < n;
+        const uint64_t e = act ? ent[lane] : kEmpty;
+        const uint32_t doc = act ? (uint32_t)(e >> 37) : 0xFFFFFFFFu;
+        const float val = __uint_as_float((uint32_t)e);
+        const uint32_t grp = __match_any_sync(0xffffffffu, doc);
+        const int cnt = __popc(grp);
+        const int lead = __ffs(grp) - 1;
+        const float partner = __shfl_sync(0xffffffffu, val, 31 - __clz(grp));  // highest lane of the group
+        const bool leader = act && lane == lead;
+        // singles and pairs finish lane-parallel
+        const bool easy = leader && cnt <= 2;
+        const uint32_t eb = __ballot_sync(0xffffffffu, easy);
+        if (easy) {
+            const float x = cnt == 1 ? val : fadd(val, partner);
+            outb[__popc(eb & ((1u << lane) - 1))] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~doc);
+        }
+        n_out = __popc(eb);
+        // docs with three or more entries: ordered tree, one doc at a time
+        uint32_t hard = __ballot_sync(0xffffffffu, leader && cnt > 2);
+        while (hard) {
+            const int l = __ffs(hard) - 1;
+            hard &= hard - 1;
+            const uint32_t d = __shfl_sync(0xffffffffu, doc, l);
+            const float x = doc_tree_sum(ent, n, d, s_scr[warp]);
+            if (lane == 0) outb[n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~d);
+            ++n_out;
+        }
+    } else {
+        // rare (a crowded bin): the first entry of each doc in the staged list
+        // leads its doc through the ordered tree
+        for (int i = 0; i < n; ++i) {
+            const uint32_t d = (uint32_t)(ent[i] >> 37);
+            bool seen = false;
+            for (int j = lane; j < i; j += 32) seen |= ((uint32_t)(ent[j] >> 37) == d);
+            if (__any_sync(0xffffffffu, seen)) continue;
+            const float x = doc_tree_sum(ent, n, d, s_scr[warp]);
+            if (lane == 0 && n_out < kBinCap) outb[n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~d);
+            ++n_out;
         }
     }
-    __syncthreads();
-    if (threadIdx.x == 0 && s_n) s_base = atomicAdd(n_pos + q, s_n);
-    __syncthreads();
-    uint64_t* out = keys + (size_t)q * key_cap;
-    for (uint32_t i = threadIdx.x; i < s_n; i += blockDim.x) {
-        if (s_base + i < key_cap) out[s_base + i] = s_out[i];
-        else atomicOr(flags + q, 4u);
+    __syncwarp();
+    if (n_out) {
+        uint32_t at = 0;
+        if (lane == 0) at = atomicAdd(n_pos + q, (uint32_t)n_out);
+        at = __shfl_sync(0xffffffffu, at, 0);
+        uint64_t* out = keys + (size_t)q * key_cap;
+        for (int j = lane; j < n_out; j += 32) {
+            if (at + j < key_cap) out[at + j] = outb[j];
+            else atomicOr(flags + q, 4u);
+        }
     }
 }
 
@@ -283,10 +344,10 @@ __device__ void block_sort_desc(uint64_t* a, int n) {
 // Is `doc` present in the query's table (any query token)?
 __device__ bool table_has_doc(const uint64_t* table, uint32_t hmask, uint32_t nbins_mask,
                               uint32_t doc) {
-    const uint32_t first = bin_of(doc, nbins_mask) * 8;
+    const uint32_t first = bin_of(doc, nbins_mask) << kBinShift;
     for (uint32_t i = 0; i <= hmask; ++i) {
         const uint64_t e = table[(first + i) & hmask];
-        if (e == kEmpty) { if (i >= 7) return false; else continue; }
+        if (e == kEmpty) { if (i >= 31) return false; else continue; }
         if ((uint32_t)(e >> 37) == doc) return true;
     }
     return false;
@@ -377,7 +438,7 @@ __global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
         const uint32_t* bm = bitmaps + (size_t)q * words;
         const uint64_t* table = tables + ((size_t)q << log2h);
         const uint32_t hmask = (1u << log2h) - 1;
-        const uint32_t nbins_mask = (1u << (log2h - 3)) - 1;
+        const uint32_t nbins_mask = (1u << (log2h - kBinShift)) - 1;
         const int64_t per = (words + blockDim.x - 1) / blockDim.x;
         const int64_t w0 = threadIdx.x * per, w1 = min(words, w0 + per);
         uint32_t zeros = 0, marked = 0;
@@ -496,8 +557,9 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     dim3 g1(kQ * splits, nq);
     stage1_score_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits);
     CHM_TRY(launch_status("stage1_score_kernel"));
-    dim3 g2((unsigned)((1ll << l) / kCombineThreads), nq);
-    stage1_combine_kernel<<<g2, kCombineThreads, 0, st>>>(tables, l, keys, key_cap, n_pos, flags);
+    const int64_t nbins = 1ll << (l - kBinShift);
+    dim3 g2((unsigned)((nbins + kCombineWarps - 1) / kCombineWarps), nq);
+    stage1_combine_kernel<<<g2, kCombineWarps * 32, 0, st>>>(tables, l, keys, key_cap, n_pos, flags);
     CHM_TRY(launch_status("stage1_combine_kernel"));
     CHM_CUDA(cudaMemsetAsync(bitmaps, 0, sizeof(uint32_t) * (size_t)nq * words, st));
     // queries whose positives fall short of k_refine get the visited-doc bitmap
