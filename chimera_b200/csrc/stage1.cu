@@ -208,89 +208,103 @@ __global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
     __shared__ uint64_t s_ent[kCombineWarps][kBinCap];
     __shared__ uint64_t s_out[kCombineWarps][kBinCap];
     __shared__ float s_scr[kCombineWarps][32];
+    __shared__ uint32_t s_cnt[kCombineWarps + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q = blockIdx.y;
+    // queries vary fastest across the grid so that concurrently running blocks
+    // spread their output-counter atomics over many queries
+    const int q = blockIdx.x;
     const uint32_t hmask = (1u << log2h) - 1;
     const uint32_t nbins = 1u << (log2h - kBinShift);
     const uint32_t nbins_mask = nbins - 1;
-    const uint32_t bin = blockIdx.x * kCombineWarps + warp;
-    if (bin >= nbins) return;
-    const uint64_t* table = tables + ((size_t)q << log2h);
-    const uint32_t first = bin << kBinShift;
-    uint64_t* ent = s_ent[warp];
-    uint64_t* outb = s_out[warp];
-    // 1) stage the bin's own entries
-    int n = 0;
-    for (uint32_t base = 0; base <= hmask; base += 32) {
-        const uint64_t e = __ldcs(table + ((first + base + lane) & hmask));
-        const bool empty = (e == kEmpty);
-        const bool mine = !empty && bin_of((uint32_t)(e >> 37), nbins_mask) == bin;
-        const uint32_t mb = __ballot_sync(0xffffffffu, mine);
-        if (mine) {
-            const int at = n + __popc(mb & ((1u << lane) - 1));
-            if (at < kBinCap) ent[at] = e;
+    // nbins is a multiple of kCombineWarps; grid.y is capped, so blocks stride over bin groups
+    for (uint32_t grp0 = blockIdx.y; grp0 < nbins / kCombineWarps; grp0 += gridDim.y) {
+        const uint32_t bin = grp0 * kCombineWarps + warp;
+        const uint64_t* table = tables + ((size_t)q << log2h);
+        const uint32_t first = bin << kBinShift;
+        uint64_t* ent = s_ent[warp];
+        uint64_t* outb = s_out[warp];
+        // 1) stage the bin's own entries
+        int n = 0;
+        for (uint32_t base = 0; base <= hmask; base += 32) {
+            const uint64_t e = __ldcs(table + ((first + base + lane) & hmask));
+            const bool empty = (e == kEmpty);
+            const bool mine = !empty && bin_of((uint32_t)(e >> 37), nbins_mask) == bin;
+            const uint32_t mb = __ballot_sync(0xffffffffu, mine);
+            if (mine) {
+                const int at = n + __popc(mb & ((1u << lane) - 1));
+                if (at < kBinCap) ent[at] = e;
+            }
+            n += __popc(mb);
+            // the chain ends at the first empty slot at or after slot 32 * bin + 31
+            if (__ballot_sync(0xffffffffu, empty && (base + lane) >= 31)) break;
         }
-        n += __popc(mb);
-        // the chain ends at the first empty slot at or after slot 32 * bin + 31
-        if (__ballot_sync(0xffffffffu, empty && (base + lane) >= 31)) break;
-    }
-    if (n > kBinCap) {
-        if (lane == 0) atomicOr(flags + q, 2u);
-        n = kBinCap;
-    }
-    __syncwarp();
-    int n_out = 0;
-    if (n <= 32) {
-        const bool act = lane < n;
-        const uint64_t e = act ? ent[lane] : kEmpty;
-        const uint32_t doc = act ? (uint32_t)(e >> 37) : 0xFFFFFFFFu;
-        const float val = __uint_as_float((uint32_t)e);
-        const uint32_t grp = __match_any_sync(0xffffffffu, doc);
-        const int cnt = __popc(grp);
-        const int lead = __ffs(grp) - 1;
-        const float partner = __shfl_sync(0xffffffffu, val, 31 - __clz(grp));  // highest lane of the group
-        const bool leader = act && lane == lead;
-        // singles and pairs finish lane-parallel
-        const bool easy = leader && cnt <= 2;
-        const uint32_t eb = __ballot_sync(0xffffffffu, easy);
-        if (easy) {
-            const float x = cnt == 1 ? val : fadd(val, partner);
-            outb[__popc(eb & ((1u << lane) - 1))] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~doc);
+        if (n > kBinCap) {
+            if (lane == 0) atomicOr(flags + q, 2u);
+            n = kBinCap;
         }
-        n_out = __popc(eb);
-        // docs with three or more entries: ordered tree, one doc at a time
-        uint32_t hard = __ballot_sync(0xffffffffu, leader && cnt > 2);
-        while (hard) {
-            const int l = __ffs(hard) - 1;
-            hard &= hard - 1;
-            const uint32_t d = __shfl_sync(0xffffffffu, doc, l);
-            const float x = doc_tree_sum(ent, n, d, s_scr[warp]);
-            if (lane == 0) outb[n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~d);
-            ++n_out;
+        __syncwarp();
+        int n_out = 0;
+        if (n <= 32) {
+            const bool act = lane < n;
+            const uint64_t e = act ? ent[lane] : kEmpty;
+            const uint32_t doc = act ? (uint32_t)(e >> 37) : 0xFFFFFFFFu;
+            const float val = __uint_as_float((uint32_t)e);
+            const uint32_t grp = __match_any_sync(0xffffffffu, doc);
+            const int cnt = __popc(grp);
+            const int lead = __ffs(grp) - 1;
+            const float partner = __shfl_sync(0xffffffffu, val, 31 - __clz(grp));  // highest lane of the group
+            const bool leader = act && lane == lead;
+            // singles and pairs finish lane-parallel
+            const bool easy = leader && cnt <= 2;
+            const uint32_t eb = __ballot_sync(0xffffffffu, easy);
+            if (easy) {
+                const float x = cnt == 1 ? val : fadd(val, partner);
+                outb[__popc(eb & ((1u << lane) - 1))] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~doc);
+            }
+            n_out = __popc(eb);
+            // docs with three or more entries: ordered tree, one doc at a time
+            uint32_t hard = __ballot_sync(0xffffffffu, leader && cnt > 2);
+            while (hard) {
+                const int l = __ffs(hard) - 1;
+                hard &= hard - 1;
+                const uint32_t d = __shfl_sync(0xffffffffu, doc, l);
+                const float x = doc_tree_sum(ent, n, d, s_scr[warp]);
+                if (lane == 0) outb[n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~d);
+                ++n_out;
+            }
+        } else {
+            // rare (a crowded bin): the first entry of each doc in the staged list
+            // leads its doc through the ordered tree
+            for (int i = 0; i < n; ++i) {
+                const uint32_t d = (uint32_t)(ent[i] >> 37);
+                bool seen = false;
+                for (int j = lane; j < i; j += 32) seen |= ((uint32_t)(ent[j] >> 37) == d);
+                if (__any_sync(0xffffffffu, seen)) continue;
+                const float x = doc_tree_sum(ent, n, d, s_scr[warp]);
+                if (lane == 0 && n_out < kBinCap) outb[n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~d);
+                ++n_out;
+            }
         }
-    } else {
-        // rare (a crowded bin): the first entry of each doc in the staged list
-        // leads its doc through the ordered tree
-        for (int i = 0; i < n; ++i) {
-            const uint32_t d = (uint32_t)(ent[i] >> 37);
-            bool seen = false;
-            for (int j = lane; j < i; j += 32) seen |= ((uint32_t)(ent[j] >> 37) == d);
-            if (__any_sync(0xffffffffu, seen)) continue;
-            const float x = doc_tree_sum(ent, n, d, s_scr[warp]);
-            if (lane == 0 && n_out < kBinCap) outb[n_out] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~d);
-            ++n_out;
+        // one output-counter atomic per block
+        if (lane == 0) s_cnt[warp] = (uint32_t)n_out;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t tot = 0;
+            for (int w = 0; w < kCombineWarps; ++w) {
+                const uint32_t c = s_cnt[w];
+                s_cnt[w] = tot;
+                tot += c;
+            }
+            s_cnt[kCombineWarps] = tot ? atomicAdd(n_pos + q, tot) : 0u;
         }
-    }
-    __syncwarp();
-    if (n_out) {
-        uint32_t at = 0;
-        if (lane == 0) at = atomicAdd(n_pos + q, (uint32_t)n_out);
-        at = __shfl_sync(0xffffffffu, at, 0);
+        __syncthreads();
+        const uint32_t at = s_cnt[kCombineWarps] + s_cnt[warp];
         uint64_t* out = keys + (size_t)q * key_cap;
         for (int j = lane; j < n_out; j += 32) {
-            if (at + j < key_cap) out[at + j] = outb[j];
+            if ((int64_t)at + j < key_cap) out[at + j] = outb[j];
             else atomicOr(flags + q, 4u);
         }
+        __syncthreads();  // s_cnt and the staging buffers are reused by the next group
     }
 }
 
@@ -558,7 +572,7 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     stage1_score_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits);
     CHM_TRY(launch_status("stage1_score_kernel"));
     const int64_t nbins = 1ll << (l - kBinShift);
-    dim3 g2((unsigned)((nbins + kCombineWarps - 1) / kCombineWarps), nq);
+    dim3 g2(nq, (unsigned)std::min<int64_t>(nbins / kCombineWarps, 65535));
     stage1_combine_kernel<<<g2, kCombineWarps * 32, 0, st>>>(tables, l, keys, key_cap, n_pos, flags);
     CHM_TRY(launch_status("stage1_combine_kernel"));
     CHM_CUDA(cudaMemsetAsync(bitmaps, 0, sizeof(uint32_t) * (size_t)nq * words, st));
