@@ -22,6 +22,8 @@ DIM = 128
 QLEN = 32
 
 CHM_OK, CHM_ERR_INVALID, CHM_ERR_CAPACITY, CHM_ERR_CUDA, CHM_ERR_TIMEOUT, CHM_ERR_UNSUPPORTED = range(6)
+# include/chimera_b200.h: CHM_PROBE_NOALLOC_MAX_ELEMENTS (static scratch of chm_probe_noalloc)
+PROBE_NOALLOC_MAX_ELEMENTS = 1 << 22
 _STATUS = {1: "invalid argument", 2: "capacity", 3: "CUDA error", 4: "timeout", 5: "unsupported"}
 
 
@@ -68,6 +70,7 @@ EXPORTS = {
     "chm_prepare_queries": ([V, I32, I32, V, I64, V, V, V, V, V], C.c_int),
     "chm_probe_workspace_bytes": ([I64, I64, I32], SZ),
     "chm_probe": ([V, I64, V, V, I64, I32, V, V, SZ, V], C.c_int),
+    "chm_probe_noalloc": ([V, I64, V, V, I64, I32, V, V], C.c_int),
     "chm_stage1_workspace_bytes": ([V, I32, I32, I32], SZ),
     "chm_stage1": ([V, I32, V, V, V, I32, I32, V, V, V, V, V, SZ, V], C.c_int),
     "chm_refine_1bit": ([V, I32, V, V, V, V, I32, V, V], C.c_int),

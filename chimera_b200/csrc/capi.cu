@@ -20,6 +20,8 @@ void set_last_error(const char* where, cudaError_t err) {
     std::snprintf(g_err, sizeof(g_err), "%s: %s", where, cudaGetErrorString(err));
 }
 
+void set_last_message(const char* msg) { std::snprintf(g_err, sizeof(g_err), "%s", msg); }
+
 chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
                       const uint32_t* labels, int32_t nprobe, int32_t k_refine,
                       int32_t* refined_docs, float* refined_partial, int32_t* num_refined,

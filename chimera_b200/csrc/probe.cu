@@ -181,3 +181,73 @@ extern "C" chm_status chm_build_assign(const float* x, int64_t n, int32_t dim, c
     }
     return CHM_OK;
 }
+
+// ---- probe without allocation ---------------------------------------------
+// chm_probe_noalloc runs the same two kernels as chm_probe, with the distance
+// matrix in a file-scope device array instead of a caller workspace.  The
+// array is fully written by dist_gemm_kernel before row_select_kernel reads
+// it, so nothing in it has to start at zero.  One array per device: calls
+// that overlap on one device (two streams, two host threads) race on it.
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+
+namespace chm {
+
+void set_last_message(const char* msg);
+
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) float g_noalloc_probe_dist[CHM_PROBE_NOALLOC_MAX_ELEMENTS];
+static std::atomic<float*> g_noalloc_probe_ptr[kNoAllocMaxDevices];
+static std::mutex g_noalloc_probe_mu;
+
+// Device address of the static scratch for the current device, looked up once
+// per device with that device current.
+static chm_status noalloc_probe_scratch(float** out) {
+    int dev = 0;
+    CHM_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        set_last_message("chm_probe_noalloc: device ordinal beyond 63");
+        return CHM_ERR_UNSUPPORTED;
+    }
+    float* p = g_noalloc_probe_ptr[dev].load(std::memory_order_acquire);
+    if (!p) {
+        std::lock_guard<std::mutex> lock(g_noalloc_probe_mu);
+        p = g_noalloc_probe_ptr[dev].load(std::memory_order_acquire);
+        if (!p) {
+            void* addr = nullptr;
+            CHM_CUDA(cudaGetSymbolAddress(&addr, g_noalloc_probe_dist));
+            p = static_cast<float*>(addr);
+            g_noalloc_probe_ptr[dev].store(p, std::memory_order_release);
+        }
+    }
+    *out = p;
+    return CHM_OK;
+}
+
+}  // namespace chm
+
+extern "C" chm_status chm_probe_noalloc(const float* rot_queries, int64_t nrows, const float* centroids,
+                                        const float* centroid_norms, int64_t n_clusters, int32_t nprobe,
+                                        uint32_t* labels, void* stream) {
+    if (nrows <= 0) return CHM_OK;
+    if (nprobe <= 0 || nprobe > CHM_MAX_NPROBE || nprobe > n_clusters) return CHM_ERR_INVALID;
+    if (nrows > (int64_t)CHM_PROBE_NOALLOC_MAX_ELEMENTS / n_clusters) {
+        char msg[200];
+        std::snprintf(msg, sizeof(msg),
+                      "chm_probe_noalloc: nrows * n_clusters = %lld * %lld exceeds the static scratch of %lld "
+                      "floats",
+                      (long long)nrows, (long long)n_clusters, (long long)CHM_PROBE_NOALLOC_MAX_ELEMENTS);
+        chm::set_last_message(msg);
+        return CHM_ERR_CAPACITY;
+    }
+    float* dist = nullptr;
+    CHM_TRY(chm::noalloc_probe_scratch(&dist));
+    cudaStream_t st = (cudaStream_t)stream;
+    dim3 g((unsigned)((n_clusters + chm::BN - 1) / chm::BN), (unsigned)((nrows + chm::BM - 1) / chm::BM));
+    chm::dist_gemm_kernel<<<g, chm::kGemmThreads, 0, st>>>(rot_queries, nrows, centroids, centroid_norms,
+                                                           n_clusters, chm::kDim, chm::kDim, dist);
+    CHM_TRY(chm::launch_status("dist_gemm_kernel"));
+    chm::row_select_kernel<<<(unsigned)nrows, chm::kSelThreads, 0, st>>>(dist, n_clusters, nprobe, labels);
+    return chm::launch_status("row_select_kernel");
+}

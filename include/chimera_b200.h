@@ -114,6 +114,23 @@ chm_status chm_probe(const float* rot_queries, int64_t nrows, const float* centr
                      const float* centroid_norms, int64_t n_clusters, int32_t nprobe,
                      uint32_t* labels, void* workspace, size_t workspace_bytes, void* stream);
 
+/* chm_probe without allocation.  No counterpart in the reference: an addition
+ * for callers that must not allocate device memory per call.  Same result as
+ * chm_probe; the [nrows x n_clusters] fp32 distance scratch is a file-scope
+ * device array of CHM_PROBE_NOALLOC_MAX_ELEMENTS floats (16 MiB per device,
+ * reserved when the module loads), e.g. one 32-token query against up to
+ * 131,072 centroids.  Larger nrows * n_clusters returns CHM_ERR_CAPACITY
+ * (message in chm_last_error) and launches nothing.  The first call on each
+ * device performs a one-time setup (cudaGetSymbolAddress with that device
+ * current); make it before any stream capture begins.  The scratch needs no
+ * zeroing (it is fully written before it is read).  There is one scratch per
+ * device: calls that overlap on one device (two streams or two host threads)
+ * race, so serialise them. */
+#define CHM_PROBE_NOALLOC_MAX_ELEMENTS (1 << 22)
+chm_status chm_probe_noalloc(const float* rot_queries, int64_t nrows, const float* centroids,
+                             const float* centroid_norms, int64_t n_clusters, int32_t nprobe,
+                             uint32_t* labels, void* stream);
+
 /* Tensor-core probe with the same exact result: a bf16 tcgen05 pass proposes
  * candidates and exact fp32 re-ranking with an error-bound certificate (or an
  * exact recomputation of the row) decides.  nprobe <= 448. */
