@@ -22,6 +22,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libchimera_ref.so")
+REF_GPU_SO = os.path.join(HERE, "_ref", "libchimera_ref_gpu.so")
 DIM = 128
 QLEN = 32
 
@@ -125,6 +126,52 @@ def ref():
                                        C.POINTER(C.c_float)]
         _ref = R
     return _ref
+
+
+_ref_gpu = None
+
+
+def ref_gpu_available() -> bool:
+    return os.path.exists(REF_GPU_SO)
+
+
+def ref_gpu():
+    """The reference's own CUDA kernels (oracle/_ref), driven as search_impl.cu
+    drives them; needs a GPU."""
+    global _ref_gpu
+    if _ref_gpu is None:
+        R = C.CDLL(REF_GPU_SO)
+        R.cref_gpu_query_stages.argtypes = [
+            _f32p, _f32p, _u32p, C.c_int, _u8p, _f32p, _i32p, C.c_int64, _u64p, C.c_int64, _i32p, _u32p,
+            C.c_int64, C.c_int, C.c_int, _f32p, C.POINTER(C.c_int64), _i32p, _f32p, C.POINTER(C.c_int32),
+            _f32p, C.c_char_p, C.c_int]
+        R.cref_gpu_query_stages.restype = C.c_int
+        _ref_gpu = R
+    return _ref_gpu
+
+
+def ref_gpu_query_stages(index, rot_q, cb1, labels, nprobe, k_refine, num_chunks):
+    """Runs the reference kernels for one query: LUT, candidate set, sorted
+    partial scores (refined prefix) and 1-bit document scores."""
+    lut = np.zeros((32, 512), np.float32)
+    ncand = C.c_int64(0)
+    nref = C.c_int32(0)
+    rd = np.zeros(k_refine, np.int32)
+    rp = np.zeros(k_refine, np.float32)
+    ob = np.zeros(k_refine, np.float32)
+    err = C.create_string_buffer(512)
+    n_tokens = index.factor1.shape[0]
+    rc = ref_gpu().cref_gpu_query_stages(
+        np.ascontiguousarray(rot_q, np.float32), np.ascontiguousarray(cb1, np.float32),
+        np.ascontiguousarray(labels, np.uint32), nprobe, index.codes1.reshape(-1), index.factor1,
+        index.doc_ids, n_tokens, index.cluster_pos.astype(np.uint64), index.cluster_pos.shape[0] - 1,
+        index.doc_ptrs.astype(np.int32), index.tok2pos, index.doc_ptrs.shape[0] - 1, k_refine, num_chunks,
+        lut, C.byref(ncand), rd, rp, C.byref(nref), ob, err, 512)
+    if rc != 0:
+        raise RuntimeError(f"reference kernels failed ({rc}): {err.value.decode()}")
+    R = nref.value
+    return dict(lut=lut, n_candidates=ncand.value, n_refined=R, refined_docs=rd[:R].copy(),
+                refined_partial=rp[:R].copy(), onebit_scores=ob[:R].copy())
 
 
 # ---------------------------------------------------------------------------
