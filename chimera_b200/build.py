@@ -32,7 +32,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE,
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
-CU_SOURCES = ["capi.cu", "query_prep.cu", "probe.cu", "stage1.cu", "refine.cu", "build.cu", "tcgemm.cu"]
+CU_SOURCES = ["capi.cu", "query_prep.cu", "probe.cu", "stage1.cu", "refine.cu", "build.cu", "tcgemm.cu",
+              "shard.cu"]
 HOST_SOURCES = ["host/chimera_index.cpp", "host/io.cpp", "host/rng.cpp"]
 
 

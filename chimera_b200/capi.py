@@ -71,6 +71,10 @@ EXPORTS = {
     "chm_probe_workspace_bytes": ([I64, I64, I32], SZ),
     "chm_probe": ([V, I64, V, V, I64, I32, V, V, SZ, V], C.c_int),
     "chm_probe_noalloc": ([V, I64, V, V, I64, I32, V, V], C.c_int),
+    "chm_stage1_ex_workspace_bytes": ([V, I32, I32, I32], SZ),
+    "chm_stage1_ex": ([V, I32, V, V, V, I32, I32, V, V, V, V, I32, V, SZ, V], C.c_int),
+    "chm_merge_refined": ([I32, I32, I32, V, V, V, V, V, V, V, V], C.c_int),
+    "chm_shard_localize": ([I32, I32, V, V, I64, I64, V, V], C.c_int),
     "chm_stage1_workspace_bytes": ([V, I32, I32, I32], SZ),
     "chm_stage1": ([V, I32, V, V, V, I32, I32, V, V, V, V, V, SZ, V], C.c_int),
     "chm_refine_1bit": ([V, I32, V, V, V, V, I32, V, V], C.c_int),
@@ -214,13 +218,17 @@ class DeviceIndex:
                     full_factors=g(self.full_factors), ex_bits=self.ex_bits)
 
 
-def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, stream=None):
+def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, stream=None, centroids=None):
     """GPU index build (chimera_index::build, build_index.cu:394-501) from a
     device tensor of raw embeddings [N, dim] and host doc lengths.
 
     Reservoir-sampled centroids (host, std::mt19937_64) -> exact nearest
     centroid on the GPU -> stable cluster order -> GPU rotation + RaBitQ
-    encoding -> cluster-ordered 1-bit arrays."""
+    encoding -> cluster-ordered 1-bit arrays.
+
+    `centroids` ([n_clusters, dim] raw device tensor) replaces the sampling:
+    a document shard is built with the centroids sampled from the whole
+    corpus, so every shard shares the global cluster ids."""
     import time
 
     import torch
@@ -241,13 +249,21 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
         raise ValueError("Document lengths do not sum to the number of embeddings")
     flips_np = fhtkac_flips(seed)
     flips = torch.from_numpy(flips_np).to(dev)
-    ids = torch.from_numpy(sample_centroids(n, n_clusters, 42)).to(dev)
+    if centroids is None:
+        ids = torch.from_numpy(sample_centroids(n, n_clusters, 42)).to(dev)
+        cent_in = emb[ids].contiguous()
+    else:
+        if tuple(centroids.shape) != (n_clusters, dim):
+            raise ValueError("centroids must be [n_clusters, dim]")
+        cent_in = centroids.to(device=dev, dtype=torch.float32).contiguous()
     if dim < DIM:
         x128 = torch.zeros(n, DIM, dtype=torch.float32, device=dev)
         x128[:, :dim] = emb
+        cent_raw = torch.zeros(n_clusters, DIM, dtype=torch.float32, device=dev)
+        cent_raw[:, :dim] = cent_in
     else:
         x128 = emb.contiguous()
-    cent_raw = x128[ids].contiguous()
+        cent_raw = cent_in
     cn_raw = torch.empty(n_clusters, dtype=torch.float32, device=dev)
     L = lib()
     check(L.chm_row_norms(_ptr(cent_raw), n_clusters, _ptr(cn_raw), st), "row_norms")
@@ -262,7 +278,6 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
     rot_c = torch.empty(n_clusters, DIM, dtype=torch.float32, device=dev)
     cb1_c = torch.empty(n_clusters, dtype=torch.float32, device=dev)
     cbex_c = torch.empty(n_clusters, dtype=torch.float32, device=dev)
-    cent_in = emb[ids].contiguous()
     check(L.chm_prepare_queries(_ptr(flips), dim, ex_bits, _ptr(cent_in), n_clusters,
                                 _ptr(rot_c), _ptr(cb1_c), _ptr(cbex_c), None, st), "rotate centroids")
     cnorm = torch.empty(n_clusters, dtype=torch.float32, device=dev)

@@ -33,6 +33,10 @@ __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
     const int r = blockIdx.x * kRefineWarps + warp;
     if (r >= R) return;
     const int64_t doc = refined_docs[(size_t)q * k_refine + r];
+    if (doc < 0) {  // a slot another document shard owns
+        if (lane == 0) scores[(size_t)q * k_refine + r] = -INFINITY;
+        return;
+    }
     const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
     float m[kQ];
 #pragma unroll
@@ -212,6 +216,10 @@ __global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
     }
     const float cb = cbex[q * kQ + lane];
     const int64_t doc = fb_docs[(size_t)q * fb_cap + i];
+    if (doc < 0) {  // a slot another document shard owns
+        if (lane == 0) scores[(size_t)q * fb_cap + i] = -INFINITY;
+        return;
+    }
     const int bytes = kDim * w / 8;       // 16 * w, a multiple of 16
     const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
     float m = -INFINITY;

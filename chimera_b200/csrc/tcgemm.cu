@@ -334,6 +334,13 @@ __global__ void __launch_bounds__(kRerankThreads) probe_rerank_kernel(
     __shared__ float s_q[kDim];
     __shared__ int s_total, s_bad;
     const int64_t row = blockIdx.x;
+    // fallback_cnt[1] is the tensor-core kernels' error flag: a launch that
+    // gave up on a bounded wait left tiles unscored, so every row of the call
+    // takes the exact path instead
+    if (fallback_cnt[1] != 0u) {
+        if (threadIdx.x == 0) fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
+        return;
+    }
     if (threadIdx.x == 0) { s_total = 0; s_bad = 0; }
     if (threadIdx.x < kDim) s_q[threadIdx.x] = q_rows[row * kDim + threadIdx.x];
     __syncthreads();
@@ -408,6 +415,10 @@ __global__ void assign_rerank_kernel(const float* __restrict__ x, int64_t rows, 
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
+    if (fallback_cnt[1] != 0u) {  // tensor-core error flag: exact path for every row
+        if (lane == 0) fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
+        return;
+    }
     const float* q = x + row * kDim;
     float qn = 0.0f;
     for (int k = lane; k < kDim; k += 32) qn = fmaf(q[k], q[k], qn);

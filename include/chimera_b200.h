@@ -159,10 +159,23 @@ chm_status chm_stage1(const chm_index* index, int32_t nq, const float* lut, cons
                       int64_t* num_candidates, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* chm_stage1 with the per-query status flags (nonzero: the stage-1 table or
+ * key buffer overflowed; rerun with table_log2_extra + 1) and an explicit
+ * table size, for callers that drive the stages themselves (document-sharded
+ * search).  flags [nq]. */
+size_t chm_stage1_ex_workspace_bytes(const chm_index* index, int32_t nq, int32_t nprobe,
+                                     int32_t table_log2_extra);
+chm_status chm_stage1_ex(const chm_index* index, int32_t nq, const float* lut, const float* cb1,
+                         const uint32_t* labels, int32_t nprobe, int32_t k_refine,
+                         int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
+                         uint32_t* flags, int32_t table_log2_extra, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Segmented 1-bit MaxSim of the refined docs (replaces
  * gather_refined_doc_lengths/positions + one_bit_token_score +
  * one_bit_document_score kernels, kernels.cu:430-617,
- * search_impl.cu:278-403).  scores [nq * k_refine]. */
+ * search_impl.cu:278-403).  scores [nq * k_refine].  A negative doc id
+ * marks a slot another document shard owns; its score is -inf. */
 chm_status chm_refine_1bit(const chm_index* index, int32_t nq, const float* lut,
                            const float* cb1, const int32_t* refined_docs,
                            const int32_t* num_refined, int32_t k_refine, float* scores,
@@ -177,7 +190,8 @@ chm_status chm_select_fullbit(int32_t nq, const int32_t* refined_docs, const flo
 
 /* (1+ex_bits)-bit MaxSim of the selected docs (replaces the AVX-512
  * compute_full_bit_scores, search_impl.cu:510-574).
- * rot [nq*32*128], cbex [nq*32], scores [nq * fb_cap]. */
+ * rot [nq*32*128], cbex [nq*32], scores [nq * fb_cap].  A negative doc id
+ * marks a slot another document shard owns; its score is -inf. */
 chm_status chm_fullbit_score(const chm_index* index, int32_t nq, const float* rot,
                              const float* cbex, const int32_t* fb_docs, const int32_t* num_fb,
                              int32_t fb_cap, float* scores, void* stream);
@@ -195,6 +209,27 @@ chm_status chm_final_topk(int32_t nq, const int32_t* fb_docs, const float* fb_sc
 chm_status chm_merge_topk(int32_t nq, int32_t shards, int32_t k, const float* scores,
                           const int64_t* docs, const int32_t* counts, int64_t* results,
                           float* result_scores, int32_t* num_results, void* stream);
+
+/* Document-sharded search (no reference counterpart; the reference runs on
+ * one GPU).  Shard s holds docs [doc_base[s], doc_base[s] + its num_docs)
+ * with local ids.
+ *
+ * chm_merge_refined: the gathered stage-1 lists of all shards
+ * (docs/partial [shards][nq][k_refine] local ids, counts [shards][nq],
+ * doc_base [shards] device array) -> the refined list of the whole corpus,
+ * global ids, ordered by (partial score desc, doc asc) as the reference's
+ * stable radix sort orders it (search_impl.cu:245-261).
+ * out_docs/out_partial [nq][k_refine], out_counts [nq]. */
+chm_status chm_merge_refined(int32_t nq, int32_t shards, int32_t k_refine, const int32_t* docs,
+                             const float* partial, const int32_t* counts, const int64_t* doc_base,
+                             int32_t* out_docs, float* out_partial, int32_t* out_counts,
+                             void* stream);
+
+/* Global doc ids [nq][cap] (first counts[q] valid) -> this shard's local ids,
+ * -1 for documents outside [doc_base, doc_base + num_docs) and past counts. */
+chm_status chm_shard_localize(int32_t nq, int32_t cap, const int32_t* global_docs,
+                              const int32_t* counts, int64_t doc_base, int64_t num_docs,
+                              int32_t* local_docs, void* stream);
 
 /*
  * Index build (replaces build_index.cu:186-363 and quantization.cpp).

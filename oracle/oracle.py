@@ -87,6 +87,8 @@ def lib():
                                        C.POINTER(_Params), _i64p, _i32p, C.c_int]
         L.orc_fullbit_doc_score.argtypes = [C.POINTER(_Index), _f32p, _f32p, C.c_int64]
         L.orc_fullbit_doc_score.restype = C.c_float
+        L.orc_onebit_doc_score.argtypes = [C.POINTER(_Index), _f32p, _f32p, C.c_int64]
+        L.orc_onebit_doc_score.restype = C.c_float
         L.orc_pack.argtypes = [_u8p, _u8p, C.c_int, C.c_int]
         L.orc_unpack.argtypes = [_u8p, _u8p, C.c_int, C.c_int]
         L.orc_best_rescale_factor.argtypes = [_f32p, C.c_int, C.c_int]
@@ -364,6 +366,10 @@ class Index:
         if rc != 0:
             raise RuntimeError("oracle batch search failed")
         return res, nres
+
+    def onebit_doc_score(self, luts, cb1, doc):
+        return lib().orc_onebit_doc_score(C.byref(self._c), np.ascontiguousarray(luts, np.float32).reshape(-1),
+                                          np.ascontiguousarray(cb1, np.float32), int(doc))
 
     def fullbit_doc_score(self, rot_q, cbex, doc):
         return lib().orc_fullbit_doc_score(C.byref(self._c), np.ascontiguousarray(rot_q, np.float32),
