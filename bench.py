@@ -130,80 +130,113 @@ def main():
     args = ap.parse_args()
 
     import torch
-    from chimera_b200 import capi, workloads as W
+    from chimera_b200 import capi, workloads as W, sharded as SH
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and rank != 0:
+        return  # the CPU reference arm runs on rank 0 alone
     torch.cuda.set_device(local)
     dist = None
-    if world > 1:
+    if world > 1 and args.impl == "ours":
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    if args.impl == "reference" and rank != 0:
-        return
 
     cfg = W.CONFIGS[args.config]
     t0 = time.time()
-    # every rank holds a full replica and serves its own query stream
     emb, doclens, queries = W.generate_torch(cfg, seed=0)
     log(f"[bench] corpus {cfg.name}: {emb.shape[0]} tokens, {cfg.num_docs} docs ({time.time() - t0:.1f}s)")
     dl_host = doclens.cpu().numpy()
+    ptr_full = torch.from_numpy(W.doc_ptrs(dl_host)).to(emb.device)
     t0 = time.time()
-    index, _ = capi.build_index(emb, dl_host, cfg.n_clusters, cfg.ex_bits)
+    if world == 1 or args.impl == "reference":
+        index, _ = capi.build_index(emb, dl_host, cfg.n_clusters, cfg.ex_bits)
+        bases = [0, cfg.num_docs]
+    else:
+        # document shard: docs [bases[rank], bases[rank+1]) with the centroids
+        # sampled from the whole corpus (the single-GPU build's centroids)
+        bases = SH.shard_bounds(cfg.num_docs, world)
+        lo, hi = bases[rank], bases[rank + 1]
+        t_lo, t_hi = int(ptr_full[lo]), int(ptr_full[hi])
+        ids = torch.from_numpy(capi.sample_centroids(int(emb.shape[0]), cfg.n_clusters, 42)).to(emb.device)
+        cents = emb[ids].contiguous()
+        index, _ = capi.build_index(emb[t_lo:t_hi].contiguous(), dl_host[lo:hi], cfg.n_clusters, cfg.ex_bits,
+                                    centroids=cents)
+        del cents
     torch.cuda.synchronize()
-    log(f"[bench] index built in {time.time() - t0:.1f}s")
+    log(f"[bench] index built in {time.time() - t0:.1f}s (rank {rank}, docs {bases[rank]}..{bases[rank + 1]})")
 
     if args.impl == "reference":
         run_reference(args, cfg, index, queries, torch)
         return
 
-    B = args.batch
-    searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
+    # exact MaxSim ground truth for the recall check, before the corpus is freed
     nq_total = queries.shape[0]
-    # rank r serves queries offset by r (weak scaling: fixed batch per GPU)
+    nrec = min(args.recall_queries, nq_total)
+    gt = ground_truth(torch, emb, ptr_full, queries, cfg.k, list(range(nrec))) if (nrec > 0 and rank == 0) else None
+    del emb
+    torch.cuda.empty_cache()
+
+    B = args.batch
+    params = dict(nprobe=cfg.nprobe, k_refine=cfg.k_refine, k_full_bit=cfg.k_full_bit, num_chunks=cfg.num_chunks,
+                  k=cfg.k)
+    if world == 1:
+        searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
+        search_device = lambda qb: searcher.search_device(qb, res_buf, nres_buf)
+        search_full = searcher.search
+        res_buf = torch.empty(B, cfg.k, dtype=torch.int64, device="cuda")
+        nres_buf = torch.empty(B, dtype=torch.int32, device="cuda")
+        parallelism = "single GPU"
+    else:
+        backend = SH.CudaShardBackend(index, bases, rank, batch=B, **params)
+        pipe = SH.ShardedPipeline(backend, SH.TorchComm(), params)
+        search_device = pipe.search_device
+        search_full = pipe.search
+        parallelism = f"document shards x{world} (NCCL all_gather/all_reduce)"
+
+    # every rank serves the same query stream (strong scaling: the corpus and
+    # the queries are fixed, the documents are split across the ranks)
     def batch_at(i):
-        s = ((i + rank) * B) % nq_total
+        s = (i * B) % nq_total
         idx = torch.arange(s, s + B, device=queries.device) % nq_total
         return queries[idx].contiguous()
 
     stream = torch.cuda.current_stream()
-    res = torch.empty(B, cfg.k, dtype=torch.int64, device="cuda")
-    nres = torch.empty(B, dtype=torch.int32, device="cuda")
     batches = [batch_at(i) for i in range(args.warmup + args.steps)]
     for i in range(args.warmup):
-        searcher.search_device(batches[i], res, nres)
+        _, nres = search_device(batches[i])
     torch.cuda.synchronize()
     if nres.min().item() < 0:
         raise RuntimeError("stage-1 table overflow during warmup")
 
-    # ---- device-timed value -------------------------------------------------
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    # ---- device-timed value -------------------------------------------------
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):
-            searcher.search_device(batches[args.warmup + i], res, nres)
+            search_device(batches[args.warmup + i])
         ev1.record(stream)
         torch.cuda.nvtx.range_pop()
         barrier()
-    ms = ev0.elapsed_time(ev1)
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_per_step = ms / args.steps
-    qps = world * B * args.steps / (ms / 1e3)
-
-    # ---- per-stage profile (CUDA events between stage calls) ---------------
-    stages = profile_stages(torch, capi, index, searcher, batches[args.warmup], cfg)
+    qps = B * args.steps / (ms / 1e3)
 
     # ---- end-to-end through the public entry point, host buffers -----------
     hq = [batches[args.warmup + i].cpu().pin_memory() for i in range(args.steps)]
@@ -214,28 +247,27 @@ def main():
     e0.record(stream)
     for i in range(args.steps):
         dq.copy_(hq[i], non_blocking=True)
-        searcher.search_device(dq, res, nres)
-        hres.copy_(res, non_blocking=True)
+        r, _ = search_device(dq)
+        hres.copy_(r, non_blocking=True)
     e1.record(stream)
     barrier()
-    ems = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([ems], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = t.item()
-    e2e_qps = world * B * args.steps / (ems / 1e3)
+    ems = max_over_ranks(e0.elapsed_time(e1))
+    e2e_qps = B * args.steps / (ems / 1e3)
 
-    # ---- latency percentiles (single-query batches, as gpu_search times) ---
-    lat = latency_percentiles(torch, capi, index, cfg, queries, n=64)
+    # ---- latency percentiles (one query per call, as gpu_search times it) --
+    lat = latency_percentiles(torch, queries, search_device, barrier, n=64)
 
     # ---- recall ------------------------------------------------------------
-    nrec = min(args.recall_queries, nq_total)
     recall = None
     if nrec > 0:
-        qsel = list(range(nrec))
-        r_all, n_all = searcher.search(queries[:nrec].contiguous())
-        gt = ground_truth(torch, emb, index.doc_ptrs, queries, cfg.k, qsel)
-        recall = round(W.recall_at_k(np.stack(gt), r_all.cpu().numpy(), cfg.k), 4)
+        r_all, _ = search_full(queries[:nrec].contiguous())
+        if rank == 0:
+            recall = round(W.recall_at_k(np.stack(gt), r_all.cpu().numpy(), cfg.k), 4)
+
+    # ---- per-stage profile on this rank's (shard) index, exchange excluded --
+    prof_searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
+    stages = profile_stages(torch, capi, index, prof_searcher, batches[args.warmup], cfg)
+    del prof_searcher
 
     hbm, bf16, kind = peaks()
     # the dominant single kernel: stages that are one launch each (probe and
@@ -244,27 +276,33 @@ def main():
     achieved = dom["algo_bytes"] / (dom["ms"] / 1e3) / 1e9 if dom["bound"] == "hbm" else \
         dom["algo_flops"] / (dom["ms"] / 1e3) / 1e12
     peak = hbm if dom["bound"] == "hbm" else bf16
+    probe_launches = next(s["launches"] for s in stages if s["name"] == "probe")
+    if world == 1:
+        launches = sum(s["launches"] for s in stages) + 1  # + chm_search's status fold
+    else:
+        # prepare, probe, stage1 (4), merge, 2 x localize, refine, select, full-bit, final
+        launches = 1 + probe_launches + 4 + 1 + 2 + 1 + 1 + 1 + 1
     line = {
         "metric": "QPS at Recall@100 (C3 passage corpus)",
         "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32+u8", "data": "synthetic",
-        "config": {"workload": f"{cfg.name}: {cfg.num_docs} docs, {int(emb.shape[0])} tokens, "
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32+u8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: {cfg.num_docs} docs, {int(ptr_full[-1])} tokens, "
                                f"{cfg.n_clusters} clusters, ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, "
                                f"k_refine {cfg.k_refine}, k_full_bit {cfg.k_full_bit}, k {cfg.k}",
                    "batch_queries": B, "l2": "inputs larger than L2 (index >> 126 MB)",
                    "recall@100": recall, "recall_queries": nrec,
-                   "latency_ms_single_query": lat, "parallelism": f"replica x{world}"},
+                   "latency_ms_single_query": lat, "parallelism": parallelism,
+                   "stages_scope": "rank 0 index" + (" shard, exchange excluded" if world > 1 else "")},
         "e2e": {"value": round(e2e_qps, 2), "unit": "queries/s",
-                "h2d_bytes_per_step": int(B * 32 * cfg.dim * 4), "d2h_bytes_per_step": int(B * cfg.k * 8)},
+                "h2d_bytes_per_step": int(world * B * 32 * cfg.dim * 4), "d2h_bytes_per_step": int(world * B * cfg.k * 8)},
         "roofline": {"kernel": dom["name"], "bound": dom["bound"], "achieved": round(achieved, 2),
                      "peak": peak, "unit": "GB/s" if dom["bound"] == "hbm" else "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": kind},
         "stages_ms_per_step": {s["name"]: round(s["ms"], 3) for s in stages},
         "stages_algo_gbs": {s["name"]: round(s["algo_bytes"] / (s["ms"] / 1e3) / 1e9, 1)
                             for s in stages if s["algo_bytes"]},
-        # stage kernels plus chm_search's per-batch status fold
-        "gpu_launches": int((sum(s["launches"] for s in stages) + 1) * args.steps),
+        "gpu_launches": int(launches * args.steps),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -375,16 +413,15 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
     return out
 
 
-def latency_percentiles(torch, capi, index, cfg, queries, n=64):
-    s1 = capi.Searcher(index, k=cfg.k, batch=1, **cfg.search_kwargs())
-    res = torch.empty(1, cfg.k, dtype=torch.int64, device="cuda")
-    nres = torch.empty(1, dtype=torch.int32, device="cuda")
+def latency_percentiles(torch, queries, search_device, barrier, n=64):
+    """Wall-clock latency of one query per call (as gpu_search times it),
+    synchronised on every rank."""
     lat = []
     for i in range(n + 3):
         q = queries[i % queries.shape[0]:i % queries.shape[0] + 1].contiguous()
-        torch.cuda.synchronize()
+        barrier()
         t = time.perf_counter()
-        s1.search_device(q, res, nres)
+        search_device(q)
         torch.cuda.synchronize()
         if i >= 3:
             lat.append((time.perf_counter() - t) * 1e3)
