@@ -45,6 +45,8 @@ struct SearchBuffers {
     size_t probe_bytes;
     void* s1_ws;
     size_t s1_bytes;
+    void* rt_ws;
+    size_t rt_bytes;
     int32_t* refined_docs;
     float* refined_partial;
     float* onebit;
@@ -68,6 +70,7 @@ static void layout(A& a, const chm_index* idx, const chm_search_params* p, Searc
                                    ? chm_probe_tc_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe)
                                    : chm_probe_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe);
     const size_t s1_bytes = stage1_bytes(idx, p->batch, p->nprobe, p->table_log2_extra);
+    const size_t rt_bytes = 0;
     auto rot = a.template take<float>(ntok * kDim);
     auto cb1 = a.template take<float>(ntok);
     auto cbex = a.template take<float>(ntok);
@@ -75,6 +78,7 @@ static void layout(A& a, const chm_index* idx, const chm_search_params* p, Searc
     auto labels = a.template take<uint32_t>(ntok * p->nprobe);
     auto pws = a.template take<char>(probe_bytes);
     auto sws = a.template take<char>(s1_bytes);
+    auto rtws = a.template take<char>(rt_bytes);
     auto rd = a.template take<int32_t>(B * p->k_refine);
     auto rp = a.template take<float>(B * p->k_refine);
     auto ob = a.template take<float>(B * p->k_refine);
@@ -85,7 +89,8 @@ static void layout(A& a, const chm_index* idx, const chm_search_params* p, Searc
     auto fl = a.template take<uint32_t>(B);
     if (b) {
         *b = SearchBuffers{(float*)rot, (float*)cb1, (float*)cbex, (float*)lut, (uint32_t*)labels,
-                           (void*)pws, probe_bytes, (void*)sws, s1_bytes, (int32_t*)rd, (float*)rp,
+                           (void*)pws, probe_bytes, (void*)sws, s1_bytes, (void*)rtws, rt_bytes,
+                           (int32_t*)rd, (float*)rp,
                            (float*)ob, (int32_t*)nr, (int32_t*)fd, (float*)fs, (int32_t*)nf,
                            (uint32_t*)fl};
     }

@@ -13,25 +13,37 @@ constexpr int kRefineWarps = 8;
 // Replaces gather_refined_doc_lengths/positions, one_bit_token_score and
 // one_bit_document_score (kernels.cu:430-617) without materialising the
 // [32 x tokens] score matrix.
+// Modes (for the tensor-core refinement in refine_tc.cu):
+//   kRefineAll     every refined doc;
+//   kRefineFlagged every refined doc of the queries whose `status` is set
+//                  (a tensor-core launch gave up on a bounded wait);
+//   kRefineListed  the refined-list positions in `list` [nq][k_refine]
+//                  (list_count [nq]): the docs longer than one tile.
+enum RefineMode { kRefineAll = 0, kRefineFlagged = 1, kRefineListed = 2 };
+
+template <int kMode>
 __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
     const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
     const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
     const float* __restrict__ lut, const float* __restrict__ cb1,
     const int32_t* __restrict__ refined_docs, const int32_t* __restrict__ num_refined, int k_refine,
-    float* __restrict__ scores) {
+    float* __restrict__ scores, const uint32_t* __restrict__ status, const int32_t* __restrict__ list,
+    const int32_t* __restrict__ list_count) {
     extern __shared__ float s_lut[];  // [32][512]
     __shared__ float s_cb1[kQ];
     const int q = blockIdx.y;
+    if (kMode == kRefineFlagged && status[q] == 0u) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int R = num_refined[q];
+    const int R = kMode == kRefineListed ? list_count[q] : num_refined[q];
     if ((int)blockIdx.x * kRefineWarps >= R) return;
     const float4* src = reinterpret_cast<const float4*>(lut + (size_t)q * kQ * kLutPerQ);
     for (int i = threadIdx.x; i < kQ * kLutPerQ / 4; i += blockDim.x)
         reinterpret_cast<float4*>(s_lut)[i] = src[i];
     if (threadIdx.x < kQ) s_cb1[threadIdx.x] = cb1[q * kQ + threadIdx.x];
     __syncthreads();
-    const int r = blockIdx.x * kRefineWarps + warp;
-    if (r >= R) return;
+    const int i = blockIdx.x * kRefineWarps + warp;
+    if (i >= R) return;
+    const int r = kMode == kRefineListed ? list[(size_t)q * k_refine + i] : i;
     const int64_t doc = refined_docs[(size_t)q * k_refine + r];
     if (doc < 0) {  // a slot another document shard owns
         if (lane == 0) scores[(size_t)q * k_refine + r] = -INFINITY;
@@ -349,12 +361,32 @@ extern "C" chm_status chm_refine_1bit(const chm_index* idx, int32_t nq, const fl
                                       void* stream) {
     if (nq <= 0) return CHM_OK;
     const size_t smem = sizeof(float) * chm::kQ * chm::kLutPerQ;
-    CHM_TRY(chm::set_smem(chm::refine_1bit_kernel, smem));
+    CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineAll>, smem));
     dim3 g((k_refine + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
-    chm::refine_1bit_kernel<<<g, chm::kRefineWarps * 32, smem, (cudaStream_t)stream>>>(
+    chm::refine_1bit_kernel<chm::kRefineAll><<<g, chm::kRefineWarps * 32, smem, (cudaStream_t)stream>>>(
         idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
-        k_refine, scores);
+        k_refine, scores, nullptr, nullptr, nullptr);
     return chm::launch_status("refine_1bit_kernel");
+}
+
+// SIMT passes that complete the tensor-core refinement: the listed long docs,
+// then every doc of the queries whose tensor-core launch reported a failure.
+chm_status chm_refine_1bit_complete(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
+                                    const int32_t* refined_docs, const int32_t* num_refined, int32_t k_refine,
+                                    float* scores, const int32_t* list, const int32_t* list_count,
+                                    const uint32_t* status, cudaStream_t st) {
+    const size_t smem = sizeof(float) * chm::kQ * chm::kLutPerQ;
+    dim3 g((k_refine + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
+    CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineListed>, smem));
+    chm::refine_1bit_kernel<chm::kRefineListed><<<g, chm::kRefineWarps * 32, smem, st>>>(
+        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
+        k_refine, scores, nullptr, list, list_count);
+    CHM_TRY(chm::launch_status("refine_1bit_listed"));
+    CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineFlagged>, smem));
+    chm::refine_1bit_kernel<chm::kRefineFlagged><<<g, chm::kRefineWarps * 32, smem, st>>>(
+        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
+        k_refine, scores, status, nullptr, nullptr);
+    return chm::launch_status("refine_1bit_flagged");
 }
 
 extern "C" chm_status chm_select_fullbit(int32_t nq, const int32_t* refined_docs,

@@ -1,0 +1,512 @@
+// 1-bit refinement with a tensor-core filter (same results as
+// refine_1bit_kernel, bit for bit).
+//
+// The 1-bit document score (one_bit_token_score + one_bit_document_score,
+// kernels.cu:430-575) is, per query token t, the max over the document's
+// tokens of dist = (ip - cb1[t]) * factor with ip the LUT sum in the
+// reference order, then the reference's tree over t.  Only the max matters,
+// so most (token, t) pairs never need their exact LUT sum:
+//
+//  1. int8 tensor-core pass (tcgen05.mma.kind::i8, M=128 tokens, N=64, K=128):
+//     A = the tokens' code bits as 0/1 bytes, B = the query token in 16-bit
+//     fixed point as two int8 limbs (q ~ (256*hi + lo) / 2^14).  The int32
+//     accumulators are exact, so ip_a = (256*acc_hi + acc_lo) / 2^14 differs
+//     from the real inner product by at most E_t = sum_d |q_d - qfix_d/2^14|.
+//  2. With the LUT sum's own rounding (34 fp32 adds, each within 2^-24 of
+//     sum |q_d|) and the roundings of the two dist operations, every token's
+//     exact dist lies in [lo, hi] = dist_a -/+ margin (directed rounding).
+//     A token can hold the max for (doc, t) only if hi >= max over the doc's
+//     tokens of lo; the true max token always passes.
+//  3. Candidates get the exact LUT sum and dist (the same fp32 operations as
+//     refine_1bit_kernel); their max is the exact max.
+//
+// Work items: the refined docs of a query packed greedily into groups of at
+// most 128 tokens and 32 docs (one M tile); docs longer than 128 tokens go to
+// a list that the SIMT kernel scores.  One CTA (4 warps) loops over items with
+// a two-deep pipeline: while item k's accumulators are read out and its docs
+// reduced (warp per doc, lane per query token), item k+1's codes are gathered,
+// expanded and multiplied.
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace chm {
+
+constexpr int kRtThreads = 128;
+constexpr int kRtRows = 128;         // tokens per tile (MMA M)
+constexpr int kRtN = 64;             // 32 query tokens x {hi, lo} limbs
+constexpr int kRtMaxDocs = 32;       // docs per packed item
+constexpr int kRtTmemCols = 128;  // two pipeline buffers of 64 columns
+constexpr float kFix = 16384.0f;     // fixed-point scale of the query limbs
+// idesc kind::i8: D s32 (bits 4-5 = 2), A s8 (bits 7-9 = 1), B s8 (bits 10-12 = 1), K-major
+constexpr uint32_t kRtIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kRtN >> 3) << 17) |
+                              ((uint32_t)(kRtRows >> 4) << 24);
+
+constexpr int kRtMaxCand = 1024;     // candidates per tile (more: the query is rescored by the SIMT kernel)
+
+struct __align__(1024) RtSmem {
+    uint8_t a[2][kRtRows * 128];     // token bits, K-major SW128 (two pipeline buffers)
+    uint8_t b[kRtN * 128];           // query limbs, K-major SW128
+    float da[kRtRows][33];           // estimated dist per (row, query token)
+    float qv[32][129];               // rotated query tokens (exact LUT entries are rebuilt from them)
+    uint4 code[2][kRtRows];
+    float fac[2][kRtRows];
+    int row_doc[2][kRtRows];         // item-local doc of each row
+    int doc_tok0[2][kRtMaxDocs + 1]; // row offsets of the item's docs
+    int64_t doc_first[2][kRtMaxDocs];// first token id of each doc
+    int doc_id[2][kRtMaxDocs];
+    int r0[2], nd[2], ntok[2];
+    uint32_t mx[kRtMaxDocs][32];     // max estimate per (doc, query token), ordered keys
+    uint32_t maxf[kRtMaxDocs];       // max |factor| per doc (float bits, >= 0)
+    uint32_t exact[kRtMaxDocs][32];  // exact max per (doc, query token), ordered keys
+    uint32_t cand[kRtMaxCand];       // (row << 5 | t)
+    int n_cand;
+    float em[32];                    // margin per unit |factor|
+    float cb1[32];
+    uint64_t bar[2];
+    uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// byte offset of (row, k) in a K-major SW128 tile with 128-byte rows
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk16) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
+// 4 bits -> 4 bytes of 0/1
+__device__ __forceinline__ uint32_t nib_bytes(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
+
+// The LUT sum of lut_ip (kernels.cu:363-373) with each LUT entry rebuilt
+// from the query as precompute_one_bit_lut_kernel builds it (kernels.cu:
+// 402-428: 0.0f plus the set bits' components in ascending order), so the
+// value is the same float.  q: one query token's 128 components.
+__device__ __forceinline__ float lut_ip_from_query(const float* q, uint4 code) {
+    float ip = 0.0f;
+    const uint32_t w[4] = {code.x, code.y, code.z, code.w};
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) {
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+            const uint32_t e = (w[qq] >> (n * 4)) & 0xF;
+            const float* qc = q + (qq * 8 + n) * 4;
+            float entry = 0.0f;
+            if (e & 1u) entry = fadd(entry, qc[0]);
+            if (e & 2u) entry = fadd(entry, qc[1]);
+            if (e & 4u) entry = fadd(entry, qc[2]);
+            if (e & 8u) entry = fadd(entry, qc[3]);
+            ip = fadd(ip, entry);
+        }
+    }
+    return ip;
+}
+
+// Greedy packing of each query's refined docs into items (r0, r1); docs
+// longer than one tile are listed for the SIMT kernel.
+__global__ void refine_plan_kernel(const int64_t* __restrict__ doc_ptrs, const int32_t* __restrict__ refined_docs,
+                                   const int32_t* __restrict__ num_refined, int k_refine,
+                                   int2* __restrict__ items, int32_t* __restrict__ n_items,
+                                   int32_t* __restrict__ big, int32_t* __restrict__ n_big) {
+    extern __shared__ int s_len[];
+    const int q = blockIdx.x;
+    const int R = num_refined[q];
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int64_t d = refined_docs[(size_t)q * k_refine + r];
+        s_len[r] = d < 0 ? 0 : (int)(doc_ptrs[d + 1] - doc_ptrs[d]);
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    int n = 0, nb = 0, r = 0;
+    int2* out = items + (size_t)q * k_refine;
+    int32_t* bl = big + (size_t)q * k_refine;
+    while (r < R) {
+        if (s_len[r] > kRtRows) {
+            bl[nb++] = r++;
+            continue;
+        }
+        const int start = r;
+        int tok = 0;
+        while (r < R && r - start < kRtMaxDocs && s_len[r] <= kRtRows && tok + s_len[r] <= kRtRows) {
+            tok += s_len[r];
+            ++r;
+        }
+        out[n++] = make_int2(start, r);
+    }
+    n_items[q] = n;
+    n_big[q] = nb;
+}
+
+// Stage of one item into pipeline buffer `buf`: doc offsets, the rows' codes
+// and factors, the expanded bits, and the MMA into TMEM columns [64 buf, +64).
+__device__ __forceinline__ void rt_stage(RtSmem& s, int buf, int item, int q, int k_refine,
+                                         const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
+                                         const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
+                                         const int32_t* __restrict__ refined_docs, const int2* __restrict__ items,
+                                         uint32_t tmem) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == 0) {
+        const int2 rr = items[(size_t)q * k_refine + item];
+        const int ndw = rr.y - rr.x;
+        int64_t first = 0;
+        int len = 0, d = -1;
+        if (lane < ndw) {
+            d = refined_docs[(size_t)q * k_refine + rr.x + lane];
+            if (d >= 0) {
+                first = doc_ptrs[d];
+                len = (int)(doc_ptrs[d + 1] - first);
+            }
+        }
+        int incl = len;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += y;
+        }
+        if (lane < ndw) {
+            s.doc_first[buf][lane] = first;
+            s.doc_tok0[buf][lane + 1] = incl;
+            s.doc_id[buf][lane] = d;
+        }
+        const int tot = __shfl_sync(0xffffffffu, incl, ndw - 1);
+        if (lane == 0) {
+            s.doc_tok0[buf][0] = 0;
+            s.r0[buf] = rr.x;
+            s.nd[buf] = ndw;
+            s.ntok[buf] = tot;
+        }
+    }
+    __syncthreads();
+    const int T = s.ntok[buf];
+    uint4 code = make_uint4(0, 0, 0, 0);
+    float f = 0.0f;
+    int ld = -1;
+    if (tid < T) {
+        ld = 0;
+        while (s.doc_tok0[buf][ld + 1] <= tid) ++ld;
+        const int64_t token = s.doc_first[buf][ld] + (tid - s.doc_tok0[buf][ld]);
+        const uint32_t pos = __ldg(tok2pos + token);
+        code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
+        f = __ldg(factor1 + pos);
+    }
+    s.code[buf][tid] = code;
+    s.fac[buf][tid] = f;
+    s.row_doc[buf][tid] = ld;
+    const uint32_t wv[4] = {code.x, code.y, code.z, code.w};
+    uint8_t* a = s.a[buf];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint32_t h = wv[c >> 1] >> ((c & 1) * 16);
+        *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) =
+            make_uint4(nib_bytes(h & 0xF), nib_bytes((h >> 4) & 0xF), nib_bytes((h >> 8) & 0xF),
+                       nib_bytes((h >> 12) & 0xF));
+    }
+    fence_proxy_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        sm100::tc_fence_after();
+        const uint32_t a_base = sm100::smem_addr(a), b_base = sm100::smem_addr(s.b);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+            mma_i8(tmem + buf * kRtN, sm100::smem_desc_sw128(a_base + kk * 32), sm100::smem_desc_sw128(b_base + kk * 32),
+                   kRtIdesc, kk > 0 ? 1u : 0u);
+        sm100::mma_commit(&s.bar[buf]);
+    }
+}
+
+__global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
+    const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos, const uint8_t* __restrict__ codes1,
+    const float* __restrict__ factor1, const float* __restrict__ lut, const float* __restrict__ cb1,
+    const float* __restrict__ rot, const int32_t* __restrict__ refined_docs, int k_refine,
+    const int2* __restrict__ items, const int32_t* __restrict__ n_items, float* __restrict__ scores,
+    uint32_t* __restrict__ status, unsigned long long* __restrict__ stats) {
+    extern __shared__ uint8_t smem_raw[];
+    RtSmem& s = *reinterpret_cast<RtSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q = blockIdx.y;
+    const int NI = n_items[q];
+    if ((int)blockIdx.x >= NI) return;
+    const float* qlut = lut + (size_t)q * kQ * kLutPerQ;
+
+    // ---- prologue: query limbs (B operand), margins, TMEM, barriers --------
+    {
+        // thread tid writes row n = tid >> 1 (limb n >> 5 of token n & 31), half (tid & 1) of K
+        const int n = tid >> 1, half = tid & 1;
+        const int t = n & 31;
+        const bool lo_limb = n >= 32;
+        const float* qv = rot + ((size_t)q * kQ + t) * kDim;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int chunk = half * 4 + c;
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int d = chunk * 16 + j * 4 + b;
+                    int fx = __float2int_rn(qv[d] * kFix);
+                    fx = max(-16384, min(16384, fx));
+                    const int lo = ((fx + 128) & 255) - 128;
+                    const int hi = (fx - lo) >> 8;
+                    word |= (uint32_t)(uint8_t)(int8_t)(lo_limb ? lo : hi) << (8 * b);
+                }
+                w[j] = word;
+            }
+            *reinterpret_cast<uint4*>(s.b + sw128_off(n, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if (tid < 32) {
+            const float* qt = rot + ((size_t)q * kQ + tid) * kDim;
+            double e = 0.0, s1 = 0.0;
+            for (int d = 0; d < kDim; ++d) {
+                const float v = qt[d];
+                int fx = __float2int_rn(v * kFix);
+                fx = max(-16384, min(16384, fx));
+                e += fabs((double)v - (double)fx / 16384.0);
+                s1 += fabs((double)v);
+            }
+            const float c = cb1[q * kQ + tid];
+            s.cb1[tid] = c;
+            // quantisation + LUT-sum rounding (34 adds) + the two dist roundings of both paths
+            const double m = e + 40.0 * 0x1p-24 * s1 + 0x1p-21 * (s1 + fabs((double)c));
+            s.em[tid] = __double2float_ru(m * (1.0 + 0x1p-20));
+        }
+        for (int i = tid; i < 32 * kDim; i += kRtThreads) s.qv[i >> 7][i & 127] = rot[(size_t)q * kQ * kDim + i];
+        for (int i = tid; i < kRtMaxDocs * 32; i += kRtThreads) {
+            (&s.mx[0][0])[i] = 0u;
+            (&s.exact[0][0])[i] = float_key_asc(-FLT_MAX);
+        }
+        if (tid < kRtMaxDocs) s.maxf[tid] = 0u;
+        if (tid == 0) {
+            s.n_cand = 0;
+            sm100::mbar_init(&s.bar[0], 1);
+            sm100::mbar_init(&s.bar[1], 1);
+            sm100::fence_mbar_init();
+        }
+        if (warp == 0) {
+            sm100::tmem_alloc(&s.tmem_base, kRtTmemCols);
+            sm100::tmem_relinquish();
+        }
+        fence_proxy_async_smem();
+        sm100::tc_fence_before();
+        __syncthreads();
+        sm100::tc_fence_after();
+    }
+    const uint32_t tmem = s.tmem_base;
+    const float inv_fix = 1.0f / kFix;
+    bool failed = false;  // uniform across the CTA (set from __syncthreads_or)
+    unsigned long long n_rows = 0, n_cand = 0;
+
+    rt_stage(s, 0, blockIdx.x, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items, tmem);
+    int k = 0;
+    bool next_issued = false;  // an MMA of item k+1 is in flight
+    for (int it = blockIdx.x; it < NI; it += gridDim.x, ++k) {
+        const int buf = k & 1;
+        const int nxt = it + gridDim.x;
+        next_issued = nxt < NI;
+        if (next_issued)  // overlaps this item's MMA and epilogue
+            rt_stage(s, buf ^ 1, nxt, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items, tmem);
+        bool ok = true;
+        if (tid == 0) ok = sm100::mbar_wait(&s.bar[buf], (uint32_t)((k >> 1) & 1));
+        if (__syncthreads_or(!ok)) {
+            failed = true;
+            break;
+        }
+        sm100::tc_fence_after();
+        // ---- accumulators -> estimated dists, one row per thread
+        uint32_t hi[32], lo[32];
+        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + buf * kRtN;
+        sm100::tmem_ld32_async(taddr, hi);
+        sm100::tmem_ld32_async(taddr + 32, lo);
+        sm100::tmem_wait_ld();
+        sm100::tc_fence_before();
+        const int T = s.ntok[buf];
+        if (tid < T) {
+            const float f = s.fac[buf][tid];
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+                const float ipa = (float)((int)hi[t] * 256 + (int)lo[t]) * inv_fix;
+                s.da[tid][t] = __fmul_rn(__fsub_rn(ipa, s.cb1[t]), f);
+            }
+        }
+        __syncthreads();
+        // ---- pass 1: warp w scans its 32 rows, lane = query token; per-doc
+        // max of the estimates and of |factor| (docs are runs of rows)
+        const int w0 = warp * 32;
+        const int nrow = max(0, min(32, T - w0));
+        {
+            int cur = -1;
+            float run = -INFINITY, runf = 0.0f;
+#pragma unroll 8
+            for (int i = 0; i < nrow; ++i) {
+                const int row = w0 + i;
+                const int ld = s.row_doc[buf][row];
+                const float v = s.da[row][lane];
+                const float fa = fabsf(s.fac[buf][row]);
+                if (ld != cur) {
+                    if (cur >= 0) {
+                        atomicMax(&s.mx[cur][lane], float_key_asc(run));
+                        if (lane == 0) atomicMax(&s.maxf[cur], __float_as_uint(runf));
+                    }
+                    cur = ld;
+                    run = -INFINITY;
+                    runf = 0.0f;
+                }
+                run = fmaxf(run, v);
+                runf = fmaxf(runf, fa);
+            }
+            if (cur >= 0) {
+                atomicMax(&s.mx[cur][lane], float_key_asc(run));
+                if (lane == 0) atomicMax(&s.maxf[cur], __float_as_uint(runf));
+            }
+        }
+        __syncthreads();
+        // ---- pass 2: candidates.  Every row's exact dist is within M =
+        // max|f| * em of its estimate, so the max row's estimate is at least
+        // (max estimate) - 2M.
+        {
+            const float em = s.em[lane];
+            int cur = -1;
+            float thr = 0.0f;
+            for (int i = 0; i < nrow; ++i) {
+                const int row = w0 + i;
+                const int ld = s.row_doc[buf][row];
+                if (ld != cur) {
+                    cur = ld;
+                    const float M = __fmul_ru(__uint_as_float(s.maxf[ld]), em);
+                    thr = __fsub_rd(key_to_float_asc(s.mx[ld][lane]), __fadd_ru(M, M));
+                }
+                const bool c = s.da[row][lane] >= thr;
+                const uint32_t mask = __ballot_sync(0xffffffffu, c);
+                if (mask) {
+                    int base = 0;
+                    if (lane == __ffs(mask) - 1) base = atomicAdd(&s.n_cand, __popc(mask));
+                    base = __shfl_sync(0xffffffffu, base, __ffs(mask) - 1);
+                    const int at = base + __popc(mask & ((1u << lane) - 1));
+                    if (c && at < kRtMaxCand) s.cand[at] = ((uint32_t)row << 5) | (uint32_t)lane;
+                }
+            }
+        }
+        __syncthreads();
+        // ---- exact LUT sums of the candidates, all threads
+        const int nc = s.n_cand;
+        if (nc > kRtMaxCand) {
+            if (tid == 0) atomicOr(status + q, 1u);  // rescored by the SIMT kernel
+        } else {
+            for (int c = tid; c < nc; c += kRtThreads) {
+                const uint32_t e = s.cand[c];
+                const int row = (int)(e >> 5), t = (int)(e & 31);
+                const float ip = lut_ip_from_query(s.qv[t], s.code[buf][row]);
+                const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[buf][row]);
+                atomicMax(&s.exact[s.row_doc[buf][row]][t], float_key_asc(dist));
+            }
+        }
+        n_cand += (unsigned long long)(tid == 0 ? nc : 0);
+        __syncthreads();
+        // ---- document scores: the reference's 128-thread tree (kernels.cu:557-570)
+        const int nd = s.nd[buf];
+        for (int j = warp; j < nd; j += kRtThreads / 32) {
+            const float m = key_to_float_asc(s.exact[j][lane]);
+            float x = fadd(fadd(fadd(0.0f, m), 0.0f), 0.0f);
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+            if (lane == 0) scores[(size_t)q * k_refine + s.r0[buf] + j] = s.doc_id[buf][j] < 0 ? -INFINITY : x;
+            s.mx[j][lane] = 0u;
+            s.exact[j][lane] = float_key_asc(-FLT_MAX);
+            if (lane == 0) s.maxf[j] = 0u;
+        }
+        if (tid == 0) s.n_cand = 0;
+        if (tid == 0) n_rows += (unsigned long long)T;
+        __syncthreads();
+    }
+    if (failed && tid == 0) {
+        // the MMAs of item k (whose wait ran out) and of item k+1 may still be
+        // in flight: wait for them again, bounded, before TMEM is released
+        sm100::mbar_wait(&s.bar[k & 1], (uint32_t)((k >> 1) & 1));
+        if (next_issued) sm100::mbar_wait(&s.bar[(k + 1) & 1], (uint32_t)(((k + 1) >> 1) & 1));
+        atomicOr(status + q, 1u);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) n_cand += __shfl_xor_sync(0xffffffffu, n_cand, off);
+    if (lane == 0 && n_cand) atomicAdd(stats + 1, n_cand);
+    if (tid == 0 && n_rows) atomicAdd(stats, n_rows);
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 0) sm100::tmem_dealloc(tmem, kRtTmemCols);
+}
+
+// Queries whose tensor-core launch gave up on a bounded wait are scored
+// again by the SIMT kernel (status bit set); others return at once.
+__global__ void refine_status_clear_kernel(uint32_t* status, int nq, unsigned long long* stats) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < nq) status[i] = 0;
+    if (i < 2) stats[i] = 0;
+}
+
+}  // namespace chm
+
+namespace chm {
+size_t refine_tc_smem_bytes() { return sizeof(RtSmem) + 1024; }
+}
+
+extern "C" size_t chm_refine_1bit_tc_workspace_bytes(int32_t nq, int32_t k_refine) {
+    chm::Sizer s;
+    s.take<int2>((size_t)nq * k_refine);
+    s.take<int32_t>((size_t)nq);
+    s.take<uint32_t>((size_t)nq);
+    s.take<unsigned long long>(2);  // rows scored by the tensor-core pass, exact candidates (last call)
+    s.take<int32_t>((size_t)nq * k_refine);
+    s.take<int32_t>((size_t)nq);
+    return s.off;
+}
+
+chm_status chm_refine_1bit_complete(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
+                                    const int32_t* refined_docs, const int32_t* num_refined, int32_t k_refine,
+                                    float* scores, const int32_t* list, const int32_t* list_count,
+                                    const uint32_t* status, cudaStream_t st);
+
+extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
+                                         const float* rot, const int32_t* refined_docs, const int32_t* num_refined,
+                                         int32_t k_refine, float* scores, void* ws, size_t ws_bytes, void* stream) {
+    if (nq <= 0) return CHM_OK;
+    if (!idx || k_refine <= 0 || k_refine > CHM_MAX_K_REFINE) return CHM_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    chm::Arena a(ws, ws_bytes);
+    int2* items = a.take<int2>((size_t)nq * k_refine);
+    int32_t* n_items = a.take<int32_t>((size_t)nq);
+    uint32_t* status = a.take<uint32_t>((size_t)nq);
+    unsigned long long* stats = a.take<unsigned long long>(2);
+    int32_t* big = a.take<int32_t>((size_t)nq * k_refine);
+    int32_t* n_big = a.take<int32_t>((size_t)nq);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    chm::refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(status, nq, stats);
+    CHM_TRY(chm::launch_status("refine_status_clear_kernel"));
+    const size_t plan_smem = sizeof(int) * (size_t)k_refine;
+    CHM_CUDA(cudaFuncSetAttribute(chm::refine_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)plan_smem));
+    chm::refine_plan_kernel<<<nq, 256, plan_smem, st>>>(idx->doc_ptrs, refined_docs, num_refined, k_refine, items,
+                                                        n_items, big, n_big);
+    CHM_TRY(chm::launch_status("refine_plan_kernel"));
+    const size_t smem = chm::refine_tc_smem_bytes();
+    CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int gx = (4 * 148 * 2 + nq - 1) / nq;
+    gx = std::max(1, std::min(gx, k_refine));
+    chm::refine_tc_kernel<<<dim3((unsigned)gx, (unsigned)nq), chm::kRtThreads, smem, st>>>(
+        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, rot, refined_docs, k_refine, items,
+        n_items, scores, status, stats);
+    CHM_TRY(chm::launch_status("refine_tc_kernel"));
+    return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, big, n_big,
+                                    status, st);
+}

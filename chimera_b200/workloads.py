@@ -66,6 +66,8 @@ CONFIGS = {
     "mini": Config("mini", 300, ("normal", 64, 20, 8, 180), 64, 6, 128, 4, 16, 60, 20, 5, 10),
     "small": Config("small", 2000, ("normal", 64, 20, 8, 180), 256, 16, 512, 4, 24, 300, 60,
                     5, 20),
+    # long documents (several 128-token tiles each), ex_bits 2
+    "long": Config("long", 300, ("lognormal", 200, 0.6, 100, 600), 64, 6, 256, 2, 16, 120, 30, 5, 10),
 }
 
 

@@ -181,6 +181,21 @@ chm_status chm_refine_1bit(const chm_index* index, int32_t nq, const float* lut,
                            const int32_t* num_refined, int32_t k_refine, float* scores,
                            void* stream);
 
+/* chm_refine_1bit with an int8 tensor-core filter: tcgen05.mma.kind::i8 of
+ * the code bits against the query in 16-bit fixed point gives each (token,
+ * query token) an estimate with a proven error bound; only tokens that can
+ * hold a document's maximum get the exact LUT sum (about 1.01 per document
+ * and query token).  Same scores as chm_refine_1bit, bit for bit.  Measured
+ * slower than chm_refine_1bit on B200 at the C3 workload (the per-pair bound
+ * bookkeeping costs as many instructions as the LUT sums it avoids), so
+ * chm_search uses chm_refine_1bit.  rot [nq*32*128] rotated queries;
+ * workspace from chm_refine_1bit_tc_workspace_bytes. */
+size_t chm_refine_1bit_tc_workspace_bytes(int32_t nq, int32_t k_refine);
+chm_status chm_refine_1bit_tc(const chm_index* index, int32_t nq, const float* lut,
+                              const float* cb1, const float* rot, const int32_t* refined_docs,
+                              const int32_t* num_refined, int32_t k_refine, float* scores,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Progressive chunked selection of the docs to full-bit score
  * (search_impl.cu:341-494).  fb_docs [nq * fb_cap], num_fb [nq]. */
 chm_status chm_select_fullbit(int32_t nq, const int32_t* refined_docs, const float* onebit,
