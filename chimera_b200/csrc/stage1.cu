@@ -206,9 +206,8 @@ __global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
     const uint64_t* __restrict__ tables, int log2h, uint64_t* __restrict__ keys, int64_t key_cap,
     uint32_t* __restrict__ n_pos, uint32_t* __restrict__ flags) {
     __shared__ uint64_t s_ent[kCombineWarps][kBinCap];
-    __shared__ uint64_t s_out[kCombineWarps][kBinCap];
+    __shared__ uint64_t s_out[kCombineWarps][2 * kBinCap];
     __shared__ float s_scr[kCombineWarps][32];
-    __shared__ uint32_t s_cnt[kCombineWarps + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // queries vary fastest across the grid so that concurrently running blocks
     // spread their output-counter atomics over many queries
@@ -216,13 +215,24 @@ __global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
     const uint32_t hmask = (1u << log2h) - 1;
     const uint32_t nbins = 1u << (log2h - kBinShift);
     const uint32_t nbins_mask = nbins - 1;
-    // nbins is a multiple of kCombineWarps; grid.y is capped, so blocks stride over bin groups
-    for (uint32_t grp0 = blockIdx.y; grp0 < nbins / kCombineWarps; grp0 += gridDim.y) {
-        const uint32_t bin = grp0 * kCombineWarps + warp;
-        const uint64_t* table = tables + ((size_t)q << log2h);
+    const uint64_t* table = tables + ((size_t)q << log2h);
+    uint64_t* out = keys + (size_t)q * key_cap;
+    uint64_t* ent = s_ent[warp];
+    int n_buf = 0;  // keys buffered in s_out[warp] over several bins, one counter atomic per flush
+    auto flush = [&]() {
+        uint32_t at = 0;
+        if (lane == 0) at = atomicAdd(n_pos + q, (uint32_t)n_buf);
+        at = __shfl_sync(0xffffffffu, at, 0);
+        for (int j = lane; j < n_buf; j += 32) {
+            if ((int64_t)at + j < key_cap) out[at + j] = s_out[warp][j];
+            else atomicOr(flags + q, 4u);
+        }
+        n_buf = 0;
+        __syncwarp();
+    };
+    // each warp walks bins with a stride of all the query's warps; no block barriers
+    for (uint32_t bin = blockIdx.y * kCombineWarps + warp; bin < nbins; bin += gridDim.y * kCombineWarps) {
         const uint32_t first = bin << kBinShift;
-        uint64_t* ent = s_ent[warp];
-        uint64_t* outb = s_out[warp];
         // 1) stage the bin's own entries
         int n = 0;
         for (uint32_t base = 0; base <= hmask; base += 32) {
@@ -243,6 +253,8 @@ __global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
             n = kBinCap;
         }
         __syncwarp();
+        if (n_buf > kBinCap) flush();  // room for this bin's (at most kBinCap) keys
+        uint64_t* outb = s_out[warp] + n_buf;
         int n_out = 0;
         if (n <= 32) {
             const bool act = lane < n;
@@ -285,27 +297,10 @@ __global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
                 ++n_out;
             }
         }
-        // one output-counter atomic per block
-        if (lane == 0) s_cnt[warp] = (uint32_t)n_out;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            uint32_t tot = 0;
-            for (int w = 0; w < kCombineWarps; ++w) {
-                const uint32_t c = s_cnt[w];
-                s_cnt[w] = tot;
-                tot += c;
-            }
-            s_cnt[kCombineWarps] = tot ? atomicAdd(n_pos + q, tot) : 0u;
-        }
-        __syncthreads();
-        const uint32_t at = s_cnt[kCombineWarps] + s_cnt[warp];
-        uint64_t* out = keys + (size_t)q * key_cap;
-        for (int j = lane; j < n_out; j += 32) {
-            if ((int64_t)at + j < key_cap) out[at + j] = outb[j];
-            else atomicOr(flags + q, 4u);
-        }
-        __syncthreads();  // s_cnt and the staging buffers are reused by the next group
+        n_buf += n_out;
+        __syncwarp();  // the staging buffer is reused by the next bin
     }
+    if (n_buf) flush();
 }
 
 // ---- block helpers for the select kernel ---------------------------------
@@ -572,7 +567,9 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     stage1_score_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits);
     CHM_TRY(launch_status("stage1_score_kernel"));
     const int64_t nbins = 1ll << (l - kBinShift);
-    dim3 g2(nq, (unsigned)std::min<int64_t>(nbins / kCombineWarps, 65535));
+    // enough blocks for about 8 resident per SM over all queries; warps stride over bins
+    const int64_t want_blocks = std::max<int64_t>(1, (int64_t)148 * 8 * 4 / std::max(1, nq));
+    dim3 g2(nq, (unsigned)std::min<int64_t>(std::min<int64_t>(nbins / kCombineWarps, want_blocks), 65535));
     stage1_combine_kernel<<<g2, kCombineWarps * 32, 0, st>>>(tables, l, keys, key_cap, n_pos, flags);
     CHM_TRY(launch_status("stage1_combine_kernel"));
     CHM_CUDA(cudaMemsetAsync(bitmaps, 0, sizeof(uint32_t) * (size_t)nq * words, st));
