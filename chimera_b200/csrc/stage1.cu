@@ -398,9 +398,18 @@ __global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
             for (int i = threadIdx.x; i < 4096; i += blockDim.x) s_hist[i] = 0;
             __syncthreads();
             const uint64_t prefix = s_prefix, pmask = s_pmask;
-            for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-                const uint64_t key = qk[i];
-                if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> sh) & dmask], 1u);
+            // four independent loads in flight per thread
+            for (int64_t i0 = threadIdx.x; i0 < n; i0 += 4 * (int64_t)blockDim.x) {
+                uint64_t k4[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int64_t i = i0 + u * (int64_t)blockDim.x;
+                    k4[u] = i < n ? __ldcg(qk + i) : ~prefix;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (i0 + u * (int64_t)blockDim.x < n && (k4[u] & pmask) == prefix)
+                        atomicAdd(&s_hist[(k4[u] >> sh) & dmask], 1u);
             }
             __syncthreads();
             // thread t owns digits [4095-4t-3, 4095-4t] (descending order)
@@ -428,11 +437,19 @@ __global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
             __syncthreads();
         }
         const uint64_t prefix = s_prefix, pmask = s_pmask;
-        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-            const uint64_t key = qk[i];
-            if ((key & pmask) >= prefix) {
-                const uint32_t at = atomicAdd(&s_cnt, 1u);
-                if (at < (uint32_t)k_eff) s_out[at] = key;
+        for (int64_t i0 = threadIdx.x; i0 < n; i0 += 4 * (int64_t)blockDim.x) {
+            uint64_t k4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t i = i0 + u * (int64_t)blockDim.x;
+                k4[u] = i < n ? __ldcg(qk + i) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (i0 + u * (int64_t)blockDim.x < n && (k4[u] & pmask) >= prefix) {
+                    const uint32_t at = atomicAdd(&s_cnt, 1u);
+                    if (at < (uint32_t)k_eff) s_out[at] = k4[u];
+                }
             }
         }
         __syncthreads();
