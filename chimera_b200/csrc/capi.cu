@@ -70,7 +70,7 @@ static void layout(A& a, const chm_index* idx, const chm_search_params* p, Searc
                                    ? chm_probe_tc_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe)
                                    : chm_probe_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe);
     const size_t s1_bytes = stage1_bytes(idx, p->batch, p->nprobe, p->table_log2_extra);
-    const size_t rt_bytes = 0;
+    const size_t rt_bytes = chm_fullbit_score_tc_workspace_bytes(p->batch, p->k_refine);
     auto rot = a.template take<float>(ntok * kDim);
     auto cb1 = a.template take<float>(ntok);
     auto cbex = a.template take<float>(ntok);
@@ -162,7 +162,13 @@ extern "C" chm_status chm_search(const chm_index* idx, const chm_search_params* 
                                 b.onebit, st));
         CHM_TRY(chm_select_fullbit(nq, b.refined_docs, b.onebit, b.num_refined, p->k_refine,
                                    p->k_full_bit, p->num_chunks, b.fb_docs, b.num_fb, fb_cap, st));
-        CHM_TRY(chm_fullbit_score(idx, nq, b.rot, b.cbex, b.fb_docs, b.num_fb, fb_cap, b.fb_scores, st));
+        // the tensor-core filter pays off on batches; a few queries are faster
+        // with the plain kernel's single launch (same scores either way)
+        if (nq >= 16)
+            CHM_TRY(chm_fullbit_score_tc(idx, nq, b.rot, b.cbex, b.fb_docs, b.num_fb, fb_cap, b.fb_scores, b.rt_ws,
+                                         b.rt_bytes, st));
+        else
+            CHM_TRY(chm_fullbit_score(idx, nq, b.rot, b.cbex, b.fb_docs, b.num_fb, fb_cap, b.fb_scores, st));
         CHM_TRY(chm_final_topk(nq, b.fb_docs, b.fb_scores, b.num_fb, fb_cap, p->k, results + q0 * p->k,
                                num_results + q0, st));
         chm::fold_flags_kernel<<<(nq + 255) / 256, 256, 0, st>>>(b.flags, num_results + q0, nq);

@@ -90,6 +90,17 @@ __device__ __forceinline__ float lut_ip(const float* lut, uint4 code) {
     return ip;
 }
 
+// Sum of 16 AVX-512 lanes in _mm512_reduce_add_ps order: upper 8 + lower 8,
+// then upper 4 + lower 4, then (0 + 2) + (1 + 3).
+__device__ __forceinline__ float reduce16_avx512(const float (&s)[16]) {
+    float t3[8], t6[4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t3[i] = fadd(s[8 + i], s[i]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) t6[i] = fadd(t3[4 + i], t3[i]);
+    return fadd(fadd(t6[0], t6[2]), fadd(t6[1], t6[3]));
+}
+
 // Ordered-key transform: ascending uint order == ascending float order.
 __device__ __forceinline__ uint32_t float_key_asc(float f) {
     uint32_t b = __float_as_uint(f);

@@ -192,23 +192,18 @@ __global__ void __launch_bounds__(1024) select_fullbit_kernel(
 // and keeps max((ip - cbex) * factor) (search_impl.cu:538-566).  The doc
 // score adds the two 16-lane halves of the maxima and reduces them the same
 // way (:569-572).
-__device__ __forceinline__ float reduce16_avx512(const float (&s)[16]) {
-    float t3[8], t6[4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) t3[i] = fadd(s[8 + i], s[i]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) t6[i] = fadd(t3[4 + i], t3[i]);
-    return fadd(fadd(t6[0], t6[2]), fadd(t6[1], t6[3]));
-}
-
 constexpr int kFbWarps = 4;
 constexpr int kFbChunkTokens = 32;   // tokens staged in shared memory at a time
 
+// kListed: only the positions in `list` [nq][fb_cap] (list_count [nq]), the
+// docs longer than one tensor-core tile (refine_tc.cu).
+template <bool kListed>
 __global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
     const int64_t* __restrict__ doc_ptrs, const uint8_t* __restrict__ full_codes,
     const float* __restrict__ full_factors, int w, const float* __restrict__ rot,
     const float* __restrict__ cbex, const int32_t* __restrict__ fb_docs,
-    const int32_t* __restrict__ num_fb, int fb_cap, float* __restrict__ scores) {
+    const int32_t* __restrict__ num_fb, int fb_cap, float* __restrict__ scores,
+    const int32_t* __restrict__ list, const int32_t* __restrict__ list_count) {
     // per warp: up to 32 tokens' packed codes (<= 128 B each) and factors,
     // plus one decoded token (128 floats)
     __shared__ __align__(16) uint8_t s_code[kFbWarps][kFbChunkTokens * 128];
@@ -216,9 +211,10 @@ __global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
     __shared__ __align__(16) float s_dec[kFbWarps][kDim];
     const int q = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int F = num_fb[q];
-    const int i = blockIdx.x * kFbWarps + warp;
-    if (i >= F) return;
+    const int F = kListed ? list_count[q] : num_fb[q];
+    const int li = blockIdx.x * kFbWarps + warp;
+    if (li >= F) return;
+    const int i = kListed ? list[(size_t)q * fb_cap + li] : li;
     float qr[kDim];
     const float4* qsrc = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + lane) * kDim);
 #pragma unroll
@@ -409,10 +405,20 @@ extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const 
                                         void* stream) {
     if (nq <= 0) return CHM_OK;
     dim3 g((fb_cap + chm::kFbWarps - 1) / chm::kFbWarps, nq);
-    chm::fullbit_kernel<<<g, chm::kFbWarps * 32, 0, (cudaStream_t)stream>>>(
+    chm::fullbit_kernel<false><<<g, chm::kFbWarps * 32, 0, (cudaStream_t)stream>>>(
         idx->doc_ptrs, idx->full_codes, idx->full_factors, 1 + idx->ex_bits, rot, cbex, fb_docs,
-        num_fb, fb_cap, scores);
+        num_fb, fb_cap, scores, nullptr, nullptr);
     return chm::launch_status("fullbit_kernel");
+}
+
+chm_status chm_fullbit_listed(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
+                              const int32_t* fb_docs, const int32_t* num_fb, int32_t fb_cap, float* scores,
+                              const int32_t* list, const int32_t* list_count, cudaStream_t st) {
+    dim3 g((fb_cap + chm::kFbWarps - 1) / chm::kFbWarps, nq);
+    chm::fullbit_kernel<true><<<g, chm::kFbWarps * 32, 0, st>>>(idx->doc_ptrs, idx->full_codes, idx->full_factors,
+                                                                1 + idx->ex_bits, rot, cbex, fb_docs, num_fb, fb_cap,
+                                                                scores, list, list_count);
+    return chm::launch_status("fullbit_listed");
 }
 
 extern "C" chm_status chm_final_topk(int32_t nq, const int32_t* fb_docs, const float* fb_scores,

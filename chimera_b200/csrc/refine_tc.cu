@@ -26,6 +26,7 @@
 // a two-deep pipeline: while item k's accumulators are read out and its docs
 // reduced (warp per doc, lane per query token), item k+1's codes are gathered,
 // expanded and multiplied.
+#include "codes.cuh"
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -149,6 +150,10 @@ __global__ void refine_plan_kernel(const int64_t* __restrict__ doc_ptrs, const i
 
 // Stage of one item into pipeline buffer `buf`: doc offsets, the rows' codes
 // and factors, the expanded bits, and the MMA into TMEM columns [64 buf, +64).
+// kFull: the (1+ex_bits)-bit codes in token order (full_codes / full_factors,
+// width w), expanded to their integer levels 0..2^w-1; else the 1-bit codes
+// in cluster order (through tok2pos), expanded to 0/1.
+template <bool kFull, int kW>
 __device__ __forceinline__ void rt_stage(RtSmem& s, int buf, int item, int q, int k_refine,
                                          const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
                                          const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
@@ -191,25 +196,57 @@ __device__ __forceinline__ void rt_stage(RtSmem& s, int buf, int item, int q, in
     uint4 code = make_uint4(0, 0, 0, 0);
     float f = 0.0f;
     int ld = -1;
-    if (tid < T) {
-        ld = 0;
-        while (s.doc_tok0[buf][ld + 1] <= tid) ++ld;
-        const int64_t token = s.doc_first[buf][ld] + (tid - s.doc_tok0[buf][ld]);
-        const uint32_t pos = __ldg(tok2pos + token);
-        code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
-        f = __ldg(factor1 + pos);
-    }
-    s.code[buf][tid] = code;
-    s.fac[buf][tid] = f;
-    s.row_doc[buf][tid] = ld;
-    const uint32_t wv[4] = {code.x, code.y, code.z, code.w};
     uint8_t* a = s.a[buf];
+    if (kFull) {
+        if (tid < T) {
+            ld = 0;
+            while (s.doc_tok0[buf][ld + 1] <= tid) ++ld;
+            const int64_t token = s.doc_first[buf][ld] + (tid - s.doc_tok0[buf][ld]);
+            constexpr int bytes = kDim * kW / 8;
+            // the packed code in registers (16 * kW bytes)
+            uint8_t pk[bytes];
+            const uint4* src = reinterpret_cast<const uint4*>(codes1 + (size_t)token * bytes);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const uint32_t h = wv[c >> 1] >> ((c & 1) * 16);
-        *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) =
-            make_uint4(nib_bytes(h & 0xF), nib_bytes((h >> 4) & 0xF), nib_bytes((h >> 8) & 0xF),
-                       nib_bytes((h >> 12) & 0xF));
+            for (int v = 0; v < kW; ++v) *reinterpret_cast<uint4*>(pk + 16 * v) = __ldg(src + v);
+            f = __ldg(factor1 + token);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t wd[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t x = 0;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) x |= (uint32_t)code_at(pk, c * 16 + j * 4 + b, kW) << (8 * b);
+                    wd[j] = x;
+                }
+                *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) = make_uint4(0, 0, 0, 0);
+        }
+        s.fac[buf][tid] = f;
+        s.row_doc[buf][tid] = ld;
+    } else {
+        if (tid < T) {
+            ld = 0;
+            while (s.doc_tok0[buf][ld + 1] <= tid) ++ld;
+            const int64_t token = s.doc_first[buf][ld] + (tid - s.doc_tok0[buf][ld]);
+            const uint32_t pos = __ldg(tok2pos + token);
+            code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
+            f = __ldg(factor1 + pos);
+        }
+        s.code[buf][tid] = code;
+        s.fac[buf][tid] = f;
+        s.row_doc[buf][tid] = ld;
+        const uint32_t wv[4] = {code.x, code.y, code.z, code.w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t h = wv[c >> 1] >> ((c & 1) * 16);
+            *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) =
+                make_uint4(nib_bytes(h & 0xF), nib_bytes((h >> 4) & 0xF), nib_bytes((h >> 8) & 0xF),
+                           nib_bytes((h >> 12) & 0xF));
+        }
     }
     fence_proxy_async_smem();
     sm100::tc_fence_before();
@@ -225,6 +262,10 @@ __device__ __forceinline__ void rt_stage(RtSmem& s, int buf, int item, int q, in
     }
 }
 
+// kFull: the full-bit MaxSim of fullbit_kernel (codes at width w, cb = cbex,
+// the AVX-512 lane order for the exact sums, its 16-lane document reduction);
+// else the 1-bit score of refine_1bit_kernel (cb = cb1).
+template <bool kFull, int kW>
 __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
     const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos, const uint8_t* __restrict__ codes1,
     const float* __restrict__ factor1, const float* __restrict__ lut, const float* __restrict__ cb1,
@@ -237,7 +278,6 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
     const int q = blockIdx.y;
     const int NI = n_items[q];
     if ((int)blockIdx.x >= NI) return;
-    const float* qlut = lut + (size_t)q * kQ * kLutPerQ;
 
     // ---- prologue: query limbs (B operand), margins, TMEM, barriers --------
     {
@@ -278,14 +318,23 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
             }
             const float c = cb1[q * kQ + tid];
             s.cb1[tid] = c;
-            // quantisation + LUT-sum rounding (34 adds) + the two dist roundings of both paths
-            const double m = e + 40.0 * 0x1p-24 * s1 + 0x1p-21 * (s1 + fabs((double)c));
+            double m;
+            if (kFull) {
+                // code levels up to W: quantisation error times W, the exact sum's 12
+                // roundings (8 fmas + 4 tree adds) and the int->float conversion of
+                // the estimate, then the two dist roundings of both paths
+                const double W = (double)((1 << kW) - 1);
+                m = W * e + 24.0 * 0x1p-24 * W * s1 + 0x1p-21 * (W * s1 + fabs((double)c));
+            } else {
+                // quantisation + LUT-sum rounding (34 adds) + the two dist roundings of both paths
+                m = e + 40.0 * 0x1p-24 * s1 + 0x1p-21 * (s1 + fabs((double)c));
+            }
             s.em[tid] = __double2float_ru(m * (1.0 + 0x1p-20));
         }
         for (int i = tid; i < 32 * kDim; i += kRtThreads) s.qv[i >> 7][i & 127] = rot[(size_t)q * kQ * kDim + i];
         for (int i = tid; i < kRtMaxDocs * 32; i += kRtThreads) {
             (&s.mx[0][0])[i] = 0u;
-            (&s.exact[0][0])[i] = float_key_asc(-FLT_MAX);
+            (&s.exact[0][0])[i] = float_key_asc(kFull ? -INFINITY : -FLT_MAX);
         }
         if (tid < kRtMaxDocs) s.maxf[tid] = 0u;
         if (tid == 0) {
@@ -308,7 +357,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
     bool failed = false;  // uniform across the CTA (set from __syncthreads_or)
     unsigned long long n_rows = 0, n_cand = 0;
 
-    rt_stage(s, 0, blockIdx.x, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items, tmem);
+    rt_stage<kFull, kW>(s, 0, blockIdx.x, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items, tmem);
     int k = 0;
     bool next_issued = false;  // an MMA of item k+1 is in flight
     for (int it = blockIdx.x; it < NI; it += gridDim.x, ++k) {
@@ -316,7 +365,8 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
         const int nxt = it + gridDim.x;
         next_issued = nxt < NI;
         if (next_issued)  // overlaps this item's MMA and epilogue
-            rt_stage(s, buf ^ 1, nxt, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items, tmem);
+            rt_stage<kFull, kW>(s, buf ^ 1, nxt, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items,
+                                tmem);
         bool ok = true;
         if (tid == 0) ok = sm100::mbar_wait(&s.bar[buf], (uint32_t)((k >> 1) & 1));
         if (__syncthreads_or(!ok)) {
@@ -407,7 +457,26 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
             for (int c = tid; c < nc; c += kRtThreads) {
                 const uint32_t e = s.cand[c];
                 const int row = (int)(e >> 5), t = (int)(e & 31);
-                const float ip = lut_ip_from_query(s.qv[t], s.code[buf][row]);
+                float ip;
+                if (kFull) {
+                    // fullbit_kernel's arithmetic: 16 lane chains over b = 0..7, reduce16
+                    const uint8_t* a = s.a[buf];
+                    float acc[16];
+#pragma unroll
+                    for (int l = 0; l < 16; ++l) acc[l] = 0.0f;
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        const uint4 raw = *reinterpret_cast<const uint4*>(a + sw128_off(row, b));
+                        const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                        for (int l = 0; l < 16; ++l)
+                            acc[l] = __fmaf_rn((float)((rw[l >> 2] >> (8 * (l & 3))) & 0xFFu), s.qv[t][16 * b + l],
+                                               acc[l]);
+                    }
+                    ip = reduce16_avx512(acc);
+                } else {
+                    ip = lut_ip_from_query(s.qv[t], s.code[buf][row]);
+                }
                 const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[buf][row]);
                 atomicMax(&s.exact[s.row_doc[buf][row]][t], float_key_asc(dist));
             }
@@ -418,12 +487,20 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
         const int nd = s.nd[buf];
         for (int j = warp; j < nd; j += kRtThreads / 32) {
             const float m = key_to_float_asc(s.exact[j][lane]);
-            float x = fadd(fadd(fadd(0.0f, m), 0.0f), 0.0f);
+            float x;
+            if (kFull) {
+                // fullbit_kernel: max[0:16] + max[16:32] lane-wise, then the 16-lane tree
+                x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+                for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
+            } else {
+                x = fadd(fadd(fadd(0.0f, m), 0.0f), 0.0f);
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+            }
             if (lane == 0) scores[(size_t)q * k_refine + s.r0[buf] + j] = s.doc_id[buf][j] < 0 ? -INFINITY : x;
             s.mx[j][lane] = 0u;
-            s.exact[j][lane] = float_key_asc(-FLT_MAX);
+            s.exact[j][lane] = float_key_asc(kFull ? -INFINITY : -FLT_MAX);
             if (lane == 0) s.maxf[j] = 0u;
         }
         if (tid == 0) s.n_cand = 0;
@@ -459,7 +536,59 @@ __global__ void refine_status_clear_kernel(uint32_t* status, int nq, unsigned lo
 
 namespace chm {
 size_t refine_tc_smem_bytes() { return sizeof(RtSmem) + 1024; }
+
+static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, const int32_t* counts, int cap,
+                          int2* items, int32_t* n_items, int32_t* big, int32_t* n_big, uint32_t* status,
+                          unsigned long long* stats, cudaStream_t st) {
+    refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(status, nq, stats);
+    CHM_TRY(launch_status("refine_status_clear_kernel"));
+    const size_t plan_smem = sizeof(int) * (size_t)cap;
+    CHM_CUDA(cudaFuncSetAttribute(refine_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem));
+    refine_plan_kernel<<<nq, 256, plan_smem, st>>>(idx->doc_ptrs, docs, counts, cap, items, n_items, big, n_big);
+    return launch_status("refine_plan_kernel");
 }
+
+static dim3 rt_grid(int nq, int cap) {
+    int gx = (3 * 148 * 2 + nq - 1) / nq;
+    gx = std::max(1, std::min(gx, cap));
+    return dim3((unsigned)gx, (unsigned)nq);
+}
+
+template <int kW>
+static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex,
+                                   const int32_t* fb_docs, int fb_cap, const int2* items, const int32_t* n_items,
+                                   float* scores, uint32_t* status, unsigned long long* stats, cudaStream_t st) {
+    const size_t smem = refine_tc_smem_bytes();
+    CHM_CUDA(cudaFuncSetAttribute(refine_tc_kernel<true, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    refine_tc_kernel<true, kW><<<rt_grid(nq, fb_cap), kRtThreads, smem, st>>>(
+        idx->doc_ptrs, nullptr, idx->full_codes, idx->full_factors, nullptr, cbex, rot, fb_docs, fb_cap, items,
+        n_items, scores, status, stats);
+    return launch_status("fullbit_tc_kernel");
+}
+
+// full-bit rescoring of the queries flagged in `status` by the plain kernel
+__global__ void flagged_counts_kernel(const uint32_t* status, const int32_t* num_fb, int32_t* out, int nq) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < nq) out[i] = status[i] ? num_fb[i] : 0;
+}
+}  // namespace chm
+
+extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
+                                        const int32_t* fb_docs, const int32_t* num_fb, int32_t fb_cap,
+                                        float* scores, void* stream);
+
+namespace chm {
+static chm_status rescore_flagged_fullbit(const chm_index* idx, int nq, const float* rot, const float* cbex,
+                                          const int32_t* fb_docs, const int32_t* num_fb, int fb_cap, float* scores,
+                                          uint32_t* status, cudaStream_t st) {
+    // the status array is reused as the per-query doc counts: 0 for queries
+    // that succeeded, num_fb for flagged ones
+    int32_t* counts = reinterpret_cast<int32_t*>(status);
+    flagged_counts_kernel<<<(nq + 255) / 256, 256, 0, st>>>(status, num_fb, counts, nq);
+    CHM_TRY(launch_status("flagged_counts_kernel"));
+    return chm_fullbit_score(idx, nq, rot, cbex, fb_docs, counts, fb_cap, scores, st);
+}
+}  // namespace chm
 
 extern "C" size_t chm_refine_1bit_tc_workspace_bytes(int32_t nq, int32_t k_refine) {
     chm::Sizer s;
@@ -491,22 +620,54 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     int32_t* big = a.take<int32_t>((size_t)nq * k_refine);
     int32_t* n_big = a.take<int32_t>((size_t)nq);
     if (a.overflow) return CHM_ERR_CAPACITY;
-    chm::refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(status, nq, stats);
-    CHM_TRY(chm::launch_status("refine_status_clear_kernel"));
-    const size_t plan_smem = sizeof(int) * (size_t)k_refine;
-    CHM_CUDA(cudaFuncSetAttribute(chm::refine_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)plan_smem));
-    chm::refine_plan_kernel<<<nq, 256, plan_smem, st>>>(idx->doc_ptrs, refined_docs, num_refined, k_refine, items,
-                                                        n_items, big, n_big);
-    CHM_TRY(chm::launch_status("refine_plan_kernel"));
+    CHM_TRY(chm::rt_plan(idx, nq, refined_docs, num_refined, k_refine, items, n_items, big, n_big, status, stats, st));
     const size_t smem = chm::refine_tc_smem_bytes();
-    CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    int gx = (4 * 148 * 2 + nq - 1) / nq;
-    gx = std::max(1, std::min(gx, k_refine));
-    chm::refine_tc_kernel<<<dim3((unsigned)gx, (unsigned)nq), chm::kRtThreads, smem, st>>>(
+    CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    chm::refine_tc_kernel<false, 1><<<chm::rt_grid(nq, k_refine), chm::kRtThreads, smem, st>>>(
         idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, rot, refined_docs, k_refine, items,
         n_items, scores, status, stats);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
     return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, big, n_big,
                                     status, st);
+}
+
+chm_status chm_fullbit_listed(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
+                              const int32_t* fb_docs, const int32_t* num_fb, int32_t fb_cap, float* scores,
+                              const int32_t* list, const int32_t* list_count, cudaStream_t st);
+
+extern "C" size_t chm_fullbit_score_tc_workspace_bytes(int32_t nq, int32_t fb_cap) {
+    return chm_refine_1bit_tc_workspace_bytes(nq, fb_cap);
+}
+
+extern "C" chm_status chm_fullbit_score_tc(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
+                                           const int32_t* fb_docs, const int32_t* num_fb, int32_t fb_cap,
+                                           float* scores, void* ws, size_t ws_bytes, void* stream) {
+    if (nq <= 0) return CHM_OK;
+    if (!idx || fb_cap <= 0 || fb_cap > CHM_MAX_K_REFINE) return CHM_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int w = 1 + idx->ex_bits;
+    if (w < 2 || w > 7)  // levels up to 255 (w = 8) do not fit the signed 8-bit operand
+        return chm_fullbit_score(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, stream);
+    chm::Arena a(ws, ws_bytes);
+    int2* items = a.take<int2>((size_t)nq * fb_cap);
+    int32_t* n_items = a.take<int32_t>((size_t)nq);
+    uint32_t* status = a.take<uint32_t>((size_t)nq);
+    unsigned long long* stats = a.take<unsigned long long>(2);
+    int32_t* big = a.take<int32_t>((size_t)nq * fb_cap);
+    int32_t* n_big = a.take<int32_t>((size_t)nq);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_TRY(chm::rt_plan(idx, nq, fb_docs, num_fb, fb_cap, items, n_items, big, n_big, status, stats, st));
+    switch (w) {
+        case 2: CHM_TRY(chm::launch_fullbit_tc<2>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
+        case 3: CHM_TRY(chm::launch_fullbit_tc<3>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
+        case 4: CHM_TRY(chm::launch_fullbit_tc<4>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
+        case 5: CHM_TRY(chm::launch_fullbit_tc<5>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
+        case 6: CHM_TRY(chm::launch_fullbit_tc<6>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
+        case 7: CHM_TRY(chm::launch_fullbit_tc<7>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
+        default: return CHM_ERR_INVALID;
+    }
+    // long docs; then every doc of a query whose tensor-core launch failed
+    CHM_TRY(chm_fullbit_listed(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, big, n_big, st));
+    return chm::rescore_flagged_fullbit(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, status, st);
 }

@@ -179,6 +179,8 @@ class CudaShardBackend:
         self.onebit = e(B, self.kr)
         self.fd, self.nf, self.fs = e(B, self.kr, dt=torch.int32), e(B, dt=torch.int32), e(B, self.kr)
         self.res, self.nres = e(B, self.k, dt=torch.int64), e(B, dt=torch.int32)
+        self.fb_bytes = self.L.chm_fullbit_score_tc_workspace_bytes(B, self.kr)
+        self.fb_ws = e(max(self.fb_bytes, 1), dt=torch.uint8)
         self._probe_ws = {}
         self._s1_extra = None
 
@@ -267,8 +269,8 @@ class CudaShardBackend:
 
     def fullbit(self, st, fb_local, nf):
         P, B = capi._ptr, self.B
-        self._chk(self.L.chm_fullbit_score(self.v, B, P(self.rot), P(self.cbex), P(fb_local), P(nf), self.kr,
-                                           P(self.fs), self._stream()), "fullbit")
+        self._chk(self.L.chm_fullbit_score_tc(self.v, B, P(self.rot), P(self.cbex), P(fb_local), P(nf), self.kr,
+                                              P(self.fs), P(self.fb_ws), self.fb_bytes, self._stream()), "fullbit")
         return self.fs[:B]
 
     def final(self, fb_docs, fbs, nf):

@@ -211,6 +211,19 @@ chm_status chm_fullbit_score(const chm_index* index, int32_t nq, const float* ro
                              const float* cbex, const int32_t* fb_docs, const int32_t* num_fb,
                              int32_t fb_cap, float* scores, void* stream);
 
+/* chm_fullbit_score with the int8 tensor-core filter of chm_refine_1bit_tc:
+ * the code levels (0..2^w-1) against the query in 16-bit fixed point give each
+ * (token, query token) an estimate with a proven error bound; only tokens that
+ * can hold a document's maximum get the exact sum in the AVX-512 lane order.
+ * Same scores as chm_fullbit_score, bit for bit.  Widths w = 1 + ex_bits of 2
+ * to 7 (w = 8 runs chm_fullbit_score).  Workspace from
+ * chm_fullbit_score_tc_workspace_bytes. */
+size_t chm_fullbit_score_tc_workspace_bytes(int32_t nq, int32_t fb_cap);
+chm_status chm_fullbit_score_tc(const chm_index* index, int32_t nq, const float* rot,
+                                const float* cbex, const int32_t* fb_docs, const int32_t* num_fb,
+                                int32_t fb_cap, float* scores, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* Final ordering of the full-bit scored docs, best first, ties to the larger
  * doc id (std::priority_queue<pair<float,size_t>> pops, search_impl.cu:
  * 496-500).  results [nq * k] (-1 padded), num_results [nq]. */
