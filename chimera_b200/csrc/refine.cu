@@ -212,63 +212,65 @@ __global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
     const int q = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int F = kListed ? list_count[q] : num_fb[q];
-    const int li = blockIdx.x * kFbWarps + warp;
-    if (li >= F) return;
-    const int i = kListed ? list[(size_t)q * fb_cap + li] : li;
-    float qr[kDim];
-    const float4* qsrc = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + lane) * kDim);
+    // warps stride over the query's docs (the grid may be smaller than F / kFbWarps)
+    for (int li = blockIdx.x * kFbWarps + warp; li < F; li += gridDim.x * kFbWarps) {
+        const int i = kListed ? list[(size_t)q * fb_cap + li] : li;
+        float qr[kDim];
+        const float4* qsrc = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + lane) * kDim);
 #pragma unroll
-    for (int j = 0; j < kDim / 4; ++j) {
-        const float4 v = qsrc[j];
-        qr[4 * j] = v.x; qr[4 * j + 1] = v.y; qr[4 * j + 2] = v.z; qr[4 * j + 3] = v.w;
-    }
-    const float cb = cbex[q * kQ + lane];
-    const int64_t doc = fb_docs[(size_t)q * fb_cap + i];
-    if (doc < 0) {  // a slot another document shard owns
-        if (lane == 0) scores[(size_t)q * fb_cap + i] = -INFINITY;
-        return;
-    }
-    const int bytes = kDim * w / 8;       // 16 * w, a multiple of 16
-    const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
-    float m = -INFINITY;
-    for (int64_t c0 = t0; c0 < t1; c0 += kFbChunkTokens) {
-        const int nt = (int)min((int64_t)kFbChunkTokens, t1 - c0);
-        // one coalesced burst: the chunk's codes are contiguous in token order
-        const uint4* src = reinterpret_cast<const uint4*>(full_codes + (size_t)c0 * bytes);
-        uint4* dst = reinterpret_cast<uint4*>(s_code[warp]);
-        for (int v = lane; v < nt * bytes / 16; v += 32) dst[v] = __ldg(src + v);
-        if (lane < nt) s_fac[warp][lane] = __ldg(full_factors + c0 + lane);
-        __syncwarp();
-        for (int t = 0; t < nt; ++t) {
-            const uint8_t* code = s_code[warp] + t * bytes;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) s_dec[warp][32 * k + lane] = (float)code_at(code, 32 * k + lane, w);
-            __syncwarp();
-            float s[16];
-#pragma unroll
-            for (int l = 0; l < 16; ++l) s[l] = 0.0f;
-#pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                const float4* dv = reinterpret_cast<const float4*>(&s_dec[warp][16 * b]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float4 d4 = dv[j];
-                    s[4 * j + 0] = __fmaf_rn(d4.x, qr[16 * b + 4 * j + 0], s[4 * j + 0]);
-                    s[4 * j + 1] = __fmaf_rn(d4.y, qr[16 * b + 4 * j + 1], s[4 * j + 1]);
-                    s[4 * j + 2] = __fmaf_rn(d4.z, qr[16 * b + 4 * j + 2], s[4 * j + 2]);
-                    s[4 * j + 3] = __fmaf_rn(d4.w, qr[16 * b + 4 * j + 3], s[4 * j + 3]);
-                }
-            }
-            const float ip = reduce16_avx512(s);
-            m = fmaxf(m, fmul(fsub(ip, cb), s_fac[warp][t]));
-            __syncwarp();
+        for (int j = 0; j < kDim / 4; ++j) {
+            const float4 v = qsrc[j];
+            qr[4 * j] = v.x; qr[4 * j + 1] = v.y; qr[4 * j + 2] = v.z; qr[4 * j + 3] = v.w;
         }
-    }
-    // sum = max[0:16] + max[16:32] lane-wise, then the 16-lane reduction
-    float x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
+        const float cb = cbex[q * kQ + lane];
+        const int64_t doc = fb_docs[(size_t)q * fb_cap + i];
+        if (doc < 0) {  // a slot another document shard owns
+            if (lane == 0) scores[(size_t)q * fb_cap + i] = -INFINITY;
+            continue;
+        }
+        const int bytes = kDim * w / 8;       // 16 * w, a multiple of 16
+        const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
+        float m = -INFINITY;
+        for (int64_t c0 = t0; c0 < t1; c0 += kFbChunkTokens) {
+            const int nt = (int)min((int64_t)kFbChunkTokens, t1 - c0);
+            // one coalesced burst: the chunk's codes are contiguous in token order
+            const uint4* src = reinterpret_cast<const uint4*>(full_codes + (size_t)c0 * bytes);
+            uint4* dst = reinterpret_cast<uint4*>(s_code[warp]);
+            for (int v = lane; v < nt * bytes / 16; v += 32) dst[v] = __ldg(src + v);
+            if (lane < nt) s_fac[warp][lane] = __ldg(full_factors + c0 + lane);
+            __syncwarp();
+            for (int t = 0; t < nt; ++t) {
+                const uint8_t* code = s_code[warp] + t * bytes;
 #pragma unroll
-    for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
-    if (lane == 0) scores[(size_t)q * fb_cap + i] = x;
+                for (int k = 0; k < 4; ++k) s_dec[warp][32 * k + lane] = (float)code_at(code, 32 * k + lane, w);
+                __syncwarp();
+                float s[16];
+#pragma unroll
+                for (int l = 0; l < 16; ++l) s[l] = 0.0f;
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                    const float4* dv = reinterpret_cast<const float4*>(&s_dec[warp][16 * b]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float4 d4 = dv[j];
+                        s[4 * j + 0] = __fmaf_rn(d4.x, qr[16 * b + 4 * j + 0], s[4 * j + 0]);
+                        s[4 * j + 1] = __fmaf_rn(d4.y, qr[16 * b + 4 * j + 1], s[4 * j + 1]);
+                        s[4 * j + 2] = __fmaf_rn(d4.z, qr[16 * b + 4 * j + 2], s[4 * j + 2]);
+                        s[4 * j + 3] = __fmaf_rn(d4.w, qr[16 * b + 4 * j + 3], s[4 * j + 3]);
+                    }
+                }
+                const float ip = reduce16_avx512(s);
+                m = fmaxf(m, fmul(fsub(ip, cb), s_fac[warp][t]));
+                __syncwarp();
+            }
+        }
+        // sum = max[0:16] + max[16:32] lane-wise, then the 16-lane reduction
+        float x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
+#pragma unroll
+        for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
+        if (lane == 0) scores[(size_t)q * fb_cap + i] = x;
+        __syncwarp();  // s_code / s_dec are reused by the warp's next doc
+    }
 }
 
 // std::priority_queue<std::pair<float, size_t>> pop order: score desc, doc
@@ -411,10 +413,20 @@ extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const 
     return chm::launch_status("fullbit_kernel");
 }
 
+// chm_fullbit_score over a small grid: for rescoring a few flagged queries
+chm_status chm_fullbit_flagged(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
+                               const int32_t* fb_docs, const int32_t* counts, int32_t fb_cap, float* scores,
+                               cudaStream_t st) {
+    chm::fullbit_kernel<false><<<dim3(2, nq), chm::kFbWarps * 32, 0, st>>>(
+        idx->doc_ptrs, idx->full_codes, idx->full_factors, 1 + idx->ex_bits, rot, cbex, fb_docs, counts, fb_cap,
+        scores, nullptr, nullptr);
+    return chm::launch_status("fullbit_flagged");
+}
+
 chm_status chm_fullbit_listed(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
                               const int32_t* fb_docs, const int32_t* num_fb, int32_t fb_cap, float* scores,
                               const int32_t* list, const int32_t* list_count, cudaStream_t st) {
-    dim3 g((fb_cap + chm::kFbWarps - 1) / chm::kFbWarps, nq);
+    dim3 g(16, nq);  // tens of long docs per query at most: 64 warps each, striding over them
     chm::fullbit_kernel<true><<<g, chm::kFbWarps * 32, 0, st>>>(idx->doc_ptrs, idx->full_codes, idx->full_factors,
                                                                 1 + idx->ex_bits, rot, cbex, fb_docs, num_fb, fb_cap,
                                                                 scores, list, list_count);

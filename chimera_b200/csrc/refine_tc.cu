@@ -573,9 +573,9 @@ __global__ void flagged_counts_kernel(const uint32_t* status, const int32_t* num
 }
 }  // namespace chm
 
-extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
-                                        const int32_t* fb_docs, const int32_t* num_fb, int32_t fb_cap,
-                                        float* scores, void* stream);
+chm_status chm_fullbit_flagged(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
+                               const int32_t* fb_docs, const int32_t* counts, int32_t fb_cap, float* scores,
+                               cudaStream_t st);
 
 namespace chm {
 static chm_status rescore_flagged_fullbit(const chm_index* idx, int nq, const float* rot, const float* cbex,
@@ -586,7 +586,7 @@ static chm_status rescore_flagged_fullbit(const chm_index* idx, int nq, const fl
     int32_t* counts = reinterpret_cast<int32_t*>(status);
     flagged_counts_kernel<<<(nq + 255) / 256, 256, 0, st>>>(status, num_fb, counts, nq);
     CHM_TRY(launch_status("flagged_counts_kernel"));
-    return chm_fullbit_score(idx, nq, rot, cbex, fb_docs, counts, fb_cap, scores, st);
+    return chm_fullbit_flagged(idx, nq, rot, cbex, fb_docs, counts, fb_cap, scores, st);
 }
 }  // namespace chm
 
