@@ -42,14 +42,16 @@ constexpr float kFix = 16384.0f;     // fixed-point scale of the query limbs
 constexpr uint32_t kRtIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kRtN >> 3) << 17) |
                               ((uint32_t)(kRtRows >> 4) << 24);
 
-constexpr int kRtMaxCand = 1024;     // candidates per tile (more: the query is rescored by the SIMT kernel)
+constexpr int kRtMaxCand = 512;      // candidates per tile (more: the query is rescored by the SIMT kernel)
 
+// kFull: no 1-bit code rows (the exact sums read the expanded tile), which
+// keeps the full-bit variant at three CTAs per SM.
+template <bool kFull>
 struct __align__(1024) RtSmem {
     uint8_t a[2][kRtRows * 128];     // token bits, K-major SW128 (two pipeline buffers)
     uint8_t b[kRtN * 128];           // query limbs, K-major SW128
     float da[kRtRows][33];           // estimated dist per (row, query token)
-    float qv[32][129];               // rotated query tokens (exact LUT entries are rebuilt from them)
-    uint4 code[2][kRtRows];
+    uint4 code[kFull ? 1 : 2][kRtRows];
     float fac[2][kRtRows];
     int row_doc[2][kRtRows];         // item-local doc of each row
     int doc_tok0[2][kRtMaxDocs + 1]; // row offsets of the item's docs
@@ -154,7 +156,7 @@ __global__ void refine_plan_kernel(const int64_t* __restrict__ doc_ptrs, const i
 // width w), expanded to their integer levels 0..2^w-1; else the 1-bit codes
 // in cluster order (through tok2pos), expanded to 0/1.
 template <bool kFull, int kW>
-__device__ __forceinline__ void rt_stage(RtSmem& s, int buf, int item, int q, int k_refine,
+__device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, int q, int k_refine,
                                          const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
                                          const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
                                          const int32_t* __restrict__ refined_docs, const int2* __restrict__ items,
@@ -236,7 +238,7 @@ __device__ __forceinline__ void rt_stage(RtSmem& s, int buf, int item, int q, in
             code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
             f = __ldg(factor1 + pos);
         }
-        s.code[buf][tid] = code;
+        s.code[kFull ? 0 : buf][tid] = code;
         s.fac[buf][tid] = f;
         s.row_doc[buf][tid] = ld;
         const uint32_t wv[4] = {code.x, code.y, code.z, code.w};
@@ -273,7 +275,8 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
     const int2* __restrict__ items, const int32_t* __restrict__ n_items, float* __restrict__ scores,
     uint32_t* __restrict__ status, unsigned long long* __restrict__ stats) {
     extern __shared__ uint8_t smem_raw[];
-    RtSmem& s = *reinterpret_cast<RtSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    RtSmem<kFull>& s =
+        *reinterpret_cast<RtSmem<kFull>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = blockIdx.y;
     const int NI = n_items[q];
@@ -331,7 +334,6 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
             }
             s.em[tid] = __double2float_ru(m * (1.0 + 0x1p-20));
         }
-        for (int i = tid; i < 32 * kDim; i += kRtThreads) s.qv[i >> 7][i & 127] = rot[(size_t)q * kQ * kDim + i];
         for (int i = tid; i < kRtMaxDocs * 32; i += kRtThreads) {
             (&s.mx[0][0])[i] = 0u;
             (&s.exact[0][0])[i] = float_key_asc(kFull ? -INFINITY : -FLT_MAX);
@@ -457,6 +459,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
             for (int c = tid; c < nc; c += kRtThreads) {
                 const uint32_t e = s.cand[c];
                 const int row = (int)(e >> 5), t = (int)(e & 31);
+                const float* qt = rot + ((size_t)q * kQ + t) * kDim;  // L1-resident: one query's 16 KB
                 float ip;
                 if (kFull) {
                     // fullbit_kernel's arithmetic: 16 lane chains over b = 0..7, reduce16
@@ -470,12 +473,12 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
                         const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
                         for (int l = 0; l < 16; ++l)
-                            acc[l] = __fmaf_rn((float)((rw[l >> 2] >> (8 * (l & 3))) & 0xFFu), s.qv[t][16 * b + l],
+                            acc[l] = __fmaf_rn((float)((rw[l >> 2] >> (8 * (l & 3))) & 0xFFu), __ldg(qt + 16 * b + l),
                                                acc[l]);
                     }
                     ip = reduce16_avx512(acc);
                 } else {
-                    ip = lut_ip_from_query(s.qv[t], s.code[buf][row]);
+                    ip = lut_ip_from_query(qt, s.code[kFull ? 0 : buf][row]);
                 }
                 const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[buf][row]);
                 atomicMax(&s.exact[s.row_doc[buf][row]][t], float_key_asc(dist));
@@ -535,7 +538,8 @@ __global__ void refine_status_clear_kernel(uint32_t* status, int nq, unsigned lo
 }  // namespace chm
 
 namespace chm {
-size_t refine_tc_smem_bytes() { return sizeof(RtSmem) + 1024; }
+template <bool kFull>
+size_t refine_tc_smem_bytes() { return sizeof(RtSmem<kFull>) + 1024; }
 
 static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, const int32_t* counts, int cap,
                           int2* items, int32_t* n_items, int32_t* big, int32_t* n_big, uint32_t* status,
@@ -549,7 +553,9 @@ static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, con
 }
 
 static dim3 rt_grid(int nq, int cap) {
-    int gx = (3 * 148 * 2 + nq - 1) / nq;
+    // about eight waves of 3 CTAs per SM: items per CTA vary by query, so
+    // finer-grained CTAs balance the tail
+    int gx = (3 * 148 * 8 + nq - 1) / nq;
     gx = std::max(1, std::min(gx, cap));
     return dim3((unsigned)gx, (unsigned)nq);
 }
@@ -558,7 +564,7 @@ template <int kW>
 static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex,
                                    const int32_t* fb_docs, int fb_cap, const int2* items, const int32_t* n_items,
                                    float* scores, uint32_t* status, unsigned long long* stats, cudaStream_t st) {
-    const size_t smem = refine_tc_smem_bytes();
+    const size_t smem = refine_tc_smem_bytes<true>();
     CHM_CUDA(cudaFuncSetAttribute(refine_tc_kernel<true, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     refine_tc_kernel<true, kW><<<rt_grid(nq, fb_cap), kRtThreads, smem, st>>>(
         idx->doc_ptrs, nullptr, idx->full_codes, idx->full_factors, nullptr, cbex, rot, fb_docs, fb_cap, items,
@@ -621,7 +627,7 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     int32_t* n_big = a.take<int32_t>((size_t)nq);
     if (a.overflow) return CHM_ERR_CAPACITY;
     CHM_TRY(chm::rt_plan(idx, nq, refined_docs, num_refined, k_refine, items, n_items, big, n_big, status, stats, st));
-    const size_t smem = chm::refine_tc_smem_bytes();
+    const size_t smem = chm::refine_tc_smem_bytes<false>();
     CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
     chm::refine_tc_kernel<false, 1><<<chm::rt_grid(nq, k_refine), chm::kRtThreads, smem, st>>>(
