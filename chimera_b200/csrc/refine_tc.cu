@@ -50,7 +50,6 @@ template <bool kFull>
 struct __align__(1024) RtSmem {
     uint8_t a[2][kRtRows * 128];     // token bits, K-major SW128 (two pipeline buffers)
     uint8_t b[kRtN * 128];           // query limbs, K-major SW128
-    float da[kRtRows][33];           // estimated dist per (row, query token)
     uint4 code[kFull ? 1 : 2][kRtRows];
     float fac[2][kRtRows];
     int row_doc[2][kRtRows];         // item-local doc of each row
@@ -376,7 +375,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
             break;
         }
         sm100::tc_fence_after();
-        // ---- accumulators -> estimated dists, one row per thread
+        // ---- accumulators -> estimated dists, one row per thread, kept in registers
         uint32_t hi[32], lo[32];
         const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + buf * kRtN;
         sm100::tmem_ld32_async(taddr, hi);
@@ -384,69 +383,47 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
         sm100::tmem_wait_ld();
         sm100::tc_fence_before();
         const int T = s.ntok[buf];
-        if (tid < T) {
-            const float f = s.fac[buf][tid];
+        const int ld = tid < T ? s.row_doc[buf][tid] : -1;
+        const float f = tid < T ? s.fac[buf][tid] : 0.0f;
+        float da[32];
 #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-                const float ipa = (float)((int)hi[t] * 256 + (int)lo[t]) * inv_fix;
-                s.da[tid][t] = __fmul_rn(__fsub_rn(ipa, s.cb1[t]), f);
-            }
+        for (int t = 0; t < 32; ++t) {
+            const float ipa = (float)((int)hi[t] * 256 + (int)lo[t]) * inv_fix;
+            da[t] = __fmul_rn(__fsub_rn(ipa, s.cb1[t]), f);
         }
-        __syncthreads();
-        // ---- pass 1: warp w scans its 32 rows, lane = query token; per-doc
-        // max of the estimates and of |factor| (docs are runs of rows)
-        const int w0 = warp * 32;
-        const int nrow = max(0, min(32, T - w0));
+        // ---- pass 1: per (doc, query token) max of the estimates and per doc
+        // max |factor|: a reduction over each doc's lanes (docs are runs of
+        // rows), then one shared atomic per doc and query token
         {
-            int cur = -1;
-            float run = -INFINITY, runf = 0.0f;
-#pragma unroll 8
-            for (int i = 0; i < nrow; ++i) {
-                const int row = w0 + i;
-                const int ld = s.row_doc[buf][row];
-                const float v = s.da[row][lane];
-                const float fa = fabsf(s.fac[buf][row]);
-                if (ld != cur) {
-                    if (cur >= 0) {
-                        atomicMax(&s.mx[cur][lane], float_key_asc(run));
-                        if (lane == 0) atomicMax(&s.maxf[cur], __float_as_uint(runf));
+            const uint32_t grp = __match_any_sync(0xffffffffu, ld);
+            for (uint32_t rem = __ballot_sync(0xffffffffu, ld >= 0); rem;) {
+                const int l = __ffs(rem) - 1;
+                const uint32_t g = __shfl_sync(0xffffffffu, grp, l);
+                rem &= ~g;
+                if ((g >> lane) & 1u) {
+                    const uint32_t fm = __reduce_max_sync(g, __float_as_uint(fabsf(f)));
+                    if (lane == l) atomicMax(&s.maxf[ld], fm);
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) {
+                        const uint32_t m = __reduce_max_sync(g, float_key_asc(da[t]));
+                        if (lane == l) atomicMax(&s.mx[ld][t], m);
                     }
-                    cur = ld;
-                    run = -INFINITY;
-                    runf = 0.0f;
                 }
-                run = fmaxf(run, v);
-                runf = fmaxf(runf, fa);
-            }
-            if (cur >= 0) {
-                atomicMax(&s.mx[cur][lane], float_key_asc(run));
-                if (lane == 0) atomicMax(&s.maxf[cur], __float_as_uint(runf));
             }
         }
         __syncthreads();
         // ---- pass 2: candidates.  Every row's exact dist is within M =
         // max|f| * em of its estimate, so the max row's estimate is at least
         // (max estimate) - 2M.
-        {
-            const float em = s.em[lane];
-            int cur = -1;
-            float thr = 0.0f;
-            for (int i = 0; i < nrow; ++i) {
-                const int row = w0 + i;
-                const int ld = s.row_doc[buf][row];
-                if (ld != cur) {
-                    cur = ld;
-                    const float M = __fmul_ru(__uint_as_float(s.maxf[ld]), em);
-                    thr = __fsub_rd(key_to_float_asc(s.mx[ld][lane]), __fadd_ru(M, M));
-                }
-                const bool c = s.da[row][lane] >= thr;
-                const uint32_t mask = __ballot_sync(0xffffffffu, c);
-                if (mask) {
-                    int base = 0;
-                    if (lane == __ffs(mask) - 1) base = atomicAdd(&s.n_cand, __popc(mask));
-                    base = __shfl_sync(0xffffffffu, base, __ffs(mask) - 1);
-                    const int at = base + __popc(mask & ((1u << lane) - 1));
-                    if (c && at < kRtMaxCand) s.cand[at] = ((uint32_t)row << 5) | (uint32_t)lane;
+        if (ld >= 0) {
+            const float mf = __uint_as_float(s.maxf[ld]);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+                const float M = __fmul_ru(mf, s.em[t]);
+                const float thr = __fsub_rd(key_to_float_asc(s.mx[ld][t]), __fadd_ru(M, M));
+                if (da[t] >= thr) {
+                    const int at = atomicAdd(&s.n_cand, 1);
+                    if (at < kRtMaxCand) s.cand[at] = ((uint32_t)tid << 5) | (uint32_t)t;
                 }
             }
         }
