@@ -127,7 +127,11 @@ def main():
     ap.add_argument("--recall-queries", type=int, default=32)
     ap.add_argument("--cpu-sample", type=int, default=4, help="queries timed on the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", choices=["probe"], default=None,
+                    help="operator microbench (BASELINE config C2) instead of the search bench")
     args = ap.parse_args()
+    if args.micro == "probe":
+        return micro_probe(args)
 
     import torch
     from chimera_b200 import capi, workloads as W, sharded as SH
@@ -312,6 +316,67 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def micro_probe(args):
+    """C2 centroid-probe microbench: 1,024 queries x 32 tokens of unit-norm
+    random vectors against 262,144 unit-norm random centroids, exact top-128
+    per token through chm_probe_tc (bf16 tcgen05 candidates, exact fp32
+    re-rank).  One step = the whole 32,768-row batch."""
+    import ctypes as C
+    import torch
+    from chimera_b200 import capi
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rows, nc, nprobe = 1024 * 32, 262144, 128
+    q = torch.randn(rows, 128, device="cuda", generator=g)
+    q /= q.norm(dim=1, keepdim=True)
+    cents = torch.randn(nc, 128, device="cuda", generator=g)
+    cents /= cents.norm(dim=1, keepdim=True)
+    L, P, st = capi.lib(), capi._ptr, capi._stream(torch)
+    cn = torch.empty(nc, device="cuda")
+    capi.check(L.chm_row_norms(P(cents), nc, P(cn), st), "norms")
+    cb = torch.empty(nc, 128, dtype=torch.bfloat16, device="cuda")
+    capi.check(L.chm_to_bf16(P(cents), nc * 128, P(cb), st), "bf16")
+    cmax = torch.empty(1, device="cuda")
+    capi.check(L.chm_max_value(P(cn), nc, P(cmax), st), "max")
+    labels = torch.empty(rows, nprobe, dtype=torch.int32, device="cuda")
+    wb = L.chm_probe_tc_workspace_bytes(rows, nc, nprobe)
+    ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
+    run = lambda: capi.check(L.chm_probe_tc(P(q), rows, P(cents), P(cb), P(cn), P(cmax), nc, nprobe, P(labels),
+                                            P(ws), wb, st), "probe_tc")
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        torch.cuda.synchronize()
+        e0.record(torch.cuda.current_stream())
+        for _ in range(args.steps):
+            run()
+        e1.record(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = 2.0 * rows * nc * 128
+    tf = flops / (ms / 1e3) / 1e12
+    hbm, bf16, kind = peaks()
+    # exactness spot check against a fp32 brute force on a few rows
+    sel = torch.arange(0, rows, rows // 16, device="cuda")
+    d = cn[None, :] - 2.0 * (q[sel] @ cents.T)
+    ref = torch.topk(-d, nprobe, dim=1).indices.sort(dim=1).values
+    got = labels[sel].long().sort(dim=1).values
+    agree = float((ref == got).float().mean().item())
+    print(json.dumps({"metric": "centroid probe TFLOP/s (C2 operator microbench)", "value": round(tf, 2),
+                      "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(ms, 3), "higher_is_better": True, "dtype": "bf16 candidates + fp32 re-rank",
+                      "data": "synthetic",
+                      "config": {"workload": "C2: 1,024 queries x 32 tokens x 128 dims vs 262,144 centroids, top-128",
+                                 "rows": rows, "centroids": nc, "nprobe": nprobe,
+                                 "top128_agreement_with_torch_fp32": agree},
+                      "roofline": {"kernel": "chm_probe_tc (all launches)", "bound": "tensor", "achieved": round(tf, 2),
+                                   "peak": bf16, "unit": "TFLOP/s", "frac": round(tf / bf16, 4), "traffic": None,
+                                   "peak_kind": kind},
+                      "clocks": clk.summary()}), flush=True)
 
 
 def profile_stages(torch, capi, index, searcher, q, cfg):
