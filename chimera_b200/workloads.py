@@ -62,6 +62,9 @@ CONFIGS = {
     # large sharded corpus
     "c5": Config("c5", 8_800_000, ("normal", 68, 22, 8, 180), 65536, 8192, 4_194_304, 4, 128,
                  3000, 300),
+    # C3's per-query shape (mean list length 244, nprobe 128, k_refine 3000) on 1/8 of its corpus:
+    # the small case for full ncu captures (about 1 GB on the device)
+    "c3s": Config("c3s", 125_000, ("normal", 64, 20, 8, 180), 2048, 128, 32768, 4, 128, 3000, 300),
     # test-sized corpora with the same recipe
     "mini": Config("mini", 300, ("normal", 64, 20, 8, 180), 64, 6, 128, 4, 16, 60, 20, 5, 10),
     "small": Config("small", 2000, ("normal", 64, 20, 8, 180), 256, 16, 512, 4, 24, 300, 60,
