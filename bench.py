@@ -88,6 +88,12 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+# DRAM bytes per unit of work of the dominant kernel, from the full ncu capture
+# in profiles/c3s_b32_top_kernels_full.md (c3s corpus, 32 queries: 862 MB read +
+# written for 8.63 M refined tokens), scaled here by this run's refined tokens.
+NCU_TRAFFIC_PER_UNIT = {"refine_1bit": 99.9}
+
+
 def peaks():
     try:
         p = json.load(open(PEAKS))
@@ -302,7 +308,11 @@ def main():
                 "h2d_bytes_per_step": int(world * B * 32 * cfg.dim * 4), "d2h_bytes_per_step": int(world * B * cfg.k * 8)},
         "roofline": {"kernel": dom["name"], "bound": dom["bound"], "achieved": round(achieved, 2),
                      "peak": peak, "unit": "GB/s" if dom["bound"] == "hbm" else "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": kind},
+                     "frac": round(achieved / peak, 4),
+                     "traffic": (round(NCU_TRAFFIC_PER_UNIT[dom["name"]] * dom["units"])
+                                 if dom["name"] in NCU_TRAFFIC_PER_UNIT and dom.get("units") else None),
+                     "traffic_source": "ncu capture of the c3s case scaled by units (profiles/c3s_b32_top_kernels_full.md)",
+                     "peak_kind": kind},
         "stages_ms_per_step": {s["name"]: round(s["ms"], 3) for s in stages},
         "stages_algo_gbs": {s["name"]: round(s["algo_bytes"] / (s["ms"] / 1e3) / 1e9, 1)
                             for s in stages if s["algo_bytes"]},
@@ -475,6 +485,7 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
             s["algo_bytes"] = uniq_bytes
         elif n == "refine_1bit":
             s["algo_bytes"] = ref_tok * 24
+            s["units"] = ref_tok
         elif n == "fullbit":
             s["algo_bytes"] = fb_tok * (16 * w + 4)
         out.append(s)
