@@ -546,9 +546,14 @@ def run_reference(args, cfg, index, queries, torch):
         if i >= warm:
             vals.append(r["value"])
     v = float(np.mean(vals))
+    n_tok = int(index.n_tokens)
     line = {"impl": "reference", "metric": "QPS at Recall@100 (C3 passage corpus)", "value": round(v, 4),
-            "unit": "queries/s", "n_gpus": 1, "steps": steps, "warmup": warm, "higher_is_better": True,
-            "data": "synthetic", "config": {"workload": cfg.name},
+            "unit": "queries/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": warm,
+            "higher_is_better": True, "data": "synthetic",
+            "config": {"workload": f"{cfg.name}: {cfg.num_docs} docs, {n_tok} tokens, {cfg.n_clusters} clusters, "
+                                   f"ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, k_refine {cfg.k_refine}, "
+                                   f"k_full_bit {cfg.k_full_bit}, k {cfg.k}",
+                       "implementation": "CPU restatement of the search path on the host cores (rank 0)"},
             "cpu_baseline": {"value": round(v, 4), "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
                              "sample": f"{per} queries per step"},
             "e2e": {"value": round(v, 4), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
