@@ -38,7 +38,9 @@ namespace chm {
 
 constexpr int kTM = 128, kTN = 128, kK = 128;
 constexpr int kStages = 4;
-constexpr int kTcThreads = 256;
+// warp 0 TMA, warp 1 MMA, warps 4-7 and 8-11 two epilogue groups that drain
+// alternate accumulators (one group for the top-16 mode)
+constexpr int kTcThreads = 384;
 constexpr int kBoxBytes = 128 * 64 * 2;             // one 128 x 64 bf16 TMA box
 constexpr int kTileBytes = 2 * kBoxBytes;           // 128 x 128 bf16
 constexpr int kTopA = 16;                           // assignment candidates per row
@@ -68,8 +70,9 @@ struct TcSmem {
     alignas(1024) uint8_t b[kStages][kTileBytes];
     uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, mma_done;
     uint32_t tmem_base;
-    float cn[2][kTN];   // per-tile ||c||^2, double-buffered for the epilogue warps
-    float pass[4][32][33];  // per-lane copy of 32 values whose mask has set bits
+    float cn[2][2][kTN];        // per-tile ||c||^2: [epilogue group][double buffer]
+    float pass[2][4][32][33];   // per-lane copy of 32 values whose mask has set bits
+    int rowcnt[kTM];            // filter: survivors appended per row (both groups)
 };
 
 __device__ __forceinline__ uint64_t dist_key(float d, uint32_t col) {
@@ -106,6 +109,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
         sm100::tmem_alloc(&s.tmem_base, 256);
         sm100::tmem_relinquish();
     }
+    if (threadIdx.x < kTM) s.rowcnt[threadIdx.x] = 0;
     sm100::tc_fence_before();
     __syncthreads();
     sm100::tc_fence_after();
@@ -159,106 +163,118 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
         // all issued MMAs complete before TMEM is released
         sm100::mma_commit(&s.mma_done);
         if (!sm100::mbar_wait(&s.mma_done, 0)) failed = true;
-    } else if (warp >= 4) {
+    } else if (warp >= 4 && (MODE != kTop16 || warp < 8)) {
         // ---- epilogue: TMEM -> registers -> filter / store / top-16 ----
-        const int q4 = warp - 4;
-        const int64_t row = row0 + q4 * 32 + lane;
+        // group g drains the tiles it = g, g + ngroups, ...; with two groups
+        // that is accumulator buffer g, so the two run side by side
+        constexpr int ngroups = (MODE == kTop16) ? 1 : 2;
+        const int g = (warp - 4) >> 2;
+        const int q4 = (warp - 4) & 3;  // TMEM lane quarter: warp % 4
+        const int rl = q4 * 32 + lane;  // row within the tile
+        const int64_t row = row0 + rl;
         const bool vrow = row < p.rows;
         float tau = -INFINITY;
         if (MODE == kFilter && vrow) tau = p.tau[row];
-        int cnt = 0;
         uint64_t best[kTopA];
         if (MODE == kTop16) {
 #pragma unroll
             for (int j = 0; j < kTopA; ++j) best[j] = ~0ull;
         }
-        const int et = threadIdx.x - 128;                       // 0..127 within the epilogue
+        const int et = q4 * 32 + lane;                          // 0..127 within the group
         float thr = INFINITY;                                   // kTop16: float of best[15]
-        for (int it = 0; it < n_tiles; ++it) {
+        float* row_vals = s.pass[g][q4][lane];
+        for (int it = g; it < n_tiles; it += ngroups) {
             const int buf = it & 1;
+            const int nb = (it / ngroups) & 1;                  // this group's norms buffer
             const int64_t n0 = (int64_t)(t_begin + it) * kTN;
-            // stage this tile's norms (other warps may still read the other buffer)
-            s.cn[buf][et] = (n0 + et < p.cols) ? __ldg(p.cn + n0 + et) : INFINITY;
-            // every epilogue warp passes this barrier once per tile, also after a
-            // failed wait, so the barrier count stays equal across warps
-            sm100::named_bar(1, 128);
+            // stage this tile's norms (the group's other buffer may still be read)
+            s.cn[g][nb][et] = (n0 + et < p.cols) ? __ldg(p.cn + n0 + et) : INFINITY;
+            // every warp of the group passes this barrier once per tile, also
+            // after a failed wait, so the barrier count stays equal across warps
+            sm100::named_bar(1 + g, 128);
             if (failed) continue;
             // warp-uniform wait: the tcgen05.ld below needs every lane
             const bool ok = __all_sync(0xffffffffu, sm100::mbar_wait(&s.acc_full[buf], (it >> 1) & 1));
             if (!ok) { failed = true; continue; }
             sm100::tc_fence_after();
-            uint32_t r[4][32];
+            const float* cnb = s.cn[g][nb];
             const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + buf * kTN;
+            // two halves of 64 columns keep 64 accumulators in registers at a time
 #pragma unroll
-            for (int c = 0; c < 4; ++c) sm100::tmem_ld32_async(tbase + c * 32, r[c]);
-            sm100::tmem_wait_ld();
-            // the accumulator is in registers: hand TMEM back to the MMA warp
-            sm100::tc_fence_before();
-            sm100::mbar_arrive(&s.acc_empty[buf]);
-            if (!vrow) continue;
-            const float* cnb = s.cn[buf];
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r[2][32];
+                sm100::tmem_ld32_async(tbase + h * 64, r[0]);
+                sm100::tmem_ld32_async(tbase + h * 64 + 32, r[1]);
+                sm100::tmem_wait_ld();
+                if (h == 1) {
+                    // the accumulator is in registers: hand TMEM back to the MMA warp
+                    sm100::tc_fence_before();
+                    sm100::mbar_arrive(&s.acc_empty[buf]);
+                }
+                if (!vrow) continue;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                if (MODE == kStore) {
-                    float* out = p.dist + row * p.ld + n0 + c * 32;
-                    if (n0 + c * 32 + 32 <= p.cols && (p.ld & 3) == 0) {
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int c = 2 * h + cc;
+                    if (MODE == kStore) {
+                        float* out = p.dist + row * p.ld + n0 + c * 32;
+                        if (n0 + c * 32 + 32 <= p.cols && (p.ld & 3) == 0) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 o;
-                            o.x = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 0]), cnb[c * 32 + j + 0]);
-                            o.y = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 1]), cnb[c * 32 + j + 1]);
-                            o.z = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 2]), cnb[c * 32 + j + 2]);
-                            o.w = __fmaf_rn(-2.0f, __uint_as_float(r[c][j + 3]), cnb[c * 32 + j + 3]);
-                            *reinterpret_cast<float4*>(out + j) = o;
+                            for (int j = 0; j < 32; j += 4) {
+                                float4 o;
+                                o.x = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 0]), cnb[c * 32 + j + 0]);
+                                o.y = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 1]), cnb[c * 32 + j + 1]);
+                                o.z = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 2]), cnb[c * 32 + j + 2]);
+                                o.w = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 3]), cnb[c * 32 + j + 3]);
+                                *reinterpret_cast<float4*>(out + j) = o;
+                            }
+                        } else {
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + c * 32 + j < p.cols)
+                                    out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j]), cnb[c * 32 + j]);
                         }
                     } else {
-                        for (int j = 0; j < 32; ++j)
-                            if (n0 + c * 32 + j < p.cols)
-                                out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[c][j]), cnb[c * 32 + j]);
-                    }
-                } else {
-                    // Branch-free pass over the 32 values: bit j set when column
-                    // j can enter (d <= tau for the filter, d <= the current
-                    // 16th best for the top-16).  d = cn - 2 v is exact in one
-                    // fma because 2 v is exact.  Out-of-range columns carry +inf
-                    // norms and never pass.
-                    const float lim = (MODE == kFilter) ? tau : thr;
-                    uint32_t mask = 0;
+                        // Branch-free pass over the 32 values: bit j set when column
+                        // j can enter (d <= tau for the filter, d <= the current
+                        // 16th best for the top-16).  d = cn - 2 v is exact in one
+                        // fma because 2 v is exact.  Out-of-range columns carry +inf
+                        // norms and never pass.
+                        const float lim = (MODE == kFilter) ? tau : thr;
+                        uint32_t mask = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float d = __fmaf_rn(-2.0f, __uint_as_float(r[c][j]), cnb[c * 32 + j]);
-                        mask |= (d <= lim ? 1u : 0u) << j;
-                    }
-                    if (mask) {
-                        // rare: copy the 32 values to this lane's shared row and
-                        // walk the set bits with a runtime index (keeps the hot
-                        // loop small and r[][] in registers)
-                        float* row_vals = s.pass[q4][lane];
+                        for (int j = 0; j < 32; ++j) {
+                            const float d = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j]), cnb[c * 32 + j]);
+                            mask |= (d <= lim ? 1u : 0u) << j;
+                        }
+                        if (mask) {
+                            // rare: copy the 32 values to this lane's shared row and
+                            // walk the set bits with a runtime index (keeps the hot
+                            // loop small and r[][] in registers)
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) row_vals[j] = __uint_as_float(r[c][j]);
-                        while (mask) {
-                            const int j = __ffs(mask) - 1;
-                            mask &= mask - 1;
-                            const float d = __fmaf_rn(-2.0f, row_vals[j], cnb[c * 32 + j]);
-                            const uint32_t col = (uint32_t)(n0 + c * 32 + j);
-                            if (MODE == kFilter) {
-                                if (cnt < p.cap)
-                                    p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + cnt] = dist_key(d, col);
-                                ++cnt;
-                            } else {
-                                const uint64_t key = dist_key(d, col);
-                                if (key < best[kTopA - 1]) {
-                                    best[kTopA - 1] = key;
+                            for (int j = 0; j < 32; ++j) row_vals[j] = __uint_as_float(r[cc][j]);
+                            while (mask) {
+                                const int j = __ffs(mask) - 1;
+                                mask &= mask - 1;
+                                const float d = __fmaf_rn(-2.0f, row_vals[j], cnb[c * 32 + j]);
+                                const uint32_t col = (uint32_t)(n0 + c * 32 + j);
+                                if (MODE == kFilter) {
+                                    const int at = atomicAdd(&s.rowcnt[rl], 1);  // shared by both groups
+                                    if (at < p.cap)
+                                        p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + at] = dist_key(d, col);
+                                } else {
+                                    const uint64_t key = dist_key(d, col);
+                                    if (key < best[kTopA - 1]) {
+                                        best[kTopA - 1] = key;
 #pragma unroll
-                                    for (int q = kTopA - 1; q > 0; --q) {
-                                        if (best[q] < best[q - 1]) {
-                                            const uint64_t t = best[q];
-                                            best[q] = best[q - 1];
-                                            best[q - 1] = t;
+                                        for (int q = kTopA - 1; q > 0; --q) {
+                                            if (best[q] < best[q - 1]) {
+                                                const uint64_t t = best[q];
+                                                best[q] = best[q - 1];
+                                                best[q - 1] = t;
+                                            }
                                         }
+                                        if (best[kTopA - 1] != ~0ull)
+                                            thr = key_to_float_asc((uint32_t)(best[kTopA - 1] >> 32));
                                     }
-                                    if (best[kTopA - 1] != ~0ull)
-                                        thr = key_to_float_asc((uint32_t)(best[kTopA - 1] >> 32));
                                 }
                             }
                         }
@@ -266,18 +282,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
                 }
             }
         }
-        if (vrow) {
-            if (MODE == kFilter) p.surv_cnt[(size_t)row * p.splits + blockIdx.x] = cnt;
-            if (MODE == kTop16) {
+        if (MODE == kTop16 && vrow) {
 #pragma unroll
-                for (int j = 0; j < kTopA; ++j) p.top[((size_t)row * p.splits + blockIdx.x) * kTopA + j] = best[j];
-            }
+            for (int j = 0; j < kTopA; ++j) p.top[((size_t)row * p.splits + blockIdx.x) * kTopA + j] = best[j];
         }
     }
     if (failed) atomicOr(p.err, 1u);
     sm100::tc_fence_before();
     __syncthreads();
     sm100::tc_fence_after();
+    // filter: both groups have appended; the first group's threads publish the counts
+    if (MODE == kFilter && warp >= 4 && warp < 8) {
+        const int rl = (warp - 4) * 32 + lane;
+        if (row0 + rl < p.rows) p.surv_cnt[(size_t)(row0 + rl) * p.splits + blockIdx.x] = s.rowcnt[rl];
+    }
     if (warp == 1) sm100::tmem_dealloc(tmem, 256);
 }
 
