@@ -40,10 +40,11 @@ struct KthState {
     uint32_t prefix, need;
 };
 
-// Key of the k-th smallest value and how many values equal to it are needed
-// to complete the k smallest (key order == float order).
-__device__ inline void block_kth_key(const float* d, int64_t cols, int k, KthState& s, uint32_t* kth,
-                                     uint32_t* need_eq) {
+// The k-th smallest of the 32-bit keys key_at(0..cols) and how many keys
+// equal to it are needed to complete the k smallest (blockDim >= 256).
+template <typename KeyAt>
+__device__ inline void block_kth_key_of(KeyAt key_at, int64_t cols, int k, KthState& s, uint32_t* kth,
+                                        uint32_t* need_eq) {
     if (threadIdx.x == 0) { s.prefix = 0; s.need = (uint32_t)k; }
     uint32_t pmask = 0;
     for (int sh = 24; sh >= 0; sh -= 8) {
@@ -51,7 +52,7 @@ __device__ inline void block_kth_key(const float* d, int64_t cols, int k, KthSta
         __syncthreads();
         const uint32_t prefix = s.prefix;
         for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
-            const uint32_t key = float_key_asc(d[i]);
+            const uint32_t key = key_at(i);
             if ((key & pmask) == prefix) atomicAdd(&s.hist[(key >> sh) & 255], 1u);
         }
         __syncthreads();
@@ -85,6 +86,13 @@ __device__ inline void block_kth_key(const float* d, int64_t cols, int k, KthSta
     *kth = s.prefix;
     *need_eq = s.need;
     __syncthreads();
+}
+
+// Key of the k-th smallest value and how many values equal to it are needed
+// to complete the k smallest (key order == float order).
+__device__ inline void block_kth_key(const float* d, int64_t cols, int k, KthState& s, uint32_t* kth,
+                                     uint32_t* need_eq) {
+    block_kth_key_of([d](int64_t i) { return float_key_asc(d[i]); }, cols, k, s, kth, need_eq);
 }
 
 // The k (<= CHM_MAX_NPROBE) smallest (value, id) of d[0..cols), nearest

@@ -392,14 +392,41 @@ __global__ void __launch_bounds__(kRerankThreads) probe_rerank_kernel(
         if (threadIdx.x == 0) fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
         return;
     }
+    const int m = min(kc, total);
+    // Only the m + 1 smallest (approx dist, id) keys matter: a radix select
+    // of the (m+1)-th smallest dist, an order-keeping compaction of every key
+    // up to it (ties included), and a sort of those give the same first
+    // m + 1 keys as sorting them all.
+    int n_sel = total;
+    if (total > m + 1) {
+        __shared__ KthState ks;
+        uint32_t kth, need_eq;
+        block_kth_key_of([](int64_t i) { return (uint32_t)(s_keys[i] >> 32); }, total, m + 1, ks, &kth, &need_eq);
+        __shared__ uint32_t s_warp[33];
+        __shared__ int s_kept;
+        if (threadIdx.x == 0) s_kept = 0;
+        __syncthreads();
+        for (int base = 0; base < total; base += blockDim.x) {
+            const int i = base + threadIdx.x;
+            const uint64_t key = i < total ? s_keys[i] : ~0ull;
+            const uint32_t keep = i < total && (uint32_t)(key >> 32) <= kth;
+            uint32_t tot;
+            const uint32_t r = blk_scan_excl(keep, s_warp, &tot);  // synchronises: reads before writes
+            const int kept = s_kept;
+            if (keep) s_keys[kept + (int)r] = key;  // kept + r <= i: in place
+            __syncthreads();
+            if (threadIdx.x == 0) s_kept = kept + (int)tot;
+            __syncthreads();
+        }
+        n_sel = s_kept;
+    }
     int n = 1;
-    while (n < total) n <<= 1;
-    for (int i = total + threadIdx.x; i < n; i += blockDim.x) s_keys[i] = ~0ull;
+    while (n < n_sel) n <<= 1;
+    for (int i = n_sel + threadIdx.x; i < n; i += blockDim.x) s_keys[i] = ~0ull;
     __syncthreads();
     bitonic_asc(s_keys, n);
-    const int m = min(kc, total);
     // the smallest approximate dist left out of the candidate set
-    const float a_star = (total > m) ? key_to_float_asc((uint32_t)(s_keys[m] >> 32)) : tau[row];
+    const float a_star = (total > m) ? key_to_float_asc((uint32_t)(s_keys[m] >> 32)) : tau[row];  // (m+1)-th
     float qn = 0.0f;
     for (int k = 0; k < kDim; ++k) qn = fmaf(s_q[k], s_q[k], qn);
     const float e = err_bound(sqrtf(qn), *cnmax);
