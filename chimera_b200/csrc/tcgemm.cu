@@ -581,8 +581,10 @@ static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
     p.nc = nc;
     p.nprobe = nprobe;
     p.kc = std::min<int64_t>(nc, std::min(512, nprobe + 64));
-    // prefix sample large enough that ~8x kc centroids survive on average
-    p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, nc / 8));
+    // prefix sample such that ~16x kc centroids survive on average (about
+    // 3,100 of the 4,096 a re-rank row holds); a larger sample costs more in
+    // the threshold pass than it saves in the re-rank
+    p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, nc / 16));
     p.prefix = (int)std::min<int64_t>(nc, ((p.prefix + kTN - 1) / kTN) * kTN);
     const int64_t row_tiles = (rows + kTM - 1) / kTM;
     const int n_tiles = (int)((nc + kTN - 1) / kTN);
