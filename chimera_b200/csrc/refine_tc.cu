@@ -53,10 +53,7 @@ struct __align__(1024) RtSmem {
     uint4 code[kFull ? 1 : 2][kRtRows];
     float fac[2][kRtRows];
     int row_doc[2][kRtRows];         // item-local doc of each row
-    int doc_tok0[2][kRtMaxDocs + 1]; // row offsets of the item's docs
-    int64_t doc_first[2][kRtMaxDocs];// first token id of each doc
-    int doc_id[2][kRtMaxDocs];
-    int r0[2], nd[2], ntok[2];
+    int rec[2][40];                  // the item's RtItem record
     uint32_t mx[kRtMaxDocs][32];     // max estimate per (doc, query token), ordered keys
     uint32_t maxf[kRtMaxDocs];       // max |factor| per doc (float bits, >= 0)
     uint32_t exact[kRtMaxDocs][32];  // exact max per (doc, query token), ordered keys
@@ -149,26 +146,39 @@ __global__ void refine_plan_kernel(const int64_t* __restrict__ doc_ptrs, const i
     n_big[q] = nb;
 }
 
-// Stage of one item into pipeline buffer `buf`: doc offsets, the rows' codes
-// and factors, the expanded bits, and the MMA into TMEM columns [64 buf, +64).
-// kFull: the (1+ex_bits)-bit codes in token order (full_codes / full_factors,
-// width w), expanded to their integer levels 0..2^w-1; else the 1-bit codes
-// in cluster order (through tok2pos), expanded to 0/1.
-template <bool kFull, int kW>
-__device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, int q, int k_refine,
-                                         const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
-                                         const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
-                                         const int32_t* __restrict__ refined_docs, const int2* __restrict__ items,
-                                         uint32_t tmem) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (warp == 0) {
-        const int2 rr = items[(size_t)q * k_refine + item];
-        const int ndw = rr.y - rr.x;
+// Per-item record, filled in parallel after planning so that staging an item
+// is one coalesced load (plus the rows' codes): row offsets of the item's docs,
+// and which docs belong to another shard (-1 ids).
+struct RtItem {
+    int r0, nd, ntok;
+    uint32_t foreign;            // bit j: doc j of the item is not this shard's
+    int tok0[kRtMaxDocs + 1];
+    int pad[3];
+};
+static_assert(sizeof(RtItem) == 160, "RtItem is 40 words");
+
+// One warp per item: its record and, per row, the code index (the cluster
+// position through tok2pos for 1-bit codes, the token id for full codes).
+template <bool kFull>
+__global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
+                               const int32_t* __restrict__ docs, int cap, const int2* __restrict__ items,
+                               const int32_t* __restrict__ n_items, RtItem* __restrict__ meta,
+                               uint32_t* __restrict__ rows) {
+    const int q = blockIdx.y;
+    const int lane = threadIdx.x & 31;
+    const int NI = n_items[q];
+    // warps stride over the query's items
+    for (int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < NI;
+         item += gridDim.x * (blockDim.x >> 5)) {
+        const int2 rr = items[(size_t)q * cap + item];
+        const int nd = rr.y - rr.x;
         int64_t first = 0;
-        int len = 0, d = -1;
-        if (lane < ndw) {
-            d = refined_docs[(size_t)q * k_refine + rr.x + lane];
-            if (d >= 0) {
+        int len = 0;
+        bool foreign = false;
+        if (lane < nd) {
+            const int64_t d = docs[(size_t)q * cap + rr.x + lane];
+            foreign = d < 0;
+            if (!foreign) {
                 first = doc_ptrs[d];
                 len = (int)(doc_ptrs[d + 1] - first);
             }
@@ -179,21 +189,59 @@ __device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, in
             const int y = __shfl_up_sync(0xffffffffu, incl, off);
             if (lane >= off) incl += y;
         }
-        if (lane < ndw) {
-            s.doc_first[buf][lane] = first;
-            s.doc_tok0[buf][lane + 1] = incl;
-            s.doc_id[buf][lane] = d;
-        }
-        const int tot = __shfl_sync(0xffffffffu, incl, ndw - 1);
+        const int ntok = __shfl_sync(0xffffffffu, incl, 31);
+        const uint32_t fmask = __ballot_sync(0xffffffffu, foreign);
+        RtItem* m = meta + (size_t)q * cap + item;
         if (lane == 0) {
-            s.doc_tok0[buf][0] = 0;
-            s.r0[buf] = rr.x;
-            s.nd[buf] = ndw;
-            s.ntok[buf] = tot;
+            m->r0 = rr.x;
+            m->nd = nd;
+            m->ntok = ntok;
+            m->foreign = fmask;
+            m->tok0[0] = 0;
+        }
+        m->tok0[lane + 1] = incl;  // docs past nd repeat the total
+        uint32_t* rw = rows + ((size_t)q * cap + item) * kRtRows;
+        for (int r0 = 0; r0 < kRtRows; r0 += 32) {  // uniform: the shuffles below need every lane
+            const int row = r0 + lane;
+            // the row's doc: the first doc whose inclusive end exceeds row
+            int lo = 0, hi = nd;
+#pragma unroll
+            for (int step = 0; step < 6; ++step) {
+                const int mid = (lo + hi) >> 1;
+                const int end = __shfl_sync(0xffffffffu, incl, mid & 31);
+                if (lo < hi) {
+                    if (end <= row) lo = mid + 1; else hi = mid;
+                }
+            }
+            const int ld = min(lo, 31);
+            const int64_t f0 = __shfl_sync(0xffffffffu, first, ld);
+            const int prev_end = __shfl_sync(0xffffffffu, incl, (ld + 31) & 31);  // every lane shuffles
+            const int start = ld > 0 ? prev_end : 0;
+            if (row < ntok) {
+                const int64_t token = f0 + (row - start);
+                rw[row] = kFull ? (uint32_t)token : __ldg(tok2pos + token);
+            }
         }
     }
+}
+// Stage of one item into pipeline buffer `buf`: doc offsets, the rows' codes
+// and factors, the expanded bits, and the MMA into TMEM columns [64 buf, +64).
+// kFull: the (1+ex_bits)-bit codes in token order (full_codes / full_factors,
+// width w), expanded to their integer levels 0..2^w-1; else the 1-bit codes
+// in cluster order (through tok2pos), expanded to 0/1.
+template <bool kFull, int kW>
+__device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, int q, int cap,
+                                         const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows,
+                                         const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
+                                         uint32_t tmem) {
+    const int tid = threadIdx.x;
+    // the item's record (40 words) and this row's code index, both coalesced
+    const int* mw = reinterpret_cast<const int*>(meta + (size_t)q * cap + item);
+    if (tid < 40) s.rec[buf][tid] = __ldg(mw + tid);
+    const uint32_t code_idx = __ldg(rows + ((size_t)q * cap + item) * kRtRows + tid);
     __syncthreads();
-    const int T = s.ntok[buf];
+    const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[buf]);
+    const int T = rec.ntok;
     uint4 code = make_uint4(0, 0, 0, 0);
     float f = 0.0f;
     int ld = -1;
@@ -201,8 +249,8 @@ __device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, in
     if (kFull) {
         if (tid < T) {
             ld = 0;
-            while (s.doc_tok0[buf][ld + 1] <= tid) ++ld;
-            const int64_t token = s.doc_first[buf][ld] + (tid - s.doc_tok0[buf][ld]);
+            while (rec.tok0[ld + 1] <= tid) ++ld;
+            const int64_t token = code_idx;
             constexpr int bytes = kDim * kW / 8;
             // the packed code in registers (16 * kW bytes)
             uint8_t pk[bytes];
@@ -231,11 +279,9 @@ __device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, in
     } else {
         if (tid < T) {
             ld = 0;
-            while (s.doc_tok0[buf][ld + 1] <= tid) ++ld;
-            const int64_t token = s.doc_first[buf][ld] + (tid - s.doc_tok0[buf][ld]);
-            const uint32_t pos = __ldg(tok2pos + token);
-            code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
-            f = __ldg(factor1 + pos);
+            while (rec.tok0[ld + 1] <= tid) ++ld;
+            code = __ldg(reinterpret_cast<const uint4*>(codes1) + code_idx);
+            f = __ldg(factor1 + code_idx);
         }
         s.code[kFull ? 0 : buf][tid] = code;
         s.fac[buf][tid] = f;
@@ -268,11 +314,10 @@ __device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, in
 // else the 1-bit score of refine_1bit_kernel (cb = cb1).
 template <bool kFull, int kW>
 __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
-    const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos, const uint8_t* __restrict__ codes1,
-    const float* __restrict__ factor1, const float* __restrict__ lut, const float* __restrict__ cb1,
-    const float* __restrict__ rot, const int32_t* __restrict__ refined_docs, int k_refine,
-    const int2* __restrict__ items, const int32_t* __restrict__ n_items, float* __restrict__ scores,
-    uint32_t* __restrict__ status, unsigned long long* __restrict__ stats) {
+    const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows, const uint8_t* __restrict__ codes1,
+    const float* __restrict__ factor1, const float* __restrict__ cb1, const float* __restrict__ rot, int k_refine,
+    const int32_t* __restrict__ n_items, float* __restrict__ scores, uint32_t* __restrict__ status,
+    unsigned long long* __restrict__ stats) {
     extern __shared__ uint8_t smem_raw[];
     RtSmem<kFull>& s =
         *reinterpret_cast<RtSmem<kFull>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -358,7 +403,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
     bool failed = false;  // uniform across the CTA (set from __syncthreads_or)
     unsigned long long n_rows = 0, n_cand = 0;
 
-    rt_stage<kFull, kW>(s, 0, blockIdx.x, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items, tmem);
+    rt_stage<kFull, kW>(s, 0, blockIdx.x, q, k_refine, meta, rows, codes1, factor1, tmem);
     int k = 0;
     bool next_issued = false;  // an MMA of item k+1 is in flight
     for (int it = blockIdx.x; it < NI; it += gridDim.x, ++k) {
@@ -366,8 +411,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
         const int nxt = it + gridDim.x;
         next_issued = nxt < NI;
         if (next_issued)  // overlaps this item's MMA and epilogue
-            rt_stage<kFull, kW>(s, buf ^ 1, nxt, q, k_refine, doc_ptrs, tok2pos, codes1, factor1, refined_docs, items,
-                                tmem);
+            rt_stage<kFull, kW>(s, buf ^ 1, nxt, q, k_refine, meta, rows, codes1, factor1, tmem);
         bool ok = true;
         if (tid == 0) ok = sm100::mbar_wait(&s.bar[buf], (uint32_t)((k >> 1) & 1));
         if (__syncthreads_or(!ok)) {
@@ -382,7 +426,8 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
         sm100::tmem_ld32_async(taddr + 32, lo);
         sm100::tmem_wait_ld();
         sm100::tc_fence_before();
-        const int T = s.ntok[buf];
+        const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[buf]);
+        const int T = rec.ntok;
         const int ld = tid < T ? s.row_doc[buf][tid] : -1;
         const float f = tid < T ? s.fac[buf][tid] : 0.0f;
         float da[32];
@@ -464,7 +509,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
         n_cand += (unsigned long long)(tid == 0 ? nc : 0);
         __syncthreads();
         // ---- document scores: the reference's 128-thread tree (kernels.cu:557-570)
-        const int nd = s.nd[buf];
+        const int nd = rec.nd;
         for (int j = warp; j < nd; j += kRtThreads / 32) {
             const float m = key_to_float_asc(s.exact[j][lane]);
             float x;
@@ -478,7 +523,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
 #pragma unroll
                 for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
             }
-            if (lane == 0) scores[(size_t)q * k_refine + s.r0[buf] + j] = s.doc_id[buf][j] < 0 ? -INFINITY : x;
+            if (lane == 0) scores[(size_t)q * k_refine + rec.r0 + j] = ((rec.foreign >> j) & 1u) ? -INFINITY : x;
             s.mx[j][lane] = 0u;
             s.exact[j][lane] = float_key_asc(kFull ? -INFINITY : -FLT_MAX);
             if (lane == 0) s.maxf[j] = 0u;
@@ -518,15 +563,55 @@ namespace chm {
 template <bool kFull>
 size_t refine_tc_smem_bytes() { return sizeof(RtSmem<kFull>) + 1024; }
 
+// Workspace of one tensor-core refinement call.
+struct RtWork {
+    int2* items;
+    int32_t* n_items;
+    uint32_t* status;
+    unsigned long long* stats;
+    int32_t* big;
+    int32_t* n_big;
+    RtItem* meta;
+    uint32_t* rows;
+};
+
+template <typename A>
+static void rt_layout(A& a, int nq, int cap, RtWork* w) {
+    auto items = a.template take<int2>((size_t)nq * cap);
+    auto n_items = a.template take<int32_t>((size_t)nq);
+    auto status = a.template take<uint32_t>((size_t)nq);
+    auto stats = a.template take<unsigned long long>(2);  // rows scored, exact candidates (last call)
+    auto big = a.template take<int32_t>((size_t)nq * cap);
+    auto n_big = a.template take<int32_t>((size_t)nq);
+    auto meta = a.template take<RtItem>((size_t)nq * cap);
+    auto rows = a.template take<uint32_t>((size_t)nq * cap * kRtRows);
+    if (w) *w = RtWork{(int2*)items, (int32_t*)n_items, (uint32_t*)status, (unsigned long long*)stats,
+                       (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint32_t*)rows};
+}
+
+struct RtSizer {
+    Sizer s;
+    template <typename T>
+    void* take(size_t n) {
+        s.take<T>(n);
+        return nullptr;
+    }
+};
+
+template <bool kFull>
 static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, const int32_t* counts, int cap,
-                          int2* items, int32_t* n_items, int32_t* big, int32_t* n_big, uint32_t* status,
-                          unsigned long long* stats, cudaStream_t st) {
-    refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(status, nq, stats);
+                          const RtWork& w, cudaStream_t st) {
+    refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(w.status, nq, w.stats);
     CHM_TRY(launch_status("refine_status_clear_kernel"));
     const size_t plan_smem = sizeof(int) * (size_t)cap;
     CHM_CUDA(cudaFuncSetAttribute(refine_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem));
-    refine_plan_kernel<<<nq, 256, plan_smem, st>>>(idx->doc_ptrs, docs, counts, cap, items, n_items, big, n_big);
-    return launch_status("refine_plan_kernel");
+    refine_plan_kernel<<<nq, 256, plan_smem, st>>>(idx->doc_ptrs, docs, counts, cap, w.items, w.n_items, w.big,
+                                                   w.n_big);
+    CHM_TRY(launch_status("refine_plan_kernel"));
+    // one warp per item, 4 warps per block, 32 blocks per query striding over its items
+    rt_fill_kernel<kFull><<<dim3(32u, (unsigned)nq), 128, 0, st>>>(
+        idx->doc_ptrs, idx->tok2pos, docs, cap, w.items, w.n_items, w.meta, w.rows);
+    return launch_status("rt_fill_kernel");
 }
 
 static dim3 rt_grid(int nq, int cap) {
@@ -538,14 +623,12 @@ static dim3 rt_grid(int nq, int cap) {
 }
 
 template <int kW>
-static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex,
-                                   const int32_t* fb_docs, int fb_cap, const int2* items, const int32_t* n_items,
-                                   float* scores, uint32_t* status, unsigned long long* stats, cudaStream_t st) {
+static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex, int fb_cap,
+                                   const RtWork& w, float* scores, cudaStream_t st) {
     const size_t smem = refine_tc_smem_bytes<true>();
     CHM_CUDA(cudaFuncSetAttribute(refine_tc_kernel<true, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     refine_tc_kernel<true, kW><<<rt_grid(nq, fb_cap), kRtThreads, smem, st>>>(
-        idx->doc_ptrs, nullptr, idx->full_codes, idx->full_factors, nullptr, cbex, rot, fb_docs, fb_cap, items,
-        n_items, scores, status, stats);
+        w.meta, w.rows, idx->full_codes, idx->full_factors, cbex, rot, fb_cap, w.n_items, scores, w.status, w.stats);
     return launch_status("fullbit_tc_kernel");
 }
 
@@ -574,14 +657,9 @@ static chm_status rescore_flagged_fullbit(const chm_index* idx, int nq, const fl
 }  // namespace chm
 
 extern "C" size_t chm_refine_1bit_tc_workspace_bytes(int32_t nq, int32_t k_refine) {
-    chm::Sizer s;
-    s.take<int2>((size_t)nq * k_refine);
-    s.take<int32_t>((size_t)nq);
-    s.take<uint32_t>((size_t)nq);
-    s.take<unsigned long long>(2);  // rows scored by the tensor-core pass, exact candidates (last call)
-    s.take<int32_t>((size_t)nq * k_refine);
-    s.take<int32_t>((size_t)nq);
-    return s.off;
+    chm::RtSizer s;
+    chm::rt_layout(s, nq, k_refine, nullptr);
+    return s.s.off;
 }
 
 chm_status chm_refine_1bit_complete(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
@@ -596,23 +674,18 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     if (!idx || k_refine <= 0 || k_refine > CHM_MAX_K_REFINE) return CHM_ERR_INVALID;
     cudaStream_t st = (cudaStream_t)stream;
     chm::Arena a(ws, ws_bytes);
-    int2* items = a.take<int2>((size_t)nq * k_refine);
-    int32_t* n_items = a.take<int32_t>((size_t)nq);
-    uint32_t* status = a.take<uint32_t>((size_t)nq);
-    unsigned long long* stats = a.take<unsigned long long>(2);
-    int32_t* big = a.take<int32_t>((size_t)nq * k_refine);
-    int32_t* n_big = a.take<int32_t>((size_t)nq);
+    chm::RtWork w;
+    chm::rt_layout(a, nq, k_refine, &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
-    CHM_TRY(chm::rt_plan(idx, nq, refined_docs, num_refined, k_refine, items, n_items, big, n_big, status, stats, st));
+    CHM_TRY(chm::rt_plan<false>(idx, nq, refined_docs, num_refined, k_refine, w, st));
     const size_t smem = chm::refine_tc_smem_bytes<false>();
     CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
     chm::refine_tc_kernel<false, 1><<<chm::rt_grid(nq, k_refine), chm::kRtThreads, smem, st>>>(
-        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, rot, refined_docs, k_refine, items,
-        n_items, scores, status, stats);
+        w.meta, w.rows, idx->codes1, idx->factor1, cb1, rot, k_refine, w.n_items, scores, w.status, w.stats);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
-    return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, big, n_big,
-                                    status, st);
+    return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, w.big, w.n_big,
+                                    w.status, st);
 }
 
 chm_status chm_fullbit_listed(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
@@ -629,28 +702,24 @@ extern "C" chm_status chm_fullbit_score_tc(const chm_index* idx, int32_t nq, con
     if (nq <= 0) return CHM_OK;
     if (!idx || fb_cap <= 0 || fb_cap > CHM_MAX_K_REFINE) return CHM_ERR_INVALID;
     cudaStream_t st = (cudaStream_t)stream;
-    const int w = 1 + idx->ex_bits;
-    if (w < 2 || w > 7)  // levels up to 255 (w = 8) do not fit the signed 8-bit operand
+    const int w_bits = 1 + idx->ex_bits;
+    if (w_bits < 2 || w_bits > 7)  // levels up to 255 (w = 8) do not fit the signed 8-bit operand
         return chm_fullbit_score(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, stream);
     chm::Arena a(ws, ws_bytes);
-    int2* items = a.take<int2>((size_t)nq * fb_cap);
-    int32_t* n_items = a.take<int32_t>((size_t)nq);
-    uint32_t* status = a.take<uint32_t>((size_t)nq);
-    unsigned long long* stats = a.take<unsigned long long>(2);
-    int32_t* big = a.take<int32_t>((size_t)nq * fb_cap);
-    int32_t* n_big = a.take<int32_t>((size_t)nq);
+    chm::RtWork w;
+    chm::rt_layout(a, nq, fb_cap, &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
-    CHM_TRY(chm::rt_plan(idx, nq, fb_docs, num_fb, fb_cap, items, n_items, big, n_big, status, stats, st));
-    switch (w) {
-        case 2: CHM_TRY(chm::launch_fullbit_tc<2>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
-        case 3: CHM_TRY(chm::launch_fullbit_tc<3>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
-        case 4: CHM_TRY(chm::launch_fullbit_tc<4>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
-        case 5: CHM_TRY(chm::launch_fullbit_tc<5>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
-        case 6: CHM_TRY(chm::launch_fullbit_tc<6>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
-        case 7: CHM_TRY(chm::launch_fullbit_tc<7>(idx, nq, rot, cbex, fb_docs, fb_cap, items, n_items, scores, status, stats, st)); break;
+    CHM_TRY(chm::rt_plan<true>(idx, nq, fb_docs, num_fb, fb_cap, w, st));
+    switch (w_bits) {
+        case 2: CHM_TRY(chm::launch_fullbit_tc<2>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
+        case 3: CHM_TRY(chm::launch_fullbit_tc<3>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
+        case 4: CHM_TRY(chm::launch_fullbit_tc<4>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
+        case 5: CHM_TRY(chm::launch_fullbit_tc<5>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
+        case 6: CHM_TRY(chm::launch_fullbit_tc<6>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
+        case 7: CHM_TRY(chm::launch_fullbit_tc<7>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
         default: return CHM_ERR_INVALID;
     }
     // long docs; then every doc of a query whose tensor-core launch failed
-    CHM_TRY(chm_fullbit_listed(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, big, n_big, st));
-    return chm::rescore_flagged_fullbit(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, status, st);
+    CHM_TRY(chm_fullbit_listed(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, w.big, w.n_big, st));
+    return chm::rescore_flagged_fullbit(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, w.status, st);
 }
