@@ -1,31 +1,36 @@
-// 1-bit refinement with a tensor-core filter (same results as
-// refine_1bit_kernel, bit for bit).
+// Refinement with a tensor-core candidate filter: the 1-bit document score
+// (same results as refine_1bit_kernel) and the full-bit document score (same
+// results as fullbit_kernel), bit for bit.
 //
-// The 1-bit document score (one_bit_token_score + one_bit_document_score,
-// kernels.cu:430-575) is, per query token t, the max over the document's
-// tokens of dist = (ip - cb1[t]) * factor with ip the LUT sum in the
-// reference order, then the reference's tree over t.  Only the max matters,
-// so most (token, t) pairs never need their exact LUT sum:
+// Both scores are, per query token t, the max over the document's tokens of
+// dist = (ip - cb[t]) * factor, then a fixed reduction over t (the reference's
+// 128-thread tree, kernels.cu:557-570, or the full-bit 16-lane sum,
+// search_impl.cu:569-572).  ip is the 1-bit LUT sum (kernels.cu:363-373) or
+// the (1+ex_bits)-bit code dot in the AVX-512 lane order (space.hpp:806-851).
+// Only the max matters, so most (token, t) pairs never need the exact ip:
 //
 //  1. int8 tensor-core pass (tcgen05.mma.kind::i8, M=128 tokens, N=64, K=128):
-//     A = the tokens' code bits as 0/1 bytes, B = the query token in 16-bit
-//     fixed point as two int8 limbs (q ~ (256*hi + lo) / 2^14).  The int32
-//     accumulators are exact, so ip_a = (256*acc_hi + acc_lo) / 2^14 differs
-//     from the real inner product by at most E_t = sum_d |q_d - qfix_d/2^14|.
-//  2. With the LUT sum's own rounding (34 fp32 adds, each within 2^-24 of
-//     sum |q_d|) and the roundings of the two dist operations, every token's
-//     exact dist lies in [lo, hi] = dist_a -/+ margin (directed rounding).
-//     A token can hold the max for (doc, t) only if hi >= max over the doc's
-//     tokens of lo; the true max token always passes.
-//  3. Candidates get the exact LUT sum and dist (the same fp32 operations as
-//     refine_1bit_kernel); their max is the exact max.
+//     A = the tokens' code levels as bytes (0/1 bits, or 0..2^w-1), B = the
+//     query token in 16-bit fixed point as two int8 limbs
+//     (q ~ (256*hi + lo) / 2^14).  The int32 accumulators are exact, so the
+//     estimate differs from the real inner product by at most
+//     (2^w - 1) * E_t, E_t = sum_d |q_d - qfix_d/2^14|.
+//  2. With the exact path's own rounding (the LUT sum's 34 adds, or the 8
+//     fmas and 4 tree adds of the lane order), the int->float conversion and
+//     the two dist roundings of both paths, every token's exact dist lies
+//     within M = max|factor| * margin_t of its estimate, so the max token's
+//     estimate is at least (max estimate) - 2M: only tokens above that are
+//     candidates (about one per document and query token).
+//  3. Candidates get the exact ip and dist with the plain kernels' fp32
+//     operations; their max is the exact max.
 //
-// Work items: the refined docs of a query packed greedily into groups of at
-// most 128 tokens and 32 docs (one M tile); docs longer than 128 tokens go to
-// a list that the SIMT kernel scores.  One CTA (4 warps) loops over items with
-// a two-deep pipeline: while item k's accumulators are read out and its docs
-// reduced (warp per doc, lane per query token), item k+1's codes are gathered,
-// expanded and multiplied.
+// Work items: the docs of a query packed greedily into groups of at most 128
+// tokens and 32 docs (one M tile); docs longer than 128 tokens go to a list
+// the SIMT kernels score.  A fill kernel writes per item a record (doc row
+// offsets) and every row's code index, so staging an item is one coalesced
+// load plus the code gather.  One CTA (4 warps, one row per thread) loops over
+// items with a two-deep pipeline: while item k's accumulators are reduced,
+// item k+1's codes are gathered, expanded and multiplied.
 #include "codes.cuh"
 #include "common.cuh"
 #include "sm100.cuh"
