@@ -290,8 +290,8 @@ def main():
     if world == 1:
         launches = sum(s["launches"] for s in stages) + 1  # + chm_search's status fold
     else:
-        # prepare, probe, stage1 (4), merge, 2 x localize, refine, select, full-bit (6), final
-        launches = 1 + probe_launches + 4 + 1 + 2 + 1 + 1 + 6 + 1
+        # prepare, probe, stage1 (4), merge, 2 x localize, refine, select, full-bit (7), final
+        launches = 1 + probe_launches + 4 + 1 + 2 + 1 + 1 + 7 + 1
     line = {
         "metric": "QPS at Recall@100 (C3 passage corpus)",
         "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -439,7 +439,7 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         ("refine_1bit", 1, lambda: L.chm_refine_1bit(v, B, P(lut), P(cb1), P(rd), P(nr), p.k_refine, P(ob), st)),
         ("select_fullbit", 1, lambda: L.chm_select_fullbit(B, P(rd), P(ob), P(nr), p.k_refine, p.k_full_bit,
                                                            p.num_chunks, P(fd), P(nf), p.k_refine, st)),
-        ("fullbit", 6, lambda: L.chm_fullbit_score_tc(v, B, P(rot), P(cbex), P(fd), P(nf), p.k_refine, P(fs),
+        ("fullbit", 7, lambda: L.chm_fullbit_score_tc(v, B, P(rot), P(cbex), P(fd), P(nf), p.k_refine, P(fs),
                                                       P(fbws), fbb, st)),
         ("final_topk", 1, lambda: L.chm_final_topk(B, P(fd), P(fs), P(nf), p.k_refine, p.k, P(res), P(nres), st)),
     ]
