@@ -89,9 +89,10 @@ class ClockSampler:
 
 
 # DRAM bytes per unit of work of the dominant kernel, from the full ncu capture
-# in profiles/c3s_b32_top_kernels_full.md (c3s corpus, 32 queries: 862 MB read +
-# written for 8.63 M refined tokens), scaled here by this run's refined tokens.
-NCU_TRAFFIC_PER_UNIT = {"refine_1bit": 99.9}
+# in profiles/refine_tc_c3s_b32_full.md (c3s corpus, 32 queries: the 1-bit
+# tensor-core refinement read + wrote 865 MB for 8.63 M refined tokens),
+# scaled here by this run's refined tokens.
+NCU_TRAFFIC_PER_UNIT = {"refine_1bit": 100.2}
 
 
 def peaks():
@@ -291,7 +292,8 @@ def main():
         launches = sum(s["launches"] for s in stages) + 1  # + chm_search's status fold
     else:
         # prepare, probe, stage1 (4), merge, 2 x localize, refine, select, full-bit (7), final
-        launches = 1 + probe_launches + 4 + 1 + 2 + 1 + 1 + 7 + 1
+        refine_launches = next(s["launches"] for s in stages if s["name"] == "refine_1bit")
+        launches = 1 + probe_launches + 4 + 1 + 2 + refine_launches + 1 + 7 + 1
     line = {
         "metric": "QPS at Recall@100 (C3 passage corpus)",
         "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -311,7 +313,7 @@ def main():
                      "frac": round(achieved / peak, 4),
                      "traffic": (round(NCU_TRAFFIC_PER_UNIT[dom["name"]] * dom["units"])
                                  if dom["name"] in NCU_TRAFFIC_PER_UNIT and dom.get("units") else None),
-                     "traffic_source": "ncu capture of the c3s case scaled by units (profiles/c3s_b32_top_kernels_full.md)",
+                     "traffic_source": "ncu capture of the c3s case scaled by units (profiles/refine_tc_c3s_b32_full.md)",
                      "peak_kind": kind},
         "stages_ms_per_step": {s["name"]: round(s["ms"], 3) for s in stages},
         "stages_algo_gbs": {s["name"]: round(s["algo_bytes"] / (s["ms"] / 1e3) / 1e9, 1)
@@ -436,6 +438,9 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         ("probe", 6 if use_tc else 2, probe),
         ("stage1", 4, lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe, p.k_refine, P(rd), P(rp),
                                            P(nr), None, P(sws), sb, st)),
+        # chm_search's choice: the tensor-core filter on batches of 16 or more
+        ("refine_1bit", 6, lambda: L.chm_refine_1bit_tc(v, B, P(lut), P(cb1), P(rot), P(rd), P(nr), p.k_refine, P(ob),
+                                                        P(fbws), fbb, st)) if B >= 16 else
         ("refine_1bit", 1, lambda: L.chm_refine_1bit(v, B, P(lut), P(cb1), P(rd), P(nr), p.k_refine, P(ob), st)),
         ("select_fullbit", 1, lambda: L.chm_select_fullbit(B, P(rd), P(ob), P(nr), p.k_refine, p.k_full_bit,
                                                            p.num_chunks, P(fd), P(nf), p.k_refine, st)),

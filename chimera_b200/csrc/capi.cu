@@ -158,12 +158,16 @@ extern "C" chm_status chm_search(const chm_index* idx, const chm_search_params* 
         CHM_TRY(chm::stage1_run(idx, nq, b.lut, b.cb1, b.labels, p->nprobe, p->k_refine,
                                 b.refined_docs, b.refined_partial, b.num_refined, nullptr, b.s1_ws,
                                 b.s1_bytes, st, false, b.flags, p->table_log2_extra));
-        CHM_TRY(chm_refine_1bit(idx, nq, b.lut, b.cb1, b.refined_docs, b.num_refined, p->k_refine,
-                                b.onebit, st));
+        // the tensor-core filters pay off on batches; a few queries are faster
+        // with the plain kernels' single launch (same scores either way)
+        if (nq >= 16)
+            CHM_TRY(chm_refine_1bit_tc(idx, nq, b.lut, b.cb1, b.rot, b.refined_docs, b.num_refined, p->k_refine,
+                                       b.onebit, b.rt_ws, b.rt_bytes, st));
+        else
+            CHM_TRY(chm_refine_1bit(idx, nq, b.lut, b.cb1, b.refined_docs, b.num_refined, p->k_refine,
+                                    b.onebit, st));
         CHM_TRY(chm_select_fullbit(nq, b.refined_docs, b.onebit, b.num_refined, p->k_refine,
                                    p->k_full_bit, p->num_chunks, b.fb_docs, b.num_fb, fb_cap, st));
-        // the tensor-core filter pays off on batches; a few queries are faster
-        // with the plain kernel's single launch (same scores either way)
         if (nq >= 16)
             CHM_TRY(chm_fullbit_score_tc(idx, nq, b.rot, b.cbex, b.fb_docs, b.num_fb, fb_cap, b.fb_scores, b.rt_ws,
                                          b.rt_bytes, st));

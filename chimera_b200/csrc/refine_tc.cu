@@ -40,39 +40,70 @@ namespace chm {
 constexpr int kRtThreads = 128;
 constexpr int kRtRows = 128;         // tokens per tile (MMA M)
 constexpr int kRtN = 64;             // 32 query tokens x {hi, lo} limbs
-constexpr int kRtMaxDocs = 32;       // docs per packed item
-constexpr int kRtTmemCols = 128;  // two pipeline buffers of 64 columns
+constexpr int kRtMaxDocs = 16;       // docs per packed item
+constexpr int kRtTmemCols = 64;      // one accumulator: item k+1's MMA is issued once item k's is read
 constexpr float kFix = 16384.0f;     // fixed-point scale of the query limbs
 // idesc kind::i8: D s32 (bits 4-5 = 2), A s8 (bits 7-9 = 1), B s8 (bits 10-12 = 1), K-major
 constexpr uint32_t kRtIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kRtN >> 3) << 17) |
                               ((uint32_t)(kRtRows >> 4) << 24);
 
 constexpr int kRtMaxCand = 512;      // candidates per tile (more: the query is rescored by the SIMT kernel)
+constexpr uint32_t kRtNoRow = 0xFFFFFFFFu;  // code index of a row past the item's tokens
 
-// kFull: no 1-bit code rows (the exact sums read the expanded tile), which
-// keeps the full-bit variant at three CTAs per SM.
-template <bool kFull>
+// Per-item record, filled in parallel after planning: row offsets of the
+// item's docs, and which docs belong to another shard (-1 ids).
+struct RtItem {
+    int r0, nd, ntok;
+    uint32_t foreign;            // bit j: doc j of the item is not this shard's
+    int tok0[kRtMaxDocs + 1];    // first row of doc j; entries past nd hold ntok
+    int pad[3];
+};
+static_assert(sizeof(RtItem) == 96, "RtItem is six 16-byte chunks");
+constexpr int kRtRecWords = (int)sizeof(RtItem) / 4;
+
+// Pipeline slots.  While item k is reduced, item k+1 is multiplied and item
+// k+2's loads land, so records and factors rotate through three slots (item
+// k in slot k % 3).  The 1-bit exact sums read item k's packed codes: three
+// code slots and one expanded tile.  The full-bit exact sums read item k's
+// expanded tile: two tiles and two code slots.
+template <bool kFull, int kW>
+struct RtShape {
+    static constexpr int kA = kFull ? 2 : 1;
+    static constexpr int kRaw = kFull ? 2 : 3;
+    static constexpr int kRowChunks = kFull ? kW : 1;  // 16-byte chunks of one row's packed code
+};
+
+template <bool kFull, int kW>
 struct __align__(1024) RtSmem {
-    uint8_t a[2][kRtRows * 128];     // token bits, K-major SW128 (two pipeline buffers)
-    uint8_t b[kRtN * 128];           // query limbs, K-major SW128
-    uint4 code[kFull ? 1 : 2][kRtRows];
-    float fac[2][kRtRows];
-    int row_doc[2][kRtRows];         // item-local doc of each row
-    int rec[2][40];                  // the item's RtItem record
-    uint32_t mx[kRtMaxDocs][32];     // max estimate per (doc, query token), ordered keys
+    uint8_t a[RtShape<kFull, kW>::kA][kRtRows * 128];  // code levels as bytes, K-major SW128
+    uint8_t b[kRtN * 128];                              // query limbs, K-major SW128
+    uint4 raw[RtShape<kFull, kW>::kRaw][kRtRows * RtShape<kFull, kW>::kRowChunks];  // packed codes as loaded
+    float fac[3][kRtRows];
+    int row_doc[2][kRtRows];         // item-local doc of each row (-1: past the item's tokens)
+    alignas(16) int rec[3][kRtRecWords];
+    uint32_t mx[kRtMaxDocs][32];     // max estimate per (doc, query token) as an ordered key, then the threshold
     uint32_t maxf[kRtMaxDocs];       // max |factor| per doc (float bits, >= 0)
     uint32_t exact[kRtMaxDocs][32];  // exact max per (doc, query token), ordered keys
     uint32_t cand[kRtMaxCand];       // (row << 5 | t)
     int n_cand;
     float em[32];                    // margin per unit |factor|
     float cb1[32];
-    uint64_t bar[2];
+    uint64_t bar;
     uint32_t tmem_base;
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sm100::smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sm100::smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -91,30 +122,6 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk16) {
 
 // 4 bits -> 4 bytes of 0/1
 __device__ __forceinline__ uint32_t nib_bytes(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
-
-// The LUT sum of lut_ip (kernels.cu:363-373) with each LUT entry rebuilt
-// from the query as precompute_one_bit_lut_kernel builds it (kernels.cu:
-// 402-428: 0.0f plus the set bits' components in ascending order), so the
-// value is the same float.  q: one query token's 128 components.
-__device__ __forceinline__ float lut_ip_from_query(const float* q, uint4 code) {
-    float ip = 0.0f;
-    const uint32_t w[4] = {code.x, code.y, code.z, code.w};
-#pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-            const uint32_t e = (w[qq] >> (n * 4)) & 0xF;
-            const float* qc = q + (qq * 8 + n) * 4;
-            float entry = 0.0f;
-            if (e & 1u) entry = fadd(entry, qc[0]);
-            if (e & 2u) entry = fadd(entry, qc[1]);
-            if (e & 4u) entry = fadd(entry, qc[2]);
-            if (e & 8u) entry = fadd(entry, qc[3]);
-            ip = fadd(ip, entry);
-        }
-    }
-    return ip;
-}
 
 // Greedy packing of each query's refined docs into items (r0, r1); docs
 // longer than one tile are listed for the SIMT kernel.
@@ -151,19 +158,9 @@ __global__ void refine_plan_kernel(const int64_t* __restrict__ doc_ptrs, const i
     n_big[q] = nb;
 }
 
-// Per-item record, filled in parallel after planning so that staging an item
-// is one coalesced load (plus the rows' codes): row offsets of the item's docs,
-// and which docs belong to another shard (-1 ids).
-struct RtItem {
-    int r0, nd, ntok;
-    uint32_t foreign;            // bit j: doc j of the item is not this shard's
-    int tok0[kRtMaxDocs + 1];
-    int pad[3];
-};
-static_assert(sizeof(RtItem) == 160, "RtItem is 40 words");
-
 // One warp per item: its record and, per row, the code index (the cluster
-// position through tok2pos for 1-bit codes, the token id for full codes).
+// position through tok2pos for 1-bit codes, the token id for full codes;
+// kRtNoRow past the item's tokens).
 template <bool kFull>
 __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
                                const int32_t* __restrict__ docs, int cap, const int2* __restrict__ items,
@@ -204,7 +201,7 @@ __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint3
             m->foreign = fmask;
             m->tok0[0] = 0;
         }
-        m->tok0[lane + 1] = incl;  // docs past nd repeat the total
+        if (lane < kRtMaxDocs) m->tok0[lane + 1] = incl;  // docs past nd repeat the total
         uint32_t* rw = rows + ((size_t)q * cap + item) * kRtRows;
         for (int r0 = 0; r0 < kRtRows; r0 += 32) {  // uniform: the shuffles below need every lane
             const int row = r0 + lane;
@@ -222,47 +219,54 @@ __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint3
             const int64_t f0 = __shfl_sync(0xffffffffu, first, ld);
             const int prev_end = __shfl_sync(0xffffffffu, incl, (ld + 31) & 31);  // every lane shuffles
             const int start = ld > 0 ? prev_end : 0;
+            uint32_t v = kRtNoRow;
             if (row < ntok) {
                 const int64_t token = f0 + (row - start);
-                rw[row] = kFull ? (uint32_t)token : __ldg(tok2pos + token);
+                v = kFull ? (uint32_t)token : __ldg(tok2pos + token);
             }
+            rw[row] = v;
         }
     }
 }
-// Stage of one item into pipeline buffer `buf`: doc offsets, the rows' codes
-// and factors, the expanded bits, and the MMA into TMEM columns [64 buf, +64).
-// kFull: the (1+ex_bits)-bit codes in token order (full_codes / full_factors,
-// width w), expanded to their integer levels 0..2^w-1; else the 1-bit codes
-// in cluster order (through tok2pos), expanded to 0/1.
+
+// Starts the asynchronous loads of one item: its record into record slot rs,
+// and this thread's row (packed code, factor) into code slot cs and factor
+// slot rs.  idx: the row's code index, kRtNoRow for none.
 template <bool kFull, int kW>
-__device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, int q, int cap,
-                                         const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows,
-                                         const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
-                                         uint32_t tmem) {
+__device__ __forceinline__ void rt_issue(RtSmem<kFull, kW>& s, int rs, int cs, const RtItem* rec, uint32_t idx,
+                                         const uint8_t* __restrict__ codes, const float* __restrict__ factors) {
+    constexpr int kC = RtShape<kFull, kW>::kRowChunks;
     const int tid = threadIdx.x;
-    // the item's record (40 words) and this row's code index, both coalesced
-    const int* mw = reinterpret_cast<const int*>(meta + (size_t)q * cap + item);
-    if (tid < 40) s.rec[buf][tid] = __ldg(mw + tid);
-    const uint32_t code_idx = __ldg(rows + ((size_t)q * cap + item) * kRtRows + tid);
-    __syncthreads();
-    const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[buf]);
-    const int T = rec.ntok;
-    uint4 code = make_uint4(0, 0, 0, 0);
-    float f = 0.0f;
-    int ld = -1;
-    uint8_t* a = s.a[buf];
-    if (kFull) {
-        if (tid < T) {
-            ld = 0;
-            while (rec.tok0[ld + 1] <= tid) ++ld;
-            const int64_t token = code_idx;
-            constexpr int bytes = kDim * kW / 8;
-            // the packed code in registers (16 * kW bytes)
-            uint8_t pk[bytes];
-            const uint4* src = reinterpret_cast<const uint4*>(codes1 + (size_t)token * bytes);
+    if (tid < kRtRecWords / 4) cp_async16(&s.rec[rs][4 * tid], reinterpret_cast<const uint4*>(rec) + tid);
+    if (idx != kRtNoRow) {
+        const uint4* src = reinterpret_cast<const uint4*>(codes) + (size_t)idx * kC;
 #pragma unroll
-            for (int v = 0; v < kW; ++v) *reinterpret_cast<uint4*>(pk + 16 * v) = __ldg(src + v);
-            f = __ldg(factor1 + token);
+        for (int v = 0; v < kC; ++v) cp_async16(&s.raw[cs][tid * kC + v], src + v);
+        cp_async4(&s.fac[rs][tid], factors + idx);
+    }
+    cp_async_commit();
+}
+
+// Expands this thread's row of the item in record slot rs / code slot cs
+// into tile ab (levels as bytes) and records the row's item-local doc in
+// row_doc[db].  Rows past the item's tokens keep stale bytes: their
+// accumulators are never read.
+// kFull: the (1+ex_bits)-bit codes (width w) expanded to 0..2^w-1; else the
+// 1-bit codes expanded to 0/1.
+template <bool kFull, int kW>
+__device__ __forceinline__ void rt_expand(RtSmem<kFull, kW>& s, int rs, int cs, int ab, int db) {
+    const int tid = threadIdx.x;
+    const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[rs]);
+    uint8_t* a = s.a[ab];
+    int ld = -1;
+    if (tid < rec.ntok) {
+        ld = 0;
+        while (rec.tok0[ld + 1] <= tid) ++ld;
+        if (kFull) {
+            constexpr int bytes = kDim * kW / 8;
+            uint8_t pk[bytes];
+#pragma unroll
+            for (int v = 0; v < kW; ++v) *reinterpret_cast<uint4*>(pk + 16 * v) = s.raw[cs][tid * kW + v];
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 uint32_t wd[4];
@@ -276,62 +280,55 @@ __device__ __forceinline__ void rt_stage(RtSmem<kFull>& s, int buf, int item, in
                 *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
             }
         } else {
+            const uint4 code = s.raw[cs][tid];
+            const uint32_t wv[4] = {code.x, code.y, code.z, code.w};
 #pragma unroll
-            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) = make_uint4(0, 0, 0, 0);
-        }
-        s.fac[buf][tid] = f;
-        s.row_doc[buf][tid] = ld;
-    } else {
-        if (tid < T) {
-            ld = 0;
-            while (rec.tok0[ld + 1] <= tid) ++ld;
-            code = __ldg(reinterpret_cast<const uint4*>(codes1) + code_idx);
-            f = __ldg(factor1 + code_idx);
-        }
-        s.code[kFull ? 0 : buf][tid] = code;
-        s.fac[buf][tid] = f;
-        s.row_doc[buf][tid] = ld;
-        const uint32_t wv[4] = {code.x, code.y, code.z, code.w};
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint32_t h = wv[c >> 1] >> ((c & 1) * 16);
-            *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) =
-                make_uint4(nib_bytes(h & 0xF), nib_bytes((h >> 4) & 0xF), nib_bytes((h >> 8) & 0xF),
-                           nib_bytes((h >> 12) & 0xF));
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t h = wv[c >> 1] >> ((c & 1) * 16);
+                *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) =
+                    make_uint4(nib_bytes(h & 0xF), nib_bytes((h >> 4) & 0xF), nib_bytes((h >> 8) & 0xF),
+                               nib_bytes((h >> 12) & 0xF));
+            }
         }
     }
-    fence_proxy_async_smem();
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-        sm100::tc_fence_after();
-        const uint32_t a_base = sm100::smem_addr(a), b_base = sm100::smem_addr(s.b);
+    s.row_doc[db][tid] = ld;
+}
+
+// One thread: the K = 128 product of tile ab with the query limbs into the
+// accumulator, completion on the barrier.
+template <bool kFull, int kW>
+__device__ __forceinline__ void rt_mma(RtSmem<kFull, kW>& s, int ab, uint32_t tmem) {
+    const uint32_t a_base = sm100::smem_addr(s.a[ab]), b_base = sm100::smem_addr(s.b);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-            mma_i8(tmem + buf * kRtN, sm100::smem_desc_sw128(a_base + kk * 32), sm100::smem_desc_sw128(b_base + kk * 32),
-                   kRtIdesc, kk > 0 ? 1u : 0u);
-        sm100::mma_commit(&s.bar[buf]);
-    }
+    for (int kk = 0; kk < 4; ++kk)
+        mma_i8(tmem, sm100::smem_desc_sw128(a_base + kk * 32), sm100::smem_desc_sw128(b_base + kk * 32), kRtIdesc,
+               kk > 0 ? 1u : 0u);
+    sm100::mma_commit(&s.bar);
 }
 
 // kFull: the full-bit MaxSim of fullbit_kernel (codes at width w, cb = cbex,
 // the AVX-512 lane order for the exact sums, its 16-lane document reduction);
-// else the 1-bit score of refine_1bit_kernel (cb = cb1).
+// else the 1-bit score of refine_1bit_kernel (cb = cb1, exact sums from the
+// query's LUTs).
+//
+// Item k (the CTA's k-th) goes through: loads issued (iteration k-2), tile
+// expanded and multiplied (iteration k-1), accumulators reduced (iteration k).
 template <bool kFull, int kW>
-__global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
-    const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows, const uint8_t* __restrict__ codes1,
-    const float* __restrict__ factor1, const float* __restrict__ cb1, const float* __restrict__ rot, int k_refine,
-    const int32_t* __restrict__ n_items, float* __restrict__ scores, uint32_t* __restrict__ status,
-    unsigned long long* __restrict__ stats) {
+__global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
+    const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows, const uint8_t* __restrict__ codes,
+    const float* __restrict__ factors, const float* __restrict__ cb1, const float* __restrict__ rot,
+    const float* __restrict__ lut, int cap, const int32_t* __restrict__ n_items, float* __restrict__ scores,
+    uint32_t* __restrict__ status, unsigned long long* __restrict__ stats) {
+    using Sh = RtShape<kFull, kW>;
     extern __shared__ uint8_t smem_raw[];
-    RtSmem<kFull>& s =
-        *reinterpret_cast<RtSmem<kFull>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    RtSmem<kFull, kW>& s =
+        *reinterpret_cast<RtSmem<kFull, kW>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = blockIdx.y;
     const int NI = n_items[q];
     if ((int)blockIdx.x >= NI) return;
 
-    // ---- prologue: query limbs (B operand), margins, TMEM, barriers --------
+    // ---- prologue: query limbs (B operand), margins, TMEM, barrier ---------
     {
         // thread tid writes row n = tid >> 1 (limb n >> 5 of token n & 31), half (tid & 1) of K
         const int n = tid >> 1, half = tid & 1;
@@ -390,8 +387,7 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
         if (tid < kRtMaxDocs) s.maxf[tid] = 0u;
         if (tid == 0) {
             s.n_cand = 0;
-            sm100::mbar_init(&s.bar[0], 1);
-            sm100::mbar_init(&s.bar[1], 1);
+            sm100::mbar_init(&s.bar, 1);
             sm100::fence_mbar_init();
         }
         if (warp == 0) {
@@ -405,36 +401,64 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
     }
     const uint32_t tmem = s.tmem_base;
     const float inv_fix = 1.0f / kFix;
+    const size_t qb = (size_t)q * cap;
+    const int G = gridDim.x;
+    int it = blockIdx.x;
+    // item 0 loaded, expanded and multiplied; item 1 loaded; item 2's code indices in registers
+    uint32_t idx = __ldg(rows + (qb + it) * kRtRows + tid);
+    rt_issue(s, 0, 0, meta + qb + it, idx, codes, factors);
+    if (it + G < NI) idx = __ldg(rows + (qb + it + G) * kRtRows + tid);
+    cp_async_wait_all();
+    __syncthreads();
+    rt_expand(s, 0, 0, 0, 0);
+    fence_proxy_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        sm100::tc_fence_after();
+        rt_mma(s, 0, tmem);
+    }
+    if (it + G < NI) rt_issue(s, 1, 1 % Sh::kRaw, meta + qb + it + G, idx, codes, factors);
+    if (it + 2 * G < NI) idx = __ldg(rows + (qb + it + 2 * G) * kRtRows + tid);
+    cp_async_wait_all();
+    __syncthreads();
+
     bool failed = false;  // uniform across the CTA (set from __syncthreads_or)
     unsigned long long n_rows = 0, n_cand = 0;
-
-    rt_stage<kFull, kW>(s, 0, blockIdx.x, q, k_refine, meta, rows, codes1, factor1, tmem);
     int k = 0;
-    bool next_issued = false;  // an MMA of item k+1 is in flight
-    for (int it = blockIdx.x; it < NI; it += gridDim.x, ++k) {
-        const int buf = k & 1;
-        const int nxt = it + gridDim.x;
-        next_issued = nxt < NI;
-        if (next_issued)  // overlaps this item's MMA and epilogue
-            rt_stage<kFull, kW>(s, buf ^ 1, nxt, q, k_refine, meta, rows, codes1, factor1, tmem);
-        bool ok = true;
-        if (tid == 0) ok = sm100::mbar_wait(&s.bar[buf], (uint32_t)((k >> 1) & 1));
+    for (; it < NI; it += G, ++k) {
+        const bool has1 = it + G < NI, has2 = it + 2 * G < NI, has3 = it + 3 * G < NI;
+        const int rs = k % 3;
+        // ---- item k's accumulators, one row per thread.  Every thread waits
+        // for the MMA itself; a wait that ran out is acted on at the barrier
+        // below (what was read or expanded meanwhile is then discarded).
+        const bool ok = sm100::mbar_wait(&s.bar, (uint32_t)(k & 1));
+        sm100::tc_fence_after();
+        uint32_t hi[32], lo[32];
+        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+        sm100::tmem_ld32_async(taddr, hi);
+        sm100::tmem_ld32_async(taddr + 32, lo);
+        sm100::tmem_wait_ld();
+        // ---- item k+1: expanded and multiplied while item k is reduced
+        if (has1) rt_expand(s, (k + 1) % 3, (k + 1) % Sh::kRaw, (k + 1) % Sh::kA, (k + 1) & 1);
+        fence_proxy_async_smem();
+        sm100::tc_fence_before();
         if (__syncthreads_or(!ok)) {
             failed = true;
             break;
         }
-        sm100::tc_fence_after();
-        // ---- accumulators -> estimated dists, one row per thread, kept in registers
-        uint32_t hi[32], lo[32];
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + buf * kRtN;
-        sm100::tmem_ld32_async(taddr, hi);
-        sm100::tmem_ld32_async(taddr + 32, lo);
-        sm100::tmem_wait_ld();
-        sm100::tc_fence_before();
-        const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[buf]);
+        if (has1 && tid == 0) {
+            sm100::tc_fence_after();
+            rt_mma(s, (k + 1) % Sh::kA, tmem);
+        }
+        // ---- item k+2's loads and item k+3's code indices, in flight during the reduction
+        if (has2) rt_issue(s, (k + 2) % 3, (k + 2) % Sh::kRaw, meta + qb + it + 2 * G, idx, codes, factors);
+        if (has3) idx = __ldg(rows + (qb + it + 3 * G) * kRtRows + tid);
+        // ---- estimated dists, kept in registers
+        const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[rs]);
         const int T = rec.ntok;
-        const int ld = tid < T ? s.row_doc[buf][tid] : -1;
-        const float f = tid < T ? s.fac[buf][tid] : 0.0f;
+        const int ld = tid < T ? s.row_doc[k & 1][tid] : -1;
+        const float f = tid < T ? s.fac[rs][tid] : 0.0f;
         float da[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
@@ -442,55 +466,83 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
             da[t] = __fmul_rn(__fsub_rn(ipa, s.cb1[t]), f);
         }
         // ---- pass 1: per (doc, query token) max of the estimates and per doc
-        // max |factor|: a reduction over each doc's lanes (docs are runs of
-        // rows), then one shared atomic per doc and query token
+        // max |factor|.  For each doc among the warp's rows (docs are runs of
+        // rows): a transposing butterfly over the 32 x 32 estimates (other
+        // docs' lanes as -inf) leaves lane t with the doc's max for query
+        // token t, then one shared atomic per lane.  The max is only used
+        // for the threshold below, where +0 and -0 give the same value.
         {
             const uint32_t grp = __match_any_sync(0xffffffffu, ld);
             for (uint32_t rem = __ballot_sync(0xffffffffu, ld >= 0); rem;) {
                 const int l = __ffs(rem) - 1;
                 const uint32_t g = __shfl_sync(0xffffffffu, grp, l);
                 rem &= ~g;
-                if ((g >> lane) & 1u) {
-                    const uint32_t fm = __reduce_max_sync(g, __float_as_uint(fabsf(f)));
-                    if (lane == l) atomicMax(&s.maxf[ld], fm);
+                const bool in = (g >> lane) & 1u;
+                const int gd = __shfl_sync(0xffffffffu, ld, l);
+                const uint32_t fm = __reduce_max_sync(0xffffffffu, in ? __float_as_uint(fabsf(f)) : 0u);
+                if (lane == 0) atomicMax(&s.maxf[gd], fm);
+                float v[32];
 #pragma unroll
-                    for (int t = 0; t < 32; ++t) {
-                        const uint32_t m = __reduce_max_sync(g, float_key_asc(da[t]));
-                        if (lane == l) atomicMax(&s.mx[ld][t], m);
+                for (int t = 0; t < 32; ++t) v[t] = in ? da[t] : -INFINITY;
+                // halving h: lanes with bit h keep the upper half of the window
+                // and take their partner's, so after h = 1 v[0] is token lane's
+#pragma unroll
+                for (int h = 16; h >= 1; h >>= 1) {
+                    const bool up = (lane & h) != 0;
+#pragma unroll
+                    for (int i = 0; i < h; ++i) {
+                        const float send = up ? v[i] : v[i + h];
+                        const float keep = up ? v[i + h] : v[i];
+                        v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, h));
                     }
                 }
+                atomicMax(&s.mx[gd][lane], float_key_asc(v[0]));
             }
         }
         __syncthreads();
         // ---- pass 2: candidates.  Every row's exact dist is within M =
         // max|f| * em of its estimate, so the max row's estimate is at least
-        // (max estimate) - 2M.
-        if (ld >= 0) {
-            const float mf = __uint_as_float(s.maxf[ld]);
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-                const float M = __fmul_ru(mf, s.em[t]);
-                const float thr = __fsub_rd(key_to_float_asc(s.mx[ld][t]), __fadd_ru(M, M));
-                if (da[t] >= thr) {
-                    const int at = atomicAdd(&s.n_cand, 1);
-                    if (at < kRtMaxCand) s.cand[at] = ((uint32_t)tid << 5) | (uint32_t)t;
-                }
-            }
+        // (max estimate) - 2M: that threshold per (doc, query token), in
+        // place of the max, then a bit per query token for each row and a
+        // block scan that places each row's candidates.
+        const int nd = rec.nd;
+        for (int i = tid; i < nd * 32; i += kRtThreads) {
+            const int d = i >> 5, t = i & 31;
+            const float M = __fmul_ru(__uint_as_float(s.maxf[d]), s.em[t]);
+            s.mx[d][t] = __float_as_uint(__fsub_rd(key_to_float_asc(s.mx[d][t]), __fadd_ru(M, M)));
         }
         __syncthreads();
-        // ---- exact LUT sums of the candidates, all threads
+        uint32_t cmask = 0;
+        if (ld >= 0) {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) cmask |= (da[t] >= __uint_as_float(s.mx[ld][t]) ? 1u : 0u) << t;
+        }
+        const int cnt = __popc(cmask);
+        int incl = cnt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += y;
+        }
+        int wbase = 0;
+        if (lane == 31 && incl > 0) wbase = atomicAdd(&s.n_cand, incl);  // one slot range per warp
+        int at = __shfl_sync(0xffffffffu, wbase, 31) + incl - cnt;
+        if (at + cnt <= kRtMaxCand)
+            for (uint32_t mm = cmask; mm; mm &= mm - 1) s.cand[at++] = ((uint32_t)tid << 5) | (uint32_t)(__ffs(mm) - 1);
+        __syncthreads();
         const int nc = s.n_cand;
+        // ---- exact sums of the candidates, spread over the four warps
         if (nc > kRtMaxCand) {
             if (tid == 0) atomicOr(status + q, 1u);  // rescored by the SIMT kernel
         } else {
-            for (int c = tid; c < nc; c += kRtThreads) {
+            for (int c = lane * (kRtThreads / 32) + warp; c < nc; c += kRtThreads) {
                 const uint32_t e = s.cand[c];
                 const int row = (int)(e >> 5), t = (int)(e & 31);
-                const float* qt = rot + ((size_t)q * kQ + t) * kDim;  // L1-resident: one query's 16 KB
                 float ip;
                 if (kFull) {
                     // fullbit_kernel's arithmetic: 16 lane chains over b = 0..7, reduce16
-                    const uint8_t* a = s.a[buf];
+                    const float* qt = rot + ((size_t)q * kQ + t) * kDim;  // L1-resident: one query's 16 KB
+                    const uint8_t* a = s.a[k % Sh::kA];
                     float acc[16];
 #pragma unroll
                     for (int l = 0; l < 16; ++l) acc[l] = 0.0f;
@@ -505,16 +557,16 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
                     }
                     ip = reduce16_avx512(acc);
                 } else {
-                    ip = lut_ip_from_query(qt, s.code[kFull ? 0 : buf][row]);
+                    // refine_1bit_kernel's LUT sum
+                    ip = lut_ip(lut + ((size_t)q * kQ + t) * kLutPerQ, s.raw[k % Sh::kRaw][row]);
                 }
-                const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[buf][row]);
-                atomicMax(&s.exact[s.row_doc[buf][row]][t], float_key_asc(dist));
+                const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[rs][row]);
+                atomicMax(&s.exact[s.row_doc[k & 1][row]][t], float_key_asc(dist));
             }
         }
         n_cand += (unsigned long long)(tid == 0 ? nc : 0);
         __syncthreads();
         // ---- document scores: the reference's 128-thread tree (kernels.cu:557-570)
-        const int nd = rec.nd;
         for (int j = warp; j < nd; j += kRtThreads / 32) {
             const float m = key_to_float_asc(s.exact[j][lane]);
             float x;
@@ -528,22 +580,25 @@ __global__ void __launch_bounds__(kRtThreads) refine_tc_kernel(
 #pragma unroll
                 for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
             }
-            if (lane == 0) scores[(size_t)q * k_refine + rec.r0 + j] = ((rec.foreign >> j) & 1u) ? -INFINITY : x;
+            if (lane == 0) scores[(size_t)q * cap + rec.r0 + j] = ((rec.foreign >> j) & 1u) ? -INFINITY : x;
             s.mx[j][lane] = 0u;
             s.exact[j][lane] = float_key_asc(kFull ? -INFINITY : -FLT_MAX);
             if (lane == 0) s.maxf[j] = 0u;
         }
-        if (tid == 0) s.n_cand = 0;
-        if (tid == 0) n_rows += (unsigned long long)T;
+        if (tid == 0) {
+            n_rows += (unsigned long long)T;
+            s.n_cand = 0;  // every thread read it before the barrier above
+        }
+        cp_async_wait_all();  // item k+2 landed
         __syncthreads();
     }
     if (failed && tid == 0) {
-        // the MMAs of item k (whose wait ran out) and of item k+1 may still be
-        // in flight: wait for them again, bounded, before TMEM is released
-        sm100::mbar_wait(&s.bar[k & 1], (uint32_t)((k >> 1) & 1));
-        if (next_issued) sm100::mbar_wait(&s.bar[(k + 1) & 1], (uint32_t)(((k + 1) >> 1) & 1));
+        // item k's MMA (whose wait ran out) may still be in flight: wait for it
+        // again, bounded, before TMEM is released
+        sm100::mbar_wait(&s.bar, (uint32_t)(k & 1));
         atomicOr(status + q, 1u);
     }
+    cp_async_wait_all();
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) n_cand += __shfl_xor_sync(0xffffffffu, n_cand, off);
     if (lane == 0 && n_cand) atomicAdd(stats + 1, n_cand);
@@ -565,8 +620,8 @@ __global__ void refine_status_clear_kernel(uint32_t* status, int nq, unsigned lo
 }  // namespace chm
 
 namespace chm {
-template <bool kFull>
-size_t refine_tc_smem_bytes() { return sizeof(RtSmem<kFull>) + 1024; }
+template <bool kFull, int kW>
+size_t refine_tc_smem_bytes() { return sizeof(RtSmem<kFull, kW>) + 1024; }
 
 // Workspace of one tensor-core refinement call.
 struct RtWork {
@@ -619,21 +674,30 @@ static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, con
     return launch_status("rt_fill_kernel");
 }
 
-static dim3 rt_grid(int nq, int cap) {
-    // about eight waves of 3 CTAs per SM: items per CTA vary by query, so
-    // finer-grained CTAs balance the tail
-    int gx = (3 * 148 * 8 + nq - 1) / nq;
+// About eight waves of the resident CTAs: items per CTA vary by query, so
+// finer-grained CTAs balance the tail.
+template <typename Kernel>
+static chm_status rt_grid(Kernel kernel, size_t smem, int nq, int cap, dim3* grid) {
+    int dev = 0, sms = 0, occ = 0;
+    CHM_CUDA(cudaGetDevice(&dev));
+    CHM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CHM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kRtThreads, smem));
+    int gx = (std::max(occ, 1) * sms * 8 + nq - 1) / nq;
     gx = std::max(1, std::min(gx, cap));
-    return dim3((unsigned)gx, (unsigned)nq);
+    *grid = dim3((unsigned)gx, (unsigned)nq);
+    return CHM_OK;
 }
 
 template <int kW>
 static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex, int fb_cap,
                                    const RtWork& w, float* scores, cudaStream_t st) {
-    const size_t smem = refine_tc_smem_bytes<true>();
+    const size_t smem = refine_tc_smem_bytes<true, kW>();
     CHM_CUDA(cudaFuncSetAttribute(refine_tc_kernel<true, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    refine_tc_kernel<true, kW><<<rt_grid(nq, fb_cap), kRtThreads, smem, st>>>(
-        w.meta, w.rows, idx->full_codes, idx->full_factors, cbex, rot, fb_cap, w.n_items, scores, w.status, w.stats);
+    dim3 grid;
+    CHM_TRY(rt_grid(refine_tc_kernel<true, kW>, smem, nq, fb_cap, &grid));
+    refine_tc_kernel<true, kW><<<grid, kRtThreads, smem, st>>>(w.meta, w.rows, idx->full_codes, idx->full_factors,
+                                                               cbex, rot, nullptr, fb_cap, w.n_items, scores,
+                                                               w.status, w.stats);
     return launch_status("fullbit_tc_kernel");
 }
 
@@ -683,11 +747,13 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     chm::rt_layout(a, nq, k_refine, &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
     CHM_TRY(chm::rt_plan<false>(idx, nq, refined_docs, num_refined, k_refine, w, st));
-    const size_t smem = chm::refine_tc_smem_bytes<false>();
+    const size_t smem = chm::refine_tc_smem_bytes<false, 1>();
     CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
-    chm::refine_tc_kernel<false, 1><<<chm::rt_grid(nq, k_refine), chm::kRtThreads, smem, st>>>(
-        w.meta, w.rows, idx->codes1, idx->factor1, cb1, rot, k_refine, w.n_items, scores, w.status, w.stats);
+    dim3 grid;
+    CHM_TRY(chm::rt_grid(chm::refine_tc_kernel<false, 1>, smem, nq, k_refine, &grid));
+    chm::refine_tc_kernel<false, 1><<<grid, chm::kRtThreads, smem, st>>>(
+        w.meta, w.rows, idx->codes1, idx->factor1, cb1, rot, lut, k_refine, w.n_items, scores, w.status, w.stats);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
     return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, w.big, w.n_big,
                                     w.status, st);

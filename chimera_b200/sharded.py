@@ -257,8 +257,13 @@ class CudaShardBackend:
 
     def refine_1bit(self, st, local, counts):
         P, B = capi._ptr, self.B
-        self._chk(self.L.chm_refine_1bit(self.v, B, P(self.lut), P(self.cb1), P(local), P(counts), self.kr,
-                                         P(self.onebit), self._stream()), "refine_1bit")
+        if B >= 16:  # chm_search's choice: the tensor-core filter on batches (same scores either way)
+            self._chk(self.L.chm_refine_1bit_tc(self.v, B, P(self.lut), P(self.cb1), P(self.rot), P(local),
+                                                P(counts), self.kr, P(self.onebit), P(self.fb_ws), self.fb_bytes,
+                                                self._stream()), "refine_1bit")
+        else:
+            self._chk(self.L.chm_refine_1bit(self.v, B, P(self.lut), P(self.cb1), P(local), P(counts), self.kr,
+                                             P(self.onebit), self._stream()), "refine_1bit")
         return self.onebit[:B]
 
     def select_fullbit(self, rdocs, onebit, counts):
