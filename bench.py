@@ -291,9 +291,9 @@ def main():
     if world == 1:
         launches = sum(s["launches"] for s in stages) + 1  # + chm_search's status fold
     else:
-        # prepare, probe, stage1 (4), merge, 2 x localize, refine, select, full-bit (7), final
+        # prepare, probe, stage1 (7), merge, 2 x localize, refine, select, full-bit (7), final
         refine_launches = next(s["launches"] for s in stages if s["name"] == "refine_1bit")
-        launches = 1 + probe_launches + 4 + 1 + 2 + refine_launches + 1 + 7 + 1
+        launches = 1 + probe_launches + 7 + 1 + 2 + refine_launches + 1 + 7 + 1
     line = {
         "metric": "QPS at Recall@100 (C3 passage corpus)",
         "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -436,7 +436,7 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         ("prepare", 1, lambda: L.chm_prepare_queries(P(index.flips), index.dim, index.ex_bits, P(q), ntok, P(rot),
                                                     P(cb1), P(cbex), P(lut), st)),
         ("probe", 6 if use_tc else 2, probe),
-        ("stage1", 4, lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe, p.k_refine, P(rd), P(rp),
+        ("stage1", 7, lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe, p.k_refine, P(rd), P(rp),
                                            P(nr), None, P(sws), sb, st)),
         # chm_search's choice: the tensor-core filter on batches of 16 or more
         ("refine_1bit", 6, lambda: L.chm_refine_1bit_tc(v, B, P(lut), P(cb1), P(rot), P(rd), P(nr), p.k_refine, P(ob),

@@ -362,13 +362,125 @@ __device__ bool table_has_doc(const uint64_t* table, uint32_t hmask, uint32_t nb
     return false;
 }
 
+// ---- pre-selection for long key lists ------------------------------------
+// The select kernel runs one CTA per query; over a list of ~10^6 keys its
+// radix passes are bound by one SM's bandwidth.  Three wide passes first cut
+// each long list down to the keys at or above the 12-bit bucket that holds
+// the k_refine-th largest key: a histogram of the top 12 bits per (query,
+// slice), the bucket per query, and a compaction.  The select kernel then
+// runs on the compacted keys, which hold every key of the top k_refine.
+constexpr int kPreThreads = 256;
+constexpr int64_t kPreCap = 65536;        // compacted keys per query (more: the full list is used)
+constexpr uint32_t kNoPivot = 0xFFFFFFFFu;
+
+__global__ void __launch_bounds__(kPreThreads) stage1_hist_kernel(const uint64_t* __restrict__ keys, int64_t key_cap,
+                                                                  const uint32_t* __restrict__ n_pos, int k_refine,
+                                                                  uint32_t* __restrict__ hist) {
+    __shared__ uint32_t h[4096];
+    const int q = blockIdx.y;
+    const int64_t n = min((int64_t)n_pos[q], key_cap);
+    for (int i = threadIdx.x; i < 4096; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    if (n > k_refine) {
+        const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+        const int64_t i0 = blockIdx.x * per, i1 = min(n, i0 + per);
+        const uint64_t* qk = keys + (size_t)q * key_cap;
+        for (int64_t i = i0 + threadIdx.x; i < i1; i += 4 * (int64_t)blockDim.x) {
+            uint64_t k4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j = i + u * (int64_t)blockDim.x;
+                k4[u] = j < i1 ? __ldcs(qk + j) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (i + u * (int64_t)blockDim.x < i1) atomicAdd(&h[(uint32_t)(k4[u] >> 52)], 1u);
+        }
+    }
+    __syncthreads();
+    uint32_t* out = hist + ((size_t)q * gridDim.x + blockIdx.x) * 4096;
+    for (int i = threadIdx.x; i < 4096; i += blockDim.x) out[i] = h[i];
+}
+
+// Per query: the highest bucket d such that the keys in buckets >= d number
+// at least k_refine (kNoPivot for lists of at most k_refine keys).
+__global__ void __launch_bounds__(kSelectThreads) stage1_pivot_kernel(const uint32_t* __restrict__ hist, int slices,
+                                                                      const uint32_t* __restrict__ n_pos,
+                                                                      int64_t key_cap, int k_refine,
+                                                                      uint32_t* __restrict__ pivot,
+                                                                      uint32_t* __restrict__ ccnt) {
+    __shared__ uint32_t s_warp[33];
+    const int q = blockIdx.x;
+    const int64_t n = min((int64_t)n_pos[q], key_cap);
+    if (n <= k_refine) {
+        if (threadIdx.x == 0) {
+            pivot[q] = kNoPivot;
+            ccnt[q] = 0;
+        }
+        return;
+    }
+    // thread t owns buckets [4095 - 4t - 3, 4095 - 4t] (descending order)
+    const int top = 4095 - 4 * threadIdx.x;
+    uint32_t c[4] = {0, 0, 0, 0};
+    for (int sl = 0; sl < slices; ++sl) {
+        const uint32_t* hs = hist + ((size_t)q * slices + sl) * 4096;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[j] += hs[top - j];
+    }
+    const uint32_t mine = c[0] + c[1] + c[2] + c[3];
+    uint32_t total;
+    const uint32_t before = block_excl_scan(mine, s_warp, &total);
+    if ((int64_t)before < k_refine && (int64_t)(before + mine) >= k_refine) {
+        uint32_t cum = before;
+        for (int j = 0; j < 4; ++j) {
+            cum += c[j];
+            if ((int64_t)cum >= k_refine) {
+                pivot[q] = (uint32_t)(top - j);
+                break;
+            }
+        }
+    }
+    if (threadIdx.x == 0) ccnt[q] = 0;
+}
+
+// Appends each query's keys in buckets >= pivot to its compacted list.
+__global__ void __launch_bounds__(kPreThreads) stage1_compact_kernel(const uint64_t* __restrict__ keys, int64_t key_cap,
+                                                                     const uint32_t* __restrict__ n_pos,
+                                                                     const uint32_t* __restrict__ pivot,
+                                                                     uint64_t* __restrict__ ckeys,
+                                                                     uint32_t* __restrict__ ccnt) {
+    const int q = blockIdx.y;
+    const uint32_t d = pivot[q];
+    if (d == kNoPivot) return;
+    const int64_t n = min((int64_t)n_pos[q], key_cap);
+    const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+    const int64_t i0 = blockIdx.x * per, i1 = min(n, i0 + per);
+    const uint64_t* qk = keys + (size_t)q * key_cap;
+    uint64_t* out = ckeys + (size_t)q * kPreCap;
+    const int lane = threadIdx.x & 31;
+    for (int64_t b = i0; b < i1; b += blockDim.x) {  // uniform trip count: the ballot needs every lane
+        const int64_t i = b + threadIdx.x;
+        const uint64_t k = i < i1 ? __ldcs(qk + i) : 0;
+        const bool keep = i < i1 && (uint32_t)(k >> 52) >= d;
+        const uint32_t m = __ballot_sync(0xffffffffu, keep);
+        if (m) {
+            uint32_t base = 0;
+            if (lane == 0) base = atomicAdd(ccnt + q, (uint32_t)__popc(m));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            const uint32_t at = base + __popc(m & ((1u << lane) - 1));
+            if (keep && at < (uint32_t)kPreCap) out[at] = k;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
     const uint64_t* __restrict__ keys, int64_t key_cap, const uint32_t* __restrict__ n_pos,
     int k_refine, const uint32_t* __restrict__ bitmaps, int64_t words,
     const uint64_t* __restrict__ tables, int log2h, int marks_all,
     int32_t* __restrict__ refined_docs, float* __restrict__ refined_partial,
     int32_t* __restrict__ num_refined, int64_t* __restrict__ num_candidates,
-    uint32_t* __restrict__ flags) {
+    uint32_t* __restrict__ flags, const uint64_t* __restrict__ ckeys, const uint32_t* __restrict__ ccnt,
+    const uint32_t* __restrict__ pivot) {
     extern __shared__ uint64_t s_dyn[];
     uint64_t* s_out = s_dyn;                                   // [sort_n]
     __shared__ uint32_t s_hist[4096];
@@ -377,8 +489,10 @@ __global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
     __shared__ uint64_t s_prefix, s_pmask;
     __shared__ int s_need, s_done;
     const int q = blockIdx.x;
-    const uint64_t* qk = keys + (size_t)q * key_cap;
-    const int64_t n = min((int64_t)n_pos[q], key_cap);
+    // a long list's compacted keys (all keys of its top k_refine), unless they overflowed
+    const bool compacted = pivot[q] != kNoPivot && ccnt[q] <= (uint32_t)kPreCap;
+    const uint64_t* qk = compacted ? ckeys + (size_t)q * kPreCap : keys + (size_t)q * key_cap;
+    const int64_t n = compacted ? (int64_t)ccnt[q] : min((int64_t)n_pos[q], key_cap);
     if ((int64_t)n_pos[q] > key_cap && threadIdx.x == 0) atomicOr(flags + q, 4u);
     const int k_eff = (int)min((int64_t)k_refine, n);
     if (threadIdx.x == 0) { s_cnt = 0; s_prefix = 0; s_pmask = 0; s_need = k_eff; s_done = 0; }
@@ -527,6 +641,12 @@ int stage1_log2h(const chm_index* idx, int nprobe, int extra) {
     return l > 31 ? 31 : l;
 }
 int64_t stage1_key_cap(const chm_index* idx) { return idx->num_docs; }
+// CTAs per query of the pre-selection passes: about four per SM in all.
+// nq x slices stays within max(nq, kPreSlots), so the histogram area sized
+// for a batch also holds any smaller chunk's.
+constexpr int kPreSlots = 640;
+int stage1_pre_slices(int nq) { return std::max(1, std::min(64, kPreSlots / std::max(1, nq))); }
+size_t stage1_hist_words(int nq) { return (size_t)std::max(nq, kPreSlots) * 4096; }
 int64_t stage1_words(const chm_index* idx) { return (idx->num_docs + 31) / 32; }
 }  // namespace chm
 
@@ -539,6 +659,10 @@ size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra)
     s.take<uint32_t>((size_t)nq * stage1_words(idx));
     s.take<uint32_t>((size_t)nq);
     s.take<uint32_t>((size_t)nq);
+    s.take<uint32_t>(stage1_hist_words(nq));                        // histograms
+    s.take<uint32_t>((size_t)nq);                                   // pivots
+    s.take<uint32_t>((size_t)nq);                                   // compacted counts
+    s.take<uint64_t>((size_t)nq * kPreCap);                         // compacted keys
     return s.off;
 }
 }  // namespace chm
@@ -569,6 +693,11 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     uint32_t* bitmaps = a.take<uint32_t>((size_t)nq * words);
     uint32_t* n_pos = a.take<uint32_t>((size_t)nq);
     uint32_t* flags = a.take<uint32_t>((size_t)nq);
+    const int slices = stage1_pre_slices(nq);
+    uint32_t* hist = a.take<uint32_t>(stage1_hist_words(nq));
+    uint32_t* pivot = a.take<uint32_t>((size_t)nq);
+    uint32_t* ccnt = a.take<uint32_t>((size_t)nq);
+    uint64_t* ckeys = a.take<uint64_t>((size_t)nq * kPreCap);
     if (a.overflow) return CHM_ERR_CAPACITY;
     CHM_CUDA(cudaMemsetAsync(tables, 0xFF, sizeof(uint64_t) * ((size_t)nq << l), st));
     CHM_CUDA(cudaMemsetAsync(n_pos, 0, sizeof(uint32_t) * nq, st));
@@ -599,9 +728,17 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     const size_t smem = sizeof(uint64_t) * sort_cap;
     // static (histogram) + dynamic (sort buffer) can exceed the 48 KB default
     CHM_CUDA(cudaFuncSetAttribute(stage1_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    stage1_hist_kernel<<<dim3((unsigned)slices, (unsigned)nq), kPreThreads, 0, st>>>(keys, key_cap, n_pos, k_refine,
+                                                                                    hist);
+    CHM_TRY(launch_status("stage1_hist_kernel"));
+    stage1_pivot_kernel<<<nq, kSelectThreads, 0, st>>>(hist, slices, n_pos, key_cap, k_refine, pivot, ccnt);
+    CHM_TRY(launch_status("stage1_pivot_kernel"));
+    stage1_compact_kernel<<<dim3((unsigned)slices, (unsigned)nq), kPreThreads, 0, st>>>(keys, key_cap, n_pos, pivot,
+                                                                                       ckeys, ccnt);
+    CHM_TRY(launch_status("stage1_compact_kernel"));
     stage1_select_kernel<<<nq, kSelectThreads, smem, st>>>(
         keys, key_cap, n_pos, k_refine, bitmaps, words, tables, l, force_marks ? 1 : 0,
-        refined_docs, refined_partial, num_refined, num_candidates, flags);
+        refined_docs, refined_partial, num_refined, num_candidates, flags, ckeys, ccnt, pivot);
     CHM_TRY(launch_status("stage1_select_kernel"));
     if (flags_out) CHM_CUDA(cudaMemcpyAsync(flags_out, flags, sizeof(uint32_t) * nq, cudaMemcpyDeviceToDevice, st));
     return CHM_OK;

@@ -183,12 +183,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
         const int et = q4 * 32 + lane;                          // 0..127 within the group
         float thr = INFINITY;                                   // kTop16: float of best[15]
         float* row_vals = s.pass[g][q4][lane];
+        float cn_next = INFINITY;  // this thread's norm of the group's next tile, loaded one tile ahead
+        if (g < n_tiles) {
+            const int64_t c0 = (int64_t)(t_begin + g) * kTN + et;
+            cn_next = c0 < p.cols ? __ldg(p.cn + c0) : INFINITY;
+        }
         for (int it = g; it < n_tiles; it += ngroups) {
             const int buf = it & 1;
             const int nb = (it / ngroups) & 1;                  // this group's norms buffer
             const int64_t n0 = (int64_t)(t_begin + it) * kTN;
             // stage this tile's norms (the group's other buffer may still be read)
-            s.cn[g][nb][et] = (n0 + et < p.cols) ? __ldg(p.cn + n0 + et) : INFINITY;
+            s.cn[g][nb][et] = cn_next;
+            if (it + ngroups < n_tiles) {
+                const int64_t c1 = (int64_t)(t_begin + it + ngroups) * kTN + et;
+                cn_next = c1 < p.cols ? __ldg(p.cn + c1) : INFINITY;
+            }
             // every warp of the group passes this barrier once per tile, also
             // after a failed wait, so the barrier count stays equal across warps
             sm100::named_bar(1 + g, 128);
@@ -572,8 +581,43 @@ namespace chm {
 
 struct ProbePlan {
     int64_t rows, nc;
-    int nprobe, kc, prefix, splits, cap;
+    int nprobe, kc, prefix, splits, store_splits, cap;
 };
+
+// SMs of the current device (148 on B200; also the answer when no device is
+// visible, so that workspace sizes can be computed anywhere).
+static int device_sms() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                   cudaSuccess || sms <= 0) {
+        (void)cudaGetLastError();
+        return 148;
+    }
+    return sms;
+}
+
+// Centroid-range splits per row tile.  The kernel runs one CTA per SM, so the
+// grid executes in waves of `sms` CTAs; a CTA costs its tiles plus a fixed
+// pipeline fill and drain of about kSplitFixedTiles tiles.  The split count
+// minimises waves x (tiles per split + fixed), so that the last wave is not
+// left mostly empty (320 CTAs on 148 SMs would run three waves, the last
+// with 24 CTAs).  Each split keeps at least 8 tiles.
+constexpr int kSplitFixedTiles = 4;
+static int choose_splits(int64_t row_tiles, int n_tiles, int sms) {
+    const int max_s = std::min(kMaxSplits, std::max(1, n_tiles / 8));
+    int best = 1;
+    double best_cost = 1e300;
+    for (int sp = 1; sp <= max_s; ++sp) {
+        const int64_t waves = (row_tiles * sp + sms - 1) / sms;
+        const int tps = (n_tiles + sp - 1) / sp;
+        const double cost = (double)waves * (tps + kSplitFixedTiles);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = sp;
+        }
+    }
+    return best;
+}
 
 static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
     ProbePlan p;
@@ -587,15 +631,13 @@ static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
     p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, nc / 16));
     p.prefix = (int)std::min<int64_t>(nc, ((p.prefix + kTN - 1) / kTN) * kTN);
     const int64_t row_tiles = (rows + kTM - 1) / kTM;
-    const int n_tiles = (int)((nc + kTN - 1) / kTN);
-    // about two CTAs' worth of work per SM: small batches split the centroid
-    // range across many CTAs so a single query still uses the whole GPU
-    int splits = (int)std::max<int64_t>(1, (2 * 148 + row_tiles - 1) / row_tiles);
-    splits = std::min(splits, std::max(1, n_tiles / 8));
-    splits = std::min(splits, kMaxSplits);
-    p.splits = splits;
+    const int sms = device_sms();
+    // small batches split the centroid range across many CTAs, so that a
+    // single query still uses the whole GPU
+    p.splits = choose_splits(row_tiles, (int)((nc + kTN - 1) / kTN), sms);
+    p.store_splits = choose_splits(row_tiles, (p.prefix + kTN - 1) / kTN, sms);
     const double expect = (double)p.kc * nc / std::max(1, p.prefix);
-    p.cap = (int)std::min<double>(kSurvMax, std::max(64.0, 4.0 * expect / splits + 64));
+    p.cap = (int)std::min<double>(kSurvMax, std::max(64.0, 4.0 * expect / p.splits + 64));
     return p;
 }
 
@@ -679,7 +721,7 @@ chm_status chm_tc_probe(const float* rot, int64_t rows, const float* centroids, 
     t1.dist = pdist;
     t1.ld = p.prefix;
     t1.err = cnt + 1;
-    CHM_TRY(launch_tc<kStore>(qb, rows, cent_bf16, p.prefix, p.splits, t1, st));
+    CHM_TRY(launch_tc<kStore>(qb, rows, cent_bf16, p.prefix, p.store_splits, t1, st));
     CHM_TRY(chm_row_kth(pdist, rows, p.prefix, p.kc, tau, tlab, st));
     // 2) filter over all centroids
     TcArgs t2{};
