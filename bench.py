@@ -291,9 +291,9 @@ def main():
     if world == 1:
         launches = sum(s["launches"] for s in stages) + 1  # + chm_search's status fold
     else:
-        # prepare, probe, stage1 (7), merge, 2 x localize, refine, select, full-bit (7), final
+        # prepare, probe, stage1 (7), merge, 2 x localize, refine, select, full-bit (8), final
         refine_launches = next(s["launches"] for s in stages if s["name"] == "refine_1bit")
-        launches = 1 + probe_launches + 7 + 1 + 2 + refine_launches + 1 + 7 + 1
+        launches = 1 + probe_launches + 7 + 1 + 2 + refine_launches + 1 + 8 + 1
     line = {
         "metric": "QPS at Recall@100 (C3 passage corpus)",
         "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -439,12 +439,12 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         ("stage1", 7, lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe, p.k_refine, P(rd), P(rp),
                                            P(nr), None, P(sws), sb, st)),
         # chm_search's choice: the tensor-core filter on batches of 16 or more
-        ("refine_1bit", 6, lambda: L.chm_refine_1bit_tc(v, B, P(lut), P(cb1), P(rot), P(rd), P(nr), p.k_refine, P(ob),
+        ("refine_1bit", 7, lambda: L.chm_refine_1bit_tc(v, B, P(lut), P(cb1), P(rot), P(rd), P(nr), p.k_refine, P(ob),
                                                         P(fbws), fbb, st)) if B >= 16 else
         ("refine_1bit", 1, lambda: L.chm_refine_1bit(v, B, P(lut), P(cb1), P(rd), P(nr), p.k_refine, P(ob), st)),
         ("select_fullbit", 1, lambda: L.chm_select_fullbit(B, P(rd), P(ob), P(nr), p.k_refine, p.k_full_bit,
                                                            p.num_chunks, P(fd), P(nf), p.k_refine, st)),
-        ("fullbit", 7, lambda: L.chm_fullbit_score_tc(v, B, P(rot), P(cbex), P(fd), P(nf), p.k_refine, P(fs),
+        ("fullbit", 8, lambda: L.chm_fullbit_score_tc(v, B, P(rot), P(cbex), P(fd), P(nf), p.k_refine, P(fs),
                                                       P(fbws), fbb, st)),
         ("final_topk", 1, lambda: L.chm_final_topk(B, P(fd), P(fs), P(nf), p.k_refine, p.k, P(res), P(nres), st)),
     ]

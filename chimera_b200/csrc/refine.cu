@@ -41,42 +41,43 @@ __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
         reinterpret_cast<float4*>(s_lut)[i] = src[i];
     if (threadIdx.x < kQ) s_cb1[threadIdx.x] = cb1[q * kQ + threadIdx.x];
     __syncthreads();
-    const int i = blockIdx.x * kRefineWarps + warp;
-    if (i >= R) return;
-    const int r = kMode == kRefineListed ? list[(size_t)q * k_refine + i] : i;
-    const int64_t doc = refined_docs[(size_t)q * k_refine + r];
-    if (doc < 0) {  // a slot another document shard owns
-        if (lane == 0) scores[(size_t)q * k_refine + r] = -INFINITY;
-        return;
-    }
-    const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
-    float m[kQ];
+    // warps stride over the query's docs (one pass for the full grid of kRefineAll)
+    for (int i = blockIdx.x * kRefineWarps + warp; i < R; i += gridDim.x * kRefineWarps) {
+        const int r = kMode == kRefineListed ? list[(size_t)q * k_refine + i] : i;
+        const int64_t doc = refined_docs[(size_t)q * k_refine + r];
+        if (doc < 0) {  // a slot another document shard owns
+            if (lane == 0) scores[(size_t)q * k_refine + r] = -INFINITY;
+            continue;
+        }
+        const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
+        float m[kQ];
 #pragma unroll
-    for (int t = 0; t < kQ; ++t) m[t] = -FLT_MAX;
-    for (int64_t tok = t0 + lane; tok < t1; tok += 32) {
-        const uint32_t pos = tok2pos[tok];
-        const uint4 code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
-        const float f = __ldg(factor1 + pos);
+        for (int t = 0; t < kQ; ++t) m[t] = -FLT_MAX;
+        for (int64_t tok = t0 + lane; tok < t1; tok += 32) {
+            const uint32_t pos = tok2pos[tok];
+            const uint4 code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
+            const float f = __ldg(factor1 + pos);
+#pragma unroll
+            for (int t = 0; t < kQ; ++t) {
+                const float ip = lut_ip(s_lut + t * kLutPerQ, code);
+                m[t] = fmaxf(m[t], fmul(fsub(ip, s_cb1[t]), f));
+            }
+        }
+        float mine = 0.0f;
 #pragma unroll
         for (int t = 0; t < kQ; ++t) {
-            const float ip = lut_ip(s_lut + t * kLutPerQ, code);
-            m[t] = fmaxf(m[t], fmul(fsub(ip, s_cb1[t]), f));
+            float x = m[t];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+            if (lane == t) mine = x;
         }
+        // one_bit_document_score_kernel's 128-thread tree (kernels.cu:557-570):
+        // 0.0f + max, two zero strides, then 16, 8, 4, 2, 1.
+        float x = fadd(fadd(fadd(0.0f, mine), 0.0f), 0.0f);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+        if (lane == 0) scores[(size_t)q * k_refine + r] = x;
     }
-    float mine = 0.0f;
-#pragma unroll
-    for (int t = 0; t < kQ; ++t) {
-        float x = m[t];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
-        if (lane == t) mine = x;
-    }
-    // one_bit_document_score_kernel's 128-thread tree (kernels.cu:557-570):
-    // 0.0f + max, two zero strides, then 16, 8, 4, 2, 1.
-    float x = fadd(fadd(fadd(0.0f, mine), 0.0f), 0.0f);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
-    if (lane == 0) scores[(size_t)q * k_refine + r] = x;
 }
 
 __device__ uint32_t excl_scan_1024(uint32_t v, uint32_t* s_warp, uint32_t* total) {
@@ -374,7 +375,9 @@ chm_status chm_refine_1bit_complete(const chm_index* idx, int32_t nq, const floa
                                     float* scores, const int32_t* list, const int32_t* list_count,
                                     const uint32_t* status, cudaStream_t st) {
     const size_t smem = sizeof(float) * chm::kQ * chm::kLutPerQ;
-    dim3 g((k_refine + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
+    // a few long docs per query, and (rarely) every doc of a flagged query:
+    // a small grid whose warps stride over them, each block staging the LUTs once
+    dim3 g(4, nq);
     CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineListed>, smem));
     chm::refine_1bit_kernel<chm::kRefineListed><<<g, chm::kRefineWarps * 32, smem, st>>>(
         idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,

@@ -33,6 +33,7 @@
 // item k+1's codes are gathered, expanded and multiplied.
 #include "codes.cuh"
 #include "common.cuh"
+#include "select.cuh"
 #include "sm100.cuh"
 
 namespace chm {
@@ -123,39 +124,173 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk16) {
 // 4 bits -> 4 bytes of 0/1
 __device__ __forceinline__ uint32_t nib_bytes(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
 
-// Greedy packing of each query's refined docs into items (r0, r1); docs
-// longer than one tile are listed for the SIMT kernel.
-__global__ void refine_plan_kernel(const int64_t* __restrict__ doc_ptrs, const int32_t* __restrict__ refined_docs,
-                                   const int32_t* __restrict__ num_refined, int k_refine,
-                                   int2* __restrict__ items, int32_t* __restrict__ n_items,
-                                   int32_t* __restrict__ big, int32_t* __restrict__ n_big) {
-    extern __shared__ int s_len[];
-    const int q = blockIdx.x;
+// Levels of dims 16c..16c+15 (one 16-byte chunk of the K-major tile) from a
+// packed (1+ex_bits)-bit code held as 32-bit words, four dims per word
+// operation.  The layouts (code_at states them per dim; r = dim within a
+// 64-dim group):
+//   w = 2: byte 4(i>>4) + (i&3), bits 2((i&15)>>2)
+//   w = 3: per 64 dims (24 bytes): two bits in byte r&15 at 2(r>>4); the
+//          third in byte 16 + (r&7), bit r>>3
+//   w = 4: byte 8(i>>4) + (i&7), nibble (i&15)>>3
+//   w = 5: per 64 dims (40 bytes): low nibbles in byte 16(r>>5) + (r&15),
+//          nibble (r>>4)&1; the fifth bit in byte 32 + (r&7), bit r>>3
+//   w = 6: per 16 dims j (12 bytes): nibble j>>3 of byte j&7; two bits
+//          2(j>>2) of byte 8 + (j&3)
+//   w = 7: per 64 dims (56 bytes): six bits in byte r (r < 48), or the top
+//          two bits of bytes r-48, r-32 and r-16 (r >= 48); the seventh in
+//          byte 48 + (r&7), bit r>>3
+// Other widths return false and the caller uses code_at.
+template <int kW>
+__device__ __forceinline__ bool expand_chunk_fast(const uint32_t* pw, int c, uint32_t (&out)[4]) {
+    if (kW == 3) {
+        const int g = c >> 2, q = c & 3;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t lo = (pw[6 * g + k] >> (2 * q)) & 0x03030303u;
+            const uint32_t hi = (pw[6 * g + 4 + (k & 1)] >> (2 * q + (k >> 1))) & 0x01010101u;
+            out[k] = lo | (hi << 2);
+        }
+        return true;
+    } else if (kW == 6) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t lo = (pw[3 * c + (k & 1)] >> (4 * (k >> 1))) & 0x0F0F0F0Fu;
+            const uint32_t hi = (pw[3 * c + 2] >> (2 * k)) & 0x03030303u;
+            out[k] = lo | (hi << 4);
+        }
+        return true;
+    } else if (kW == 7) {
+        const int g = c >> 2, q = c & 3;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t lo;
+            if (q < 3) {
+                lo = pw[14 * g + 4 * q + k] & 0x3F3F3F3Fu;
+            } else {
+                lo = ((pw[14 * g + k] >> 6) & 0x03030303u) | (((pw[14 * g + 4 + k] >> 6) & 0x03030303u) << 2) |
+                     (((pw[14 * g + 8 + k] >> 6) & 0x03030303u) << 4);
+            }
+            const uint32_t hi = (pw[14 * g + 12 + (k & 1)] >> (2 * q + (k >> 1))) & 0x01010101u;
+            out[k] = lo | (hi << 6);
+        }
+        return true;
+    } else if (kW == 2) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) out[k] = (pw[c] >> (2 * k)) & 0x03030303u;
+        return true;
+    } else if (kW == 4) {
+        out[0] = pw[2 * c] & 0x0F0F0F0Fu;
+        out[1] = pw[2 * c + 1] & 0x0F0F0F0Fu;
+        out[2] = (pw[2 * c] >> 4) & 0x0F0F0F0Fu;
+        out[3] = (pw[2 * c + 1] >> 4) & 0x0F0F0F0Fu;
+        return true;
+    } else if (kW == 5) {
+        const int g = c >> 2, cc = c & 3;  // 64-dim group, 16-dim quarter within it
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = (pw[10 * g + 4 * (cc >> 1) + j] >> (4 * (cc & 1))) & 0x0F0F0F0Fu;
+            const uint32_t hi = (pw[10 * g + 8 + (j & 1)] >> (2 * cc + (j >> 1))) & 0x01010101u;
+            out[j] = lo | (hi << 4);
+        }
+        return true;
+    }
+    return false;
+}
+
+// Greedy packing of each query's refined docs into items, in refined order:
+// an item takes consecutive docs while it holds at most kRtMaxDocs docs and
+// kRtRows tokens; a doc longer than kRtRows closes the item before it and is
+// listed for the SIMT kernel.  The walk is computed in parallel: next(r) is
+// where it continues from r (r + 1 after a listed doc, else the end of the
+// longest run that fits), and the walk from 0 visits c_i = next^i(0), found
+// by composing the tables next^(2^k), k < levels (2^levels > k_refine).
+// Shared memory: the tables as 16-bit positions ([levels][k_refine + 1];
+// the top one holds the doc lengths until it is built) and a bitmask of the
+// listed docs.
+__global__ void __launch_bounds__(1024) refine_plan_kernel(const int64_t* __restrict__ doc_ptrs,
+                                                           const int32_t* __restrict__ refined_docs,
+                                                           const int32_t* __restrict__ num_refined, int k_refine,
+                                                           int levels, int2* __restrict__ items,
+                                                           int32_t* __restrict__ n_items, int32_t* __restrict__ big,
+                                                           int32_t* __restrict__ n_big) {
+    extern __shared__ uint16_t s_j[];
+    __shared__ uint32_t s_warp[33];
+    const int q = blockIdx.x, tid = threadIdx.x;
     const int R = num_refined[q];
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const int W = k_refine + 1;
+    uint32_t* s_big = reinterpret_cast<uint32_t*>(s_j + (size_t)levels * W + ((levels * W) & 1));
+    uint16_t* len = s_j + (size_t)(levels - 1) * W;
+    for (int w = tid; w < (k_refine + 31) / 32; w += blockDim.x) s_big[w] = 0;
+    for (int r = tid; r < R; r += blockDim.x) {
         const int64_t d = refined_docs[(size_t)q * k_refine + r];
-        s_len[r] = d < 0 ? 0 : (int)(doc_ptrs[d + 1] - doc_ptrs[d]);
+        const int64_t l = d < 0 ? 0 : doc_ptrs[d + 1] - doc_ptrs[d];
+        len[r] = (uint16_t)(l < 0xFFFF ? l : 0xFFFF);
     }
     __syncthreads();
-    if (threadIdx.x != 0) return;
-    int n = 0, nb = 0, r = 0;
-    int2* out = items + (size_t)q * k_refine;
-    int32_t* bl = big + (size_t)q * k_refine;
-    while (r < R) {
-        if (s_len[r] > kRtRows) {
-            bl[nb++] = r++;
-            continue;
+    for (int r = tid; r <= R; r += blockDim.x) {
+        int nx = R;
+        if (r < R) {
+            if (len[r] > kRtRows) {
+                nx = r + 1;
+                atomicOr(&s_big[r >> 5], 1u << (r & 31));
+            } else {
+                int e = r + 1, tok = len[r];
+                while (e < R && e - r < kRtMaxDocs && len[e] <= kRtRows && tok + len[e] <= kRtRows) tok += len[e++];
+                nx = e;
+            }
         }
-        const int start = r;
-        int tok = 0;
-        while (r < R && r - start < kRtMaxDocs && s_len[r] <= kRtRows && tok + s_len[r] <= kRtRows) {
-            tok += s_len[r];
-            ++r;
-        }
-        out[n++] = make_int2(start, r);
+        s_j[r] = (uint16_t)nx;
     }
-    n_items[q] = n;
-    n_big[q] = nb;
+    __syncthreads();
+    for (int k = 1; k < levels; ++k) {  // the last level overwrites the lengths
+        const uint16_t* a = s_j + (size_t)(k - 1) * W;
+        uint16_t* b = s_j + (size_t)k * W;
+        for (int r = tid; r <= R; r += blockDim.x) b[r] = a[a[r]];
+        __syncthreads();
+    }
+    auto walk = [&](int i) {
+        int pos = 0;
+        for (int k = 0; k < levels; ++k)
+            if ((i >> k) & 1) pos = s_j[(size_t)k * W + pos];
+        return pos;
+    };
+    // walk steps [i0, i1) per thread, in order: count, scan, then write
+    const int per = (R + (int)blockDim.x - 1) / (int)blockDim.x;
+    const int i0 = min(R, tid * per), i1 = min(R, i0 + per);
+    uint32_t cnt_it = 0, cnt_bg = 0;
+    for (int i = i0; i < i1; ++i) {
+        const int c = walk(i);
+        if (c < R) {
+            if ((s_big[c >> 5] >> (c & 31)) & 1u) ++cnt_bg; else ++cnt_it;
+        }
+    }
+    uint32_t tot_it, tot_bg;
+    uint32_t at_it = blk_scan_excl(cnt_it, s_warp, &tot_it);
+    uint32_t at_bg = blk_scan_excl(cnt_bg, s_warp, &tot_bg);
+    for (int i = i0; i < i1; ++i) {
+        const int c = walk(i);
+        if (c < R) {
+            if ((s_big[c >> 5] >> (c & 31)) & 1u) big[(size_t)q * k_refine + at_bg++] = c;
+            else items[(size_t)q * k_refine + at_it++] = make_int2(c, (int)s_j[c]);
+        }
+    }
+    if (tid == 0) {
+        n_items[q] = (int32_t)tot_it;
+        n_big[q] = (int32_t)tot_bg;
+    }
+}
+
+// Levels of the planner's doubling tables (2^levels > cap, at least 2) and
+// its shared memory.
+static int rt_plan_levels(int cap) {
+    int l = 0;
+    while ((1 << l) <= cap) ++l;
+    return l < 2 ? 2 : l;
+}
+static size_t rt_plan_smem(int cap) {
+    const int levels = rt_plan_levels(cap);
+    const size_t w = (size_t)cap + 1;
+    return 2 * ((size_t)levels * w + ((levels * w) & 1)) + 4 * (size_t)((cap + 31) / 32);
 }
 
 // One warp per item: its record and, per row, the code index (the cluster
@@ -203,8 +338,12 @@ __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint3
         }
         if (lane < kRtMaxDocs) m->tok0[lane + 1] = incl;  // docs past nd repeat the total
         uint32_t* rw = rows + ((size_t)q * cap + item) * kRtRows;
-        for (int r0 = 0; r0 < kRtRows; r0 += 32) {  // uniform: the shuffles below need every lane
-            const int row = r0 + lane;
+        // this lane's four rows: their tokens first (shuffles need every lane),
+        // then the four cluster-position loads together
+        int64_t token[kRtRows / 32];
+#pragma unroll
+        for (int g = 0; g < kRtRows / 32; ++g) {
+            const int row = 32 * g + lane;
             // the row's doc: the first doc whose inclusive end exceeds row
             int lo = 0, hi = nd;
 #pragma unroll
@@ -218,14 +357,14 @@ __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint3
             const int ld = min(lo, 31);
             const int64_t f0 = __shfl_sync(0xffffffffu, first, ld);
             const int prev_end = __shfl_sync(0xffffffffu, incl, (ld + 31) & 31);  // every lane shuffles
-            const int start = ld > 0 ? prev_end : 0;
-            uint32_t v = kRtNoRow;
-            if (row < ntok) {
-                const int64_t token = f0 + (row - start);
-                v = kFull ? (uint32_t)token : __ldg(tok2pos + token);
-            }
-            rw[row] = v;
+            token[g] = row < ntok ? f0 + (row - (ld > 0 ? prev_end : 0)) : -1;
         }
+        uint32_t v[kRtRows / 32];
+#pragma unroll
+        for (int g = 0; g < kRtRows / 32; ++g)
+            v[g] = token[g] < 0 ? kRtNoRow : kFull ? (uint32_t)token[g] : __ldg(tok2pos + token[g]);
+#pragma unroll
+        for (int g = 0; g < kRtRows / 32; ++g) rw[32 * g + lane] = v[g];
     }
 }
 
@@ -264,18 +403,27 @@ __device__ __forceinline__ void rt_expand(RtSmem<kFull, kW>& s, int rs, int cs, 
         while (rec.tok0[ld + 1] <= tid) ++ld;
         if (kFull) {
             constexpr int bytes = kDim * kW / 8;
-            uint8_t pk[bytes];
+            uint32_t pw[bytes / 4];
 #pragma unroll
-            for (int v = 0; v < kW; ++v) *reinterpret_cast<uint4*>(pk + 16 * v) = s.raw[cs][tid * kW + v];
+            for (int v = 0; v < kW; ++v) {
+                const uint4 x = s.raw[cs][tid * kW + v];
+                pw[4 * v] = x.x;
+                pw[4 * v + 1] = x.y;
+                pw[4 * v + 2] = x.z;
+                pw[4 * v + 3] = x.w;
+            }
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 uint32_t wd[4];
+                if (!expand_chunk_fast<kW>(pw, c, wd)) {
+                    const uint8_t* pk = reinterpret_cast<const uint8_t*>(pw);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    uint32_t x = 0;
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t x = 0;
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) x |= (uint32_t)code_at(pk, c * 16 + j * 4 + b, kW) << (8 * b);
-                    wd[j] = x;
+                        for (int b = 0; b < 4; ++b) x |= (uint32_t)code_at(pk, c * 16 + j * 4 + b, kW) << (8 * b);
+                        wd[j] = x;
+                    }
                 }
                 *reinterpret_cast<uint4*>(a + sw128_off(tid, c)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
             }
@@ -306,38 +454,28 @@ __device__ __forceinline__ void rt_mma(RtSmem<kFull, kW>& s, int ab, uint32_t tm
     sm100::mma_commit(&s.bar);
 }
 
-// kFull: the full-bit MaxSim of fullbit_kernel (codes at width w, cb = cbex,
-// the AVX-512 lane order for the exact sums, its 16-lane document reduction);
-// else the 1-bit score of refine_1bit_kernel (cb = cb1, exact sums from the
-// query's LUTs).
-//
-// Item k (the CTA's k-th) goes through: loads issued (iteration k-2), tile
-// expanded and multiplied (iteration k-1), accumulators reduced (iteration k).
+// Per query, once per call: the B operand (each query token in 16-bit fixed
+// point as two int8 limbs, K-major SW128, the byte image of the tensor-core
+// kernel's B tile) and the error margin per query token (per unit |factor|):
+//   kFull: code levels up to W = 2^w - 1: the quantisation error times W, the
+//          exact sum's 12 roundings (8 fmas + 4 tree adds) and the int->float
+//          conversion of the estimate, then the two dist roundings of both paths;
+//   else:  quantisation + LUT-sum rounding (34 adds) + the two dist roundings.
+// E_t = sum_d |q_d - qfix_d / 2^14| and sum_d |q_d| are summed in double by a
+// warp; the 2^-20 safety factor covers the order of those sums.
 template <bool kFull, int kW>
-__global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
-    const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows, const uint8_t* __restrict__ codes,
-    const float* __restrict__ factors, const float* __restrict__ cb1, const float* __restrict__ rot,
-    const float* __restrict__ lut, int cap, const int32_t* __restrict__ n_items, float* __restrict__ scores,
-    uint32_t* __restrict__ status, unsigned long long* __restrict__ stats) {
-    using Sh = RtShape<kFull, kW>;
-    extern __shared__ uint8_t smem_raw[];
-    RtSmem<kFull, kW>& s =
-        *reinterpret_cast<RtSmem<kFull, kW>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int q = blockIdx.y;
-    const int NI = n_items[q];
-    if ((int)blockIdx.x >= NI) return;
-
-    // ---- prologue: query limbs (B operand), margins, TMEM, barrier ---------
+__global__ void __launch_bounds__(256) rt_query_kernel(const float* __restrict__ rot, const float* __restrict__ cb,
+                                                       uint8_t* __restrict__ qtile, float* __restrict__ qem) {
+    const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     {
-        // thread tid writes row n = tid >> 1 (limb n >> 5 of token n & 31), half (tid & 1) of K
-        const int n = tid >> 1, half = tid & 1;
-        const int t = n & 31;
+        // thread tid: row n = tid >> 2 (limb n >> 5 of token n & 31), chunks 2 (tid & 3) + {0, 1}
+        const int n = tid >> 2, t = n & 31;
         const bool lo_limb = n >= 32;
         const float* qv = rot + ((size_t)q * kQ + t) * kDim;
+        uint8_t* out = qtile + (size_t)q * kRtN * 128;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int chunk = half * 4 + c;
+        for (int cc = 0; cc < 2; ++cc) {
+            const int chunk = (tid & 3) * 2 + cc;
             uint32_t w[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -353,32 +491,68 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
                 }
                 w[j] = word;
             }
-            *reinterpret_cast<uint4*>(s.b + sw128_off(n, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(out + sw128_off(n, chunk)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        if (tid < 32) {
-            const float* qt = rot + ((size_t)q * kQ + tid) * kDim;
-            double e = 0.0, s1 = 0.0;
-            for (int d = 0; d < kDim; ++d) {
-                const float v = qt[d];
-                int fx = __float2int_rn(v * kFix);
-                fx = max(-16384, min(16384, fx));
-                e += fabs((double)v - (double)fx / 16384.0);
-                s1 += fabs((double)v);
-            }
-            const float c = cb1[q * kQ + tid];
-            s.cb1[tid] = c;
+    }
+    for (int t = warp; t < kQ; t += 8) {
+        const float* qt = rot + ((size_t)q * kQ + t) * kDim;
+        double e = 0.0, s1 = 0.0;
+        for (int d = lane; d < kDim; d += 32) {
+            const float v = qt[d];
+            int fx = __float2int_rn(v * kFix);
+            fx = max(-16384, min(16384, fx));
+            e += fabs((double)v - (double)fx / 16384.0);
+            s1 += fabs((double)v);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            e += __shfl_xor_sync(0xffffffffu, e, off);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+        }
+        if (lane == 0) {
+            const double c = fabs((double)cb[q * kQ + t]);
             double m;
             if (kFull) {
-                // code levels up to W: quantisation error times W, the exact sum's 12
-                // roundings (8 fmas + 4 tree adds) and the int->float conversion of
-                // the estimate, then the two dist roundings of both paths
                 const double W = (double)((1 << kW) - 1);
-                m = W * e + 24.0 * 0x1p-24 * W * s1 + 0x1p-21 * (W * s1 + fabs((double)c));
+                m = W * e + 24.0 * 0x1p-24 * W * s1 + 0x1p-21 * (W * s1 + c);
             } else {
-                // quantisation + LUT-sum rounding (34 adds) + the two dist roundings of both paths
-                m = e + 40.0 * 0x1p-24 * s1 + 0x1p-21 * (s1 + fabs((double)c));
+                m = e + 40.0 * 0x1p-24 * s1 + 0x1p-21 * (s1 + c);
             }
-            s.em[tid] = __double2float_ru(m * (1.0 + 0x1p-20));
+            qem[q * kQ + t] = __double2float_ru(m * (1.0 + 0x1p-20));
+        }
+    }
+}
+
+// kFull: the full-bit MaxSim of fullbit_kernel (codes at width w, cb = cbex,
+// the AVX-512 lane order for the exact sums, its 16-lane document reduction);
+// else the 1-bit score of refine_1bit_kernel (cb = cb1, exact sums from the
+// query's LUTs).
+//
+// Item k (the CTA's k-th) goes through: loads issued (iteration k-2), tile
+// expanded and multiplied (iteration k-1), accumulators reduced (iteration k).
+template <bool kFull, int kW>
+__global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
+    const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows, const uint8_t* __restrict__ codes,
+    const float* __restrict__ factors, const float* __restrict__ cb1, const float* __restrict__ rot,
+    const float* __restrict__ lut, const uint8_t* __restrict__ qtile, const float* __restrict__ qem, int cap,
+    const int32_t* __restrict__ n_items, float* __restrict__ scores, uint32_t* __restrict__ status,
+    unsigned long long* __restrict__ stats) {
+    using Sh = RtShape<kFull, kW>;
+    extern __shared__ uint8_t smem_raw[];
+    RtSmem<kFull, kW>& s =
+        *reinterpret_cast<RtSmem<kFull, kW>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q = blockIdx.y;
+    const int NI = n_items[q];
+    if ((int)blockIdx.x >= NI) return;
+
+    // ---- prologue: the query's B tile and margins (rt_query_kernel), TMEM, barrier
+    {
+        const uint4* qb = reinterpret_cast<const uint4*>(qtile + (size_t)q * kRtN * 128);
+        for (int i = tid; i < kRtN * 128 / 16; i += kRtThreads) reinterpret_cast<uint4*>(s.b)[i] = __ldg(qb + i);
+        if (tid < 32) {
+            s.cb1[tid] = cb1[q * kQ + tid];
+            s.em[tid] = qem[q * kQ + tid];
         }
         for (int i = tid; i < kRtMaxDocs * 32; i += kRtThreads) {
             (&s.mx[0][0])[i] = 0u;
@@ -541,7 +715,8 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
                 float ip;
                 if (kFull) {
                     // fullbit_kernel's arithmetic: 16 lane chains over b = 0..7, reduce16
-                    const float* qt = rot + ((size_t)q * kQ + t) * kDim;  // L1-resident: one query's 16 KB
+                    // (the query row: L1-resident, one query's 16 KB; 16-byte aligned)
+                    const float4* qt = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + t) * kDim);
                     const uint8_t* a = s.a[k % Sh::kA];
                     float acc[16];
 #pragma unroll
@@ -551,9 +726,13 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
                         const uint4 raw = *reinterpret_cast<const uint4*>(a + sw128_off(row, b));
                         const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-                        for (int l = 0; l < 16; ++l)
-                            acc[l] = __fmaf_rn((float)((rw[l >> 2] >> (8 * (l & 3))) & 0xFFu), __ldg(qt + 16 * b + l),
-                                               acc[l]);
+                        for (int l4 = 0; l4 < 4; ++l4) {
+                            const float4 qv = __ldg(qt + 4 * b + l4);
+                            const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                acc[4 * l4 + e] = __fmaf_rn((float)((rw[l4] >> (8 * e)) & 0xFFu), qq[e], acc[4 * l4 + e]);
+                        }
                     }
                     ip = reduce16_avx512(acc);
                 } else {
@@ -633,6 +812,8 @@ struct RtWork {
     int32_t* n_big;
     RtItem* meta;
     uint32_t* rows;
+    uint8_t* qtile;  // per query: the B tile (rt_query_kernel)
+    float* qem;      // per query token: the margin
 };
 
 template <typename A>
@@ -645,8 +826,10 @@ static void rt_layout(A& a, int nq, int cap, RtWork* w) {
     auto n_big = a.template take<int32_t>((size_t)nq);
     auto meta = a.template take<RtItem>((size_t)nq * cap);
     auto rows = a.template take<uint32_t>((size_t)nq * cap * kRtRows);
+    auto qtile = a.template take<uint8_t>((size_t)nq * kRtN * 128);
+    auto qem = a.template take<float>((size_t)nq * kQ);
     if (w) *w = RtWork{(int2*)items, (int32_t*)n_items, (uint32_t*)status, (unsigned long long*)stats,
-                       (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint32_t*)rows};
+                       (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint32_t*)rows, (uint8_t*)qtile, (float*)qem};
 }
 
 struct RtSizer {
@@ -663,26 +846,41 @@ static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, con
                           const RtWork& w, cudaStream_t st) {
     refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(w.status, nq, w.stats);
     CHM_TRY(launch_status("refine_status_clear_kernel"));
-    const size_t plan_smem = sizeof(int) * (size_t)cap;
+    const size_t plan_smem = rt_plan_smem(cap);
     CHM_CUDA(cudaFuncSetAttribute(refine_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem));
-    refine_plan_kernel<<<nq, 256, plan_smem, st>>>(idx->doc_ptrs, docs, counts, cap, w.items, w.n_items, w.big,
-                                                   w.n_big);
+    refine_plan_kernel<<<nq, 1024, plan_smem, st>>>(idx->doc_ptrs, docs, counts, cap, rt_plan_levels(cap), w.items,
+                                                    w.n_items, w.big, w.n_big);
     CHM_TRY(launch_status("refine_plan_kernel"));
-    // one warp per item, 4 warps per block, 32 blocks per query striding over its items
-    rt_fill_kernel<kFull><<<dim3(32u, (unsigned)nq), 128, 0, st>>>(
+    // one warp per item, 4 warps per block, 128 blocks per query striding over its items
+    rt_fill_kernel<kFull><<<dim3(128u, (unsigned)nq), 128, 0, st>>>(
         idx->doc_ptrs, idx->tok2pos, docs, cap, w.items, w.n_items, w.meta, w.rows);
     return launch_status("rt_fill_kernel");
 }
 
 // About eight waves of the resident CTAs: items per CTA vary by query, so
-// finer-grained CTAs balance the tail.
+// finer-grained CTAs balance the tail.  Resident CTAs per SM come from the
+// kernel's shared memory, registers and TMEM columns (the runtime's occupancy
+// query answers 1 for these kernels).
 template <typename Kernel>
 static chm_status rt_grid(Kernel kernel, size_t smem, int nq, int cap, dim3* grid) {
-    int dev = 0, sms = 0, occ = 0;
+    int dev = 0, sms = 0, smem_sm = 0, resv = 0, regs_sm = 0;
     CHM_CUDA(cudaGetDevice(&dev));
     CHM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    CHM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kRtThreads, smem));
-    int gx = (std::max(occ, 1) * sms * 8 + nq - 1) / nq;
+    CHM_CUDA(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    CHM_CUDA(cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev));
+    CHM_CUDA(cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev));
+    // the largest shared-memory carveout, so that those CTAs fit
+    CHM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  (int)cudaSharedmemCarveoutMaxShared));
+    cudaFuncAttributes fa;
+    CHM_CUDA(cudaFuncGetAttributes(&fa, kernel));
+    const size_t smem_blk = smem + fa.sharedSizeBytes + (size_t)resv;
+    const int by_smem = (int)((size_t)smem_sm / std::max<size_t>(smem_blk, 1));
+    const int regs_warp = ((fa.numRegs * 32 + 255) / 256) * 256;  // allocated per warp in units of 256
+    const int by_regs = regs_sm / std::max(1, regs_warp * (kRtThreads / 32));
+    const int by_tmem = 512 / kRtTmemCols;
+    const int occ = std::max(1, std::min(std::min(by_smem, by_regs), std::min(by_tmem, 32)));
+    int gx = (occ * sms * 8 + nq - 1) / nq;
     gx = std::max(1, std::min(gx, cap));
     *grid = dim3((unsigned)gx, (unsigned)nq);
     return CHM_OK;
@@ -691,13 +889,15 @@ static chm_status rt_grid(Kernel kernel, size_t smem, int nq, int cap, dim3* gri
 template <int kW>
 static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex, int fb_cap,
                                    const RtWork& w, float* scores, cudaStream_t st) {
+    rt_query_kernel<true, kW><<<nq, 256, 0, st>>>(rot, cbex, w.qtile, w.qem);
+    CHM_TRY(launch_status("rt_query_kernel"));
     const size_t smem = refine_tc_smem_bytes<true, kW>();
     CHM_CUDA(cudaFuncSetAttribute(refine_tc_kernel<true, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid;
     CHM_TRY(rt_grid(refine_tc_kernel<true, kW>, smem, nq, fb_cap, &grid));
     refine_tc_kernel<true, kW><<<grid, kRtThreads, smem, st>>>(w.meta, w.rows, idx->full_codes, idx->full_factors,
-                                                               cbex, rot, nullptr, fb_cap, w.n_items, scores,
-                                                               w.status, w.stats);
+                                                               cbex, rot, nullptr, w.qtile, w.qem, fb_cap, w.n_items,
+                                                               scores, w.status, w.stats);
     return launch_status("fullbit_tc_kernel");
 }
 
@@ -747,13 +947,16 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     chm::rt_layout(a, nq, k_refine, &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
     CHM_TRY(chm::rt_plan<false>(idx, nq, refined_docs, num_refined, k_refine, w, st));
+    chm::rt_query_kernel<false, 1><<<nq, 256, 0, st>>>(rot, cb1, w.qtile, w.qem);
+    CHM_TRY(chm::launch_status("rt_query_kernel"));
     const size_t smem = chm::refine_tc_smem_bytes<false, 1>();
     CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
     dim3 grid;
     CHM_TRY(chm::rt_grid(chm::refine_tc_kernel<false, 1>, smem, nq, k_refine, &grid));
     chm::refine_tc_kernel<false, 1><<<grid, chm::kRtThreads, smem, st>>>(
-        w.meta, w.rows, idx->codes1, idx->factor1, cb1, rot, lut, k_refine, w.n_items, scores, w.status, w.stats);
+        w.meta, w.rows, idx->codes1, idx->factor1, cb1, rot, lut, w.qtile, w.qem, k_refine, w.n_items, scores,
+        w.status, w.stats);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
     return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, w.big, w.n_big,
                                     w.status, st);

@@ -458,17 +458,26 @@ __global__ void __launch_bounds__(kPreThreads) stage1_compact_kernel(const uint6
     const uint64_t* qk = keys + (size_t)q * key_cap;
     uint64_t* out = ckeys + (size_t)q * kPreCap;
     const int lane = threadIdx.x & 31;
-    for (int64_t b = i0; b < i1; b += blockDim.x) {  // uniform trip count: the ballot needs every lane
-        const int64_t i = b + threadIdx.x;
-        const uint64_t k = i < i1 ? __ldcs(qk + i) : 0;
-        const bool keep = i < i1 && (uint32_t)(k >> 52) >= d;
-        const uint32_t m = __ballot_sync(0xffffffffu, keep);
-        if (m) {
-            uint32_t base = 0;
-            if (lane == 0) base = atomicAdd(ccnt + q, (uint32_t)__popc(m));
-            base = __shfl_sync(0xffffffffu, base, 0);
-            const uint32_t at = base + __popc(m & ((1u << lane) - 1));
-            if (keep && at < (uint32_t)kPreCap) out[at] = k;
+    // uniform trip count (the ballots need every lane); four loads in flight per thread
+    for (int64_t b = i0; b < i1; b += 4 * (int64_t)blockDim.x) {
+        uint64_t k4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = b + u * (int64_t)blockDim.x + threadIdx.x;
+            k4[u] = i < i1 ? __ldcs(qk + i) : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = b + u * (int64_t)blockDim.x + threadIdx.x;
+            const bool keep = i < i1 && (uint32_t)(k4[u] >> 52) >= d;
+            const uint32_t m = __ballot_sync(0xffffffffu, keep);
+            if (m) {
+                uint32_t base = 0;
+                if (lane == 0) base = atomicAdd(ccnt + q, (uint32_t)__popc(m));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                const uint32_t at = base + __popc(m & ((1u << lane) - 1));
+                if (keep && at < (uint32_t)kPreCap) out[at] = k4[u];
+            }
         }
     }
 }
