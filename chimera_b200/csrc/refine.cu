@@ -16,10 +16,8 @@ constexpr int kRefineWarps = 8;
 // Modes (for the tensor-core refinement in refine_tc.cu):
 //   kRefineAll     every refined doc;
 //   kRefineFlagged every refined doc of the queries whose `status` is set
-//                  (a tensor-core launch gave up on a bounded wait);
-//   kRefineListed  the refined-list positions in `list` [nq][k_refine]
-//                  (list_count [nq]): the docs longer than one tile.
-enum RefineMode { kRefineAll = 0, kRefineFlagged = 1, kRefineListed = 2 };
+//                  (a tensor-core launch gave up on a bounded wait).
+enum RefineMode { kRefineAll = 0, kRefineFlagged = 1 };
 
 template <int kMode>
 __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
@@ -27,14 +25,13 @@ __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
     const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
     const float* __restrict__ lut, const float* __restrict__ cb1,
     const int32_t* __restrict__ refined_docs, const int32_t* __restrict__ num_refined, int k_refine,
-    float* __restrict__ scores, const uint32_t* __restrict__ status, const int32_t* __restrict__ list,
-    const int32_t* __restrict__ list_count) {
+    float* __restrict__ scores, const uint32_t* __restrict__ status) {
     extern __shared__ float s_lut[];  // [32][512]
     __shared__ float s_cb1[kQ];
     const int q = blockIdx.y;
     if (kMode == kRefineFlagged && status[q] == 0u) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int R = kMode == kRefineListed ? list_count[q] : num_refined[q];
+    const int R = num_refined[q];
     if ((int)blockIdx.x * kRefineWarps >= R) return;
     const float4* src = reinterpret_cast<const float4*>(lut + (size_t)q * kQ * kLutPerQ);
     for (int i = threadIdx.x; i < kQ * kLutPerQ / 4; i += blockDim.x)
@@ -43,7 +40,7 @@ __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
     __syncthreads();
     // warps stride over the query's docs (one pass for the full grid of kRefineAll)
     for (int i = blockIdx.x * kRefineWarps + warp; i < R; i += gridDim.x * kRefineWarps) {
-        const int r = kMode == kRefineListed ? list[(size_t)q * k_refine + i] : i;
+        const int r = i;
         const int64_t doc = refined_docs[(size_t)q * k_refine + r];
         if (doc < 0) {  // a slot another document shard owns
             if (lane == 0) scores[(size_t)q * k_refine + r] = -INFINITY;
@@ -77,6 +74,73 @@ __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
         if (lane == 0) scores[(size_t)q * k_refine + r] = x;
+    }
+}
+
+// The refined docs longer than one tensor-core tile (positions in `list`
+// [nq][k_refine], list_count [nq]): one CTA per doc, its warps striding over
+// the doc's tokens, the per-query-token maxima merged across warps (max is
+// exact in any order), then refine_1bit_kernel's tree.  CTAs stride over the
+// listed docs; each stages the query's LUTs once.
+__global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_long_kernel(
+    const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
+    const uint8_t* __restrict__ codes1, const float* __restrict__ factor1,
+    const float* __restrict__ lut, const float* __restrict__ cb1,
+    const int32_t* __restrict__ refined_docs, int k_refine, float* __restrict__ scores,
+    const int32_t* __restrict__ list, const int32_t* __restrict__ list_count) {
+    extern __shared__ float s_lut[];  // [32][512]
+    __shared__ float s_cb1[kQ];
+    __shared__ float s_m[kRefineWarps][kQ];
+    const int q = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int F = list_count[q];
+    if ((int)blockIdx.x >= F) return;
+    const float4* src = reinterpret_cast<const float4*>(lut + (size_t)q * kQ * kLutPerQ);
+    for (int i = threadIdx.x; i < kQ * kLutPerQ / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(s_lut)[i] = src[i];
+    if (threadIdx.x < kQ) s_cb1[threadIdx.x] = cb1[q * kQ + threadIdx.x];
+    __syncthreads();
+    for (int li = blockIdx.x; li < F; li += gridDim.x) {
+        const int r = list[(size_t)q * k_refine + li];
+        const int64_t doc = refined_docs[(size_t)q * k_refine + r];
+        if (doc < 0) {  // uniform across the CTA
+            if (threadIdx.x == 0) scores[(size_t)q * k_refine + r] = -INFINITY;
+            continue;
+        }
+        const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
+        float m[kQ];
+#pragma unroll
+        for (int t = 0; t < kQ; ++t) m[t] = -FLT_MAX;
+        for (int64_t tok = t0 + threadIdx.x; tok < t1; tok += blockDim.x) {
+            const uint32_t pos = tok2pos[tok];
+            const uint4 code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
+            const float f = __ldg(factor1 + pos);
+#pragma unroll
+            for (int t = 0; t < kQ; ++t) {
+                const float ip = lut_ip(s_lut + t * kLutPerQ, code);
+                m[t] = fmaxf(m[t], fmul(fsub(ip, s_cb1[t]), f));
+            }
+        }
+        float mine = 0.0f;
+#pragma unroll
+        for (int t = 0; t < kQ; ++t) {
+            float x = m[t];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+            if (lane == t) mine = x;
+        }
+        s_m[warp][lane] = mine;
+        __syncthreads();
+        if (warp == 0) {
+            float v = s_m[0][lane];
+#pragma unroll
+            for (int w = 1; w < kRefineWarps; ++w) v = fmaxf(v, s_m[w][lane]);
+            float x = fadd(fadd(fadd(0.0f, v), 0.0f), 0.0f);
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+            if (lane == 0) scores[(size_t)q * k_refine + r] = x;
+        }
+        __syncthreads();  // s_m is reused by the next doc
     }
 }
 
@@ -196,15 +260,11 @@ __global__ void __launch_bounds__(1024) select_fullbit_kernel(
 constexpr int kFbWarps = 4;
 constexpr int kFbChunkTokens = 32;   // tokens staged in shared memory at a time
 
-// kListed: only the positions in `list` [nq][fb_cap] (list_count [nq]), the
-// docs longer than one tensor-core tile (refine_tc.cu).
-template <bool kListed>
 __global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
     const int64_t* __restrict__ doc_ptrs, const uint8_t* __restrict__ full_codes,
     const float* __restrict__ full_factors, int w, const float* __restrict__ rot,
     const float* __restrict__ cbex, const int32_t* __restrict__ fb_docs,
-    const int32_t* __restrict__ num_fb, int fb_cap, float* __restrict__ scores,
-    const int32_t* __restrict__ list, const int32_t* __restrict__ list_count) {
+    const int32_t* __restrict__ num_fb, int fb_cap, float* __restrict__ scores) {
     // per warp: up to 32 tokens' packed codes (<= 128 B each) and factors,
     // plus one decoded token (128 floats)
     __shared__ __align__(16) uint8_t s_code[kFbWarps][kFbChunkTokens * 128];
@@ -212,10 +272,10 @@ __global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
     __shared__ __align__(16) float s_dec[kFbWarps][kDim];
     const int q = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int F = kListed ? list_count[q] : num_fb[q];
+    const int F = num_fb[q];
     // warps stride over the query's docs (the grid may be smaller than F / kFbWarps)
     for (int li = blockIdx.x * kFbWarps + warp; li < F; li += gridDim.x * kFbWarps) {
-        const int i = kListed ? list[(size_t)q * fb_cap + li] : li;
+        const int i = li;
         float qr[kDim];
         const float4* qsrc = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + lane) * kDim);
 #pragma unroll
@@ -271,6 +331,90 @@ __global__ void __launch_bounds__(kFbWarps * 32) fullbit_kernel(
         for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
         if (lane == 0) scores[(size_t)q * fb_cap + i] = x;
         __syncwarp();  // s_code / s_dec are reused by the warp's next doc
+    }
+}
+
+// The full-bit docs longer than one tensor-core tile (positions in `list`
+// [nq][fb_cap], list_count [nq]): one CTA per doc, each warp taking every
+// kFbWarps-th chunk of kFbChunkTokens tokens with fullbit_kernel's
+// arithmetic, the per-query-token maxima merged across warps (exact in any
+// order), then fullbit_kernel's reduction.  CTAs stride over the listed docs.
+__global__ void __launch_bounds__(kFbWarps * 32) fullbit_long_kernel(
+    const int64_t* __restrict__ doc_ptrs, const uint8_t* __restrict__ full_codes,
+    const float* __restrict__ full_factors, int w, const float* __restrict__ rot,
+    const float* __restrict__ cbex, const int32_t* __restrict__ fb_docs, int fb_cap, float* __restrict__ scores,
+    const int32_t* __restrict__ list, const int32_t* __restrict__ list_count) {
+    __shared__ __align__(16) uint8_t s_code[kFbWarps][kFbChunkTokens * 128];
+    __shared__ float s_fac[kFbWarps][kFbChunkTokens];
+    __shared__ __align__(16) float s_dec[kFbWarps][kDim];
+    __shared__ float s_m[kFbWarps][kQ];
+    const int q = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int F = list_count[q];
+    if ((int)blockIdx.x >= F) return;
+    float qr[kDim];
+    const float4* qsrc = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + lane) * kDim);
+#pragma unroll
+    for (int j = 0; j < kDim / 4; ++j) {
+        const float4 v = qsrc[j];
+        qr[4 * j] = v.x; qr[4 * j + 1] = v.y; qr[4 * j + 2] = v.z; qr[4 * j + 3] = v.w;
+    }
+    const float cb = cbex[q * kQ + lane];
+    const int bytes = kDim * w / 8;  // 16 * w, a multiple of 16
+    for (int li = blockIdx.x; li < F; li += gridDim.x) {
+        const int i = list[(size_t)q * fb_cap + li];
+        const int64_t doc = fb_docs[(size_t)q * fb_cap + i];
+        if (doc < 0) {  // uniform across the CTA
+            if (threadIdx.x == 0) scores[(size_t)q * fb_cap + i] = -INFINITY;
+            continue;
+        }
+        const int64_t t0 = doc_ptrs[doc], t1 = doc_ptrs[doc + 1];
+        float m = -INFINITY;
+        for (int64_t c0 = t0 + (int64_t)warp * kFbChunkTokens; c0 < t1; c0 += kFbWarps * kFbChunkTokens) {
+            const int nt = (int)min((int64_t)kFbChunkTokens, t1 - c0);
+            const uint4* src = reinterpret_cast<const uint4*>(full_codes + (size_t)c0 * bytes);
+            uint4* dst = reinterpret_cast<uint4*>(s_code[warp]);
+            for (int v = lane; v < nt * bytes / 16; v += 32) dst[v] = __ldg(src + v);
+            if (lane < nt) s_fac[warp][lane] = __ldg(full_factors + c0 + lane);
+            __syncwarp();
+            for (int t = 0; t < nt; ++t) {
+                const uint8_t* code = s_code[warp] + t * bytes;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) s_dec[warp][32 * k + lane] = (float)code_at(code, 32 * k + lane, w);
+                __syncwarp();
+                float s[16];
+#pragma unroll
+                for (int l = 0; l < 16; ++l) s[l] = 0.0f;
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                    const float4* dv = reinterpret_cast<const float4*>(&s_dec[warp][16 * b]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float4 d4 = dv[j];
+                        s[4 * j + 0] = __fmaf_rn(d4.x, qr[16 * b + 4 * j + 0], s[4 * j + 0]);
+                        s[4 * j + 1] = __fmaf_rn(d4.y, qr[16 * b + 4 * j + 1], s[4 * j + 1]);
+                        s[4 * j + 2] = __fmaf_rn(d4.z, qr[16 * b + 4 * j + 2], s[4 * j + 2]);
+                        s[4 * j + 3] = __fmaf_rn(d4.w, qr[16 * b + 4 * j + 3], s[4 * j + 3]);
+                    }
+                }
+                const float ip = reduce16_avx512(s);
+                m = fmaxf(m, fmul(fsub(ip, cb), s_fac[warp][t]));
+                __syncwarp();
+            }
+        }
+        s_m[warp][lane] = m;
+        __syncthreads();
+        if (warp == 0) {
+            float v = s_m[0][lane];
+#pragma unroll
+            for (int ww = 1; ww < kFbWarps; ++ww) v = fmaxf(v, s_m[ww][lane]);
+            // sum = max[0:16] + max[16:32] lane-wise, then the 16-lane reduction
+            float x = fadd(v, __shfl_down_sync(0xffffffffu, v, 16));
+#pragma unroll
+            for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
+            if (lane == 0) scores[(size_t)q * fb_cap + i] = x;
+        }
+        __syncthreads();  // s_m is reused by the next doc
     }
 }
 
@@ -364,7 +508,7 @@ extern "C" chm_status chm_refine_1bit(const chm_index* idx, int32_t nq, const fl
     dim3 g((k_refine + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
     chm::refine_1bit_kernel<chm::kRefineAll><<<g, chm::kRefineWarps * 32, smem, (cudaStream_t)stream>>>(
         idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
-        k_refine, scores, nullptr, nullptr, nullptr);
+        k_refine, scores, nullptr);
     return chm::launch_status("refine_1bit_kernel");
 }
 
@@ -375,18 +519,17 @@ chm_status chm_refine_1bit_complete(const chm_index* idx, int32_t nq, const floa
                                     float* scores, const int32_t* list, const int32_t* list_count,
                                     const uint32_t* status, cudaStream_t st) {
     const size_t smem = sizeof(float) * chm::kQ * chm::kLutPerQ;
-    // a few long docs per query, and (rarely) every doc of a flagged query:
-    // a small grid whose warps stride over them, each block staging the LUTs once
-    dim3 g(4, nq);
-    CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineListed>, smem));
-    chm::refine_1bit_kernel<chm::kRefineListed><<<g, chm::kRefineWarps * 32, smem, st>>>(
-        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
-        k_refine, scores, nullptr, list, list_count);
-    CHM_TRY(chm::launch_status("refine_1bit_listed"));
+    // a few long docs per query, a CTA each
+    CHM_TRY(chm::set_smem(chm::refine_1bit_long_kernel, smem));
+    chm::refine_1bit_long_kernel<<<dim3(16, nq), chm::kRefineWarps * 32, smem, st>>>(
+        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, k_refine, scores, list,
+        list_count);
+    CHM_TRY(chm::launch_status("refine_1bit_long_kernel"));
+    // (rarely) every doc of a flagged query: a small grid whose warps stride over them
     CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineFlagged>, smem));
-    chm::refine_1bit_kernel<chm::kRefineFlagged><<<g, chm::kRefineWarps * 32, smem, st>>>(
+    chm::refine_1bit_kernel<chm::kRefineFlagged><<<dim3(4, nq), chm::kRefineWarps * 32, smem, st>>>(
         idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
-        k_refine, scores, status, nullptr, nullptr);
+        k_refine, scores, status);
     return chm::launch_status("refine_1bit_flagged");
 }
 
@@ -410,9 +553,9 @@ extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const 
                                         void* stream) {
     if (nq <= 0) return CHM_OK;
     dim3 g((fb_cap + chm::kFbWarps - 1) / chm::kFbWarps, nq);
-    chm::fullbit_kernel<false><<<g, chm::kFbWarps * 32, 0, (cudaStream_t)stream>>>(
+    chm::fullbit_kernel<<<g, chm::kFbWarps * 32, 0, (cudaStream_t)stream>>>(
         idx->doc_ptrs, idx->full_codes, idx->full_factors, 1 + idx->ex_bits, rot, cbex, fb_docs,
-        num_fb, fb_cap, scores, nullptr, nullptr);
+        num_fb, fb_cap, scores);
     return chm::launch_status("fullbit_kernel");
 }
 
@@ -420,19 +563,19 @@ extern "C" chm_status chm_fullbit_score(const chm_index* idx, int32_t nq, const 
 chm_status chm_fullbit_flagged(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
                                const int32_t* fb_docs, const int32_t* counts, int32_t fb_cap, float* scores,
                                cudaStream_t st) {
-    chm::fullbit_kernel<false><<<dim3(2, nq), chm::kFbWarps * 32, 0, st>>>(
+    chm::fullbit_kernel<<<dim3(2, nq), chm::kFbWarps * 32, 0, st>>>(
         idx->doc_ptrs, idx->full_codes, idx->full_factors, 1 + idx->ex_bits, rot, cbex, fb_docs, counts, fb_cap,
-        scores, nullptr, nullptr);
+        scores);
     return chm::launch_status("fullbit_flagged");
 }
 
 chm_status chm_fullbit_listed(const chm_index* idx, int32_t nq, const float* rot, const float* cbex,
                               const int32_t* fb_docs, const int32_t* num_fb, int32_t fb_cap, float* scores,
                               const int32_t* list, const int32_t* list_count, cudaStream_t st) {
-    dim3 g(16, nq);  // tens of long docs per query at most: 64 warps each, striding over them
-    chm::fullbit_kernel<true><<<g, chm::kFbWarps * 32, 0, st>>>(idx->doc_ptrs, idx->full_codes, idx->full_factors,
-                                                                1 + idx->ex_bits, rot, cbex, fb_docs, num_fb, fb_cap,
-                                                                scores, list, list_count);
+    // a few long docs per query, a CTA each
+    chm::fullbit_long_kernel<<<dim3(16, nq), chm::kFbWarps * 32, 0, st>>>(
+        idx->doc_ptrs, idx->full_codes, idx->full_factors, 1 + idx->ex_bits, rot, cbex, fb_docs, fb_cap, scores, list,
+        list_count);
     return chm::launch_status("fullbit_listed");
 }
 
