@@ -24,13 +24,13 @@
 //  3. Candidates get the exact ip and dist with the plain kernels' fp32
 //     operations; their max is the exact max.
 //
-// Work items: the docs of a query packed greedily into groups of at most 128
-// tokens and 32 docs (one M tile); docs longer than 128 tokens go to a list
-// the SIMT kernels score.  A fill kernel writes per item a record (doc row
-// offsets) and every row's code index, so staging an item is one coalesced
-// load plus the code gather.  One CTA (4 warps, one row per thread) loops over
-// items with a two-deep pipeline: while item k's accumulators are reduced,
-// item k+1's codes are gathered, expanded and multiplied.
+// Work items: the docs of a query packed greedily, in refined order, into
+// groups of at most 128 tokens and 16 docs (one M tile); docs longer than 128
+// tokens go to a list the SIMT kernels score.  A fill kernel writes per item
+// a record (doc row offsets) and every row's code index, so staging an item is
+// one coalesced load plus the code gather.  One CTA (4 warps, one row per
+// thread) loops over items with a three-stage pipeline: while item k is
+// reduced, item k+1 is expanded and multiplied and item k+2's data lands.
 #include "codes.cuh"
 #include "common.cuh"
 #include "select.cuh"
