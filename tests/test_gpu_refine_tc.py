@@ -2,8 +2,8 @@
 candidates) against chm_refine_1bit (exact LUT sums of every token): the
 1-bit document scores must be identical bit for bit.  Covers the realistic
 refined lists of the oracle, random lists, documents longer than one
-128-token tile (the two-pass items), shard-foreign slots (-1) and short
-per-query counts."""
+128-token tile (scored by the SIMT long-document kernel), shard-foreign slots
+(-1) and short per-query counts."""
 import numpy as np
 import pytest
 
