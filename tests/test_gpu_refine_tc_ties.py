@@ -73,3 +73,20 @@ def test_fullbit_tc_tied_rows_overflow_to_simt():
     lists, counts = _lists(c, tied, 120)
     a = _both(c, d, lists, counts, 120)
     assert np.all(np.isfinite(a[0, :len(tied)]))
+
+
+def test_refine_tc_at_max_k_refine():
+    """k_refine = CHM_MAX_K_REFINE (8192): the item planner's doubling tables
+    take about 225 KB of shared memory, the largest launch of that kernel."""
+    c = _corpus.corpus("small")
+    cfg = c["cfg"]
+    d = _corpus.device_index(c, torch)
+    rng = np.random.default_rng(13)
+    nq = c["qrot"].shape[0]
+    cap = 8192
+    lists = np.full((nq, cap), -1, np.int32)
+    counts = np.full(nq, cfg.num_docs, np.int32)
+    for q in range(nq):
+        lists[q, :cfg.num_docs] = rng.permutation(cfg.num_docs)
+    _run_both(c, d, lists, counts, cap)
+    _both(c, d, lists, counts, cap)
