@@ -131,8 +131,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c3")
     ap.add_argument("--batch", type=int, default=128)
-    ap.add_argument("--recall-queries", type=int, default=32)
-    ap.add_argument("--cpu-sample", type=int, default=4, help="queries timed on the CPU baseline")
+    ap.add_argument("--recall-queries", type=int, default=256)
+    ap.add_argument("--cpu-sample", type=int, default=32,
+                    help="queries whose full-bit stage the CPU baseline times")
+    ap.add_argument("--parity-queries", type=int, default=8,
+                    help="queries searched by the CPU oracle and compared with the GPU results")
+    ap.add_argument("--ref-sample", type=int, default=16, help="queries per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["probe"], default=None,
                     help="operator microbench (BASELINE config C2) instead of the search bench")
@@ -180,7 +184,7 @@ def main():
     log(f"[bench] index built in {time.time() - t0:.1f}s (rank {rank}, docs {bases[rank]}..{bases[rank + 1]})")
 
     if args.impl == "reference":
-        run_reference(args, cfg, index, queries, torch)
+        run_reference(args, cfg, index, queries, torch, emb, ptr_full)
         return
 
     # exact MaxSim ground truth for the recall check, before the corpus is freed
@@ -195,15 +199,18 @@ def main():
                   k=cfg.k)
     if world == 1:
         searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
-        search_device = lambda qb: searcher.search_device(qb, res_buf, nres_buf)
+        # one result buffer per step, so that every timed step's counts can be
+        # checked after the timed region
+        nbuf = args.warmup + args.steps
+        res_bufs = [torch.empty(B, cfg.k, dtype=torch.int64, device="cuda") for _ in range(nbuf)]
+        nres_bufs = [torch.empty(B, dtype=torch.int32, device="cuda") for _ in range(nbuf)]
+        search_device = lambda qb, i: searcher.search_device(qb, res_bufs[i], nres_bufs[i])
         search_full = searcher.search
-        res_buf = torch.empty(B, cfg.k, dtype=torch.int64, device="cuda")
-        nres_buf = torch.empty(B, dtype=torch.int32, device="cuda")
         parallelism = "single GPU"
     else:
         backend = SH.CudaShardBackend(index, bases, rank, batch=B, **params)
         pipe = SH.ShardedPipeline(backend, SH.TorchComm(), params)
-        search_device = pipe.search_device
+        search_device = lambda qb, i: pipe.search_device(qb)
         search_full = pipe.search
         parallelism = f"document shards x{world} (NCCL all_gather/all_reduce)"
 
@@ -217,7 +224,7 @@ def main():
     stream = torch.cuda.current_stream()
     batches = [batch_at(i) for i in range(args.warmup + args.steps)]
     for i in range(args.warmup):
-        _, nres = search_device(batches[i])
+        _, nres = search_device(batches[i], 0)
     torch.cuda.synchronize()
     if nres.min().item() < 0:
         raise RuntimeError("stage-1 table overflow during warmup")
@@ -240,14 +247,20 @@ def main():
         barrier()
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
+        timed_counts = []
         for i in range(args.steps):
-            search_device(batches[args.warmup + i])
+            timed_counts.append(search_device(batches[args.warmup + i], args.warmup + i)[1])
         ev1.record(stream)
         torch.cuda.nvtx.range_pop()
         barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_per_step = ms / args.steps
     qps = B * args.steps / (ms / 1e3)
+    # every timed query must have completed without a stage-1 overflow
+    # (an overflowed query would have been timed with an incomplete result)
+    bad_timed = int(sum(int((c < 0).sum().item()) for c in timed_counts))
+    if bad_timed:
+        raise RuntimeError(f"{bad_timed} timed queries overflowed their stage-1 tables")
 
     # ---- end-to-end through the public entry point, host buffers -----------
     hq = [batches[args.warmup + i].cpu().pin_memory() for i in range(args.steps)]
@@ -256,28 +269,35 @@ def main():
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    e2e_counts = []
     for i in range(args.steps):
         dq.copy_(hq[i], non_blocking=True)
-        r, _ = search_device(dq)
+        r, c = search_device(dq, args.warmup + i)
         hres.copy_(r, non_blocking=True)
+        e2e_counts.append(c)
     e1.record(stream)
     barrier()
     ems = max_over_ranks(e0.elapsed_time(e1))
     e2e_qps = B * args.steps / (ems / 1e3)
+    bad_e2e = int(sum(int((c < 0).sum().item()) for c in e2e_counts))
+    if bad_e2e:
+        raise RuntimeError(f"{bad_e2e} end-to-end queries overflowed their stage-1 tables")
 
     # ---- latency percentiles (one query per call, as gpu_search times it) --
-    lat = latency_percentiles(torch, queries, search_device, barrier, n=64)
+    lat = latency_percentiles(torch, queries, lambda q: search_device(q, 0), barrier, n=64)
 
     # ---- recall ------------------------------------------------------------
     recall = None
+    r_all = None
     if nrec > 0:
         r_all, _ = search_full(queries[:nrec].contiguous())
+        r_all = r_all.cpu().numpy()
         if rank == 0:
-            recall = round(W.recall_at_k(np.stack(gt), r_all.cpu().numpy(), cfg.k), 4)
+            recall = round(W.recall_at_k(np.stack(gt), r_all, cfg.k), 4)
 
     # ---- per-stage profile on this rank's (shard) index, exchange excluded --
     prof_searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
-    stages = profile_stages(torch, capi, index, prof_searcher, batches[args.warmup], cfg)
+    stages, stages_extra = profile_stages(torch, capi, index, prof_searcher, batches[args.warmup], cfg)
     del prof_searcher
 
     hbm, bf16, kind = peaks()
@@ -313,7 +333,7 @@ def main():
                      "frac": round(achieved / peak, 4),
                      "traffic": (round(NCU_TRAFFIC_PER_UNIT[dom["name"]] * dom["units"])
                                  if dom["name"] in NCU_TRAFFIC_PER_UNIT and dom.get("units") else None),
-                     "traffic_source": "ncu capture of the c3s case scaled by units (profiles/refine_tc_c3s_b32_full.md)",
+                     "traffic_source": "ncu capture of the same kernel on the c3s case, scaled by refined tokens",
                      "peak_kind": kind},
         "stages_ms_per_step": {s["name"]: round(s["ms"], 3) for s in stages},
         "stages_algo_gbs": {s["name"]: round(s["algo_bytes"] / (s["ms"] / 1e3) / 1e9, 1)
@@ -322,7 +342,9 @@ def main():
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args, cfg, index, queries, torch)
+        line["cpu_baseline"] = cpu_baseline(args, cfg, index, queries, torch, stages_extra)
+        if args.parity_queries > 0:
+            line["parity"] = oracle_parity(args, cfg, index, queries, torch, r_all, gt)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -494,7 +516,9 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         elif n == "fullbit":
             s["algo_bytes"] = fb_tok * (16 * w + 4)
         out.append(s)
-    return out
+    # the batch's full-bit selection and scores, for the CPU baseline's check
+    extra = dict(rot=rot.view(B, 32, 128), cbex=cbex.view(B, 32), fb_docs=fd, num_fb=nf, fb_scores=fs)
+    return out, extra
 
 
 def latency_percentiles(torch, queries, search_device, barrier, n=64):
@@ -519,49 +543,142 @@ def _host_index(index):
     return O.Index(**index.to_host())
 
 
-def cpu_baseline(args, cfg, index, queries, torch, sample=None):
-    """The oracle (plain-C restatement of the path, full-bit stage in the
-    reference's AVX-512 order) on all host cores over a bounded sample."""
+def cpu_baseline(args, cfg, index, queries, torch, extra):
+    """The reference's own CPU stage: its AVX-512 full-bit MaxSim
+    (compute_full_bit_scores, search_impl.cu:510-574, through
+    oracle/_ref/libchimera_ref.so) on all host cores over the docs that the
+    GPU run selected for full-bit scoring, for `--cpu-sample` queries of the
+    profiled batch.  The GPU full-bit scores of the same docs must equal it
+    bit for bit."""
     from oracle import oracle as O
-    sample = sample or args.cpu_sample
+    if not O.ref_available():
+        return {"value": None, "unit": "queries/s", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref/libchimera_ref.so not built"}
+    R = O.ref()
+    threads = os.cpu_count()
+    S = min(args.cpu_sample, int(extra["num_fb"].shape[0]))
+    full = index.full_codes.cpu().numpy().reshape(-1)
+    ff = index.full_factors.cpu().numpy()
+    dp = index.doc_ptrs.cpu().numpy()
+    rot = extra["rot"][:S].cpu().numpy()
+    cbex = extra["cbex"][:S].cpu().numpy()
+    nfh = extra["num_fb"][:S].cpu().numpy()
+    fd = extra["fb_docs"][:S].cpu().numpy()
+    fs = extra["fb_scores"][:S].cpu().numpy()
+    w = 1 + index.ex_bits
+    secs, toks, docs, exact = 0.0, 0, 0, 0
+    for q in range(S):
+        d = np.ascontiguousarray(fd[q, :nfh[q]], np.int32)
+        out = np.zeros(len(d), np.float32)
+        t0 = time.perf_counter()
+        R.cref_fullbit_doc_scores(np.ascontiguousarray(rot[q]), np.ascontiguousarray(cbex[q]), full, ff, dp, d,
+                                  len(d), index.ex_bits, out, threads)
+        secs += time.perf_counter() - t0
+        toks += int((dp[d.astype(np.int64) + 1] - dp[d]).sum())
+        docs += len(d)
+        exact += int(np.array_equal(out.view(np.uint32), fs[q, :nfh[q]].view(np.uint32)))
+    gbytes = toks * (16 * w + 4) / 1e9
+    return {"value": round(S / secs, 3), "unit": "queries/s (full-bit stage)", "cores": threads,
+            "kind": "reference",
+            "sample": f"the reference's AVX-512 full-bit MaxSim over the docs the GPU selected, {S} queries "
+                      f"({docs} docs, {toks} tokens)",
+            "per_query_ms": round(secs / S * 1e3, 3), "docs_per_s": round(docs / secs, 1),
+            "code_gbs": round(gbytes / secs, 3), "gpu_scores_bit_exact_queries": exact}
+
+
+def oracle_parity(args, cfg, index, queries, torch, gpu_results, gt):
+    """The CPU oracle (exact probe + every stage of the path, oracle/) on the
+    first `--parity-queries` queries of the recall set, over the same index:
+    its results against the GPU's, and both recalls on those queries."""
+    from oracle import oracle as O
+    P = min(args.parity_queries, 0 if gpu_results is None else gpu_results.shape[0])
+    if P == 0:
+        return None
     threads = os.cpu_count()
     hidx = _host_index(index)
-    q = queries[:sample].contiguous()
-    ntok = sample * 32
-    rot = O.rotate(index.flips.cpu().numpy(), q.reshape(-1, q.shape[-1]).cpu().numpy()).reshape(sample, 32, 128)
+    q = queries[:P].contiguous()
+    rot = O.rotate(index.flips.cpu().numpy(), q.reshape(-1, q.shape[-1]).cpu().numpy()).reshape(P, 32, 128)
     cb1, cbex = O.query_state(rot, cfg.ex_bits)
-    cents = index.centroids.cpu().numpy()
-    cn = index.centroid_norms.cpu().numpy()
+    labels = O.probe(rot.reshape(P * 32, 128), index.centroids.cpu().numpy(), index.centroid_norms.cpu().numpy(),
+                     cfg.nprobe, threads).reshape(P, 32, cfg.nprobe)
     t0 = time.perf_counter()
-    labels = O.probe(rot.reshape(ntok, 128), cents, cn, cfg.nprobe, threads).reshape(sample, 32, cfg.nprobe)
-    t1 = time.perf_counter()
-    hidx.search_batch(rot, cb1, cbex, labels, cfg.nprobe, cfg.k_refine, cfg.k_full_bit, cfg.num_chunks, cfg.k,
-                      threads)
-    t2 = time.perf_counter()
-    return {"value": round(sample / (t2 - t0), 4), "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} queries of the same workload (probe {t1 - t0:.2f}s + search {t2 - t1:.2f}s)"}
+    res, nres = hidx.search_batch(rot, cb1, cbex, labels, cfg.nprobe, cfg.k_refine, cfg.k_full_bit,
+                                  cfg.num_chunks, cfg.k, threads)
+    secs = time.perf_counter() - t0
+    same = sum(int(np.array_equal(res[i, :nres[i]], gpu_results[i, :nres[i]])) for i in range(P))
+    return {"queries": P, "bit_exact": same,
+            "oracle_recall@100": round(W_recall(np.stack(gt[:P]), res, cfg.k), 4),
+            "gpu_recall@100": round(W_recall(np.stack(gt[:P]), gpu_results[:P], cfg.k), 4),
+            "oracle": "plain-C restatement (oracle/), exact probe, all host threads",
+            "oracle_qps": round(P / secs, 3)}
 
 
-def run_reference(args, cfg, index, queries, torch):
-    steps, warm = args.steps, args.warmup
-    per = max(1, args.cpu_sample // 2)
-    vals = []
-    for i in range(warm + steps):
-        r = cpu_baseline(args, cfg, index, queries[(i * per) % queries.shape[0]:], torch, sample=per)
-        if i >= warm:
-            vals.append(r["value"])
-    v = float(np.mean(vals))
-    n_tok = int(index.n_tokens)
-    line = {"impl": "reference", "metric": "QPS at Recall@100 (C3 passage corpus)", "value": round(v, 4),
-            "unit": "queries/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": warm,
-            "higher_is_better": True, "data": "synthetic",
-            "config": {"workload": f"{cfg.name}: {cfg.num_docs} docs, {n_tok} tokens, {cfg.n_clusters} clusters, "
-                                   f"ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, k_refine {cfg.k_refine}, "
-                                   f"k_full_bit {cfg.k_full_bit}, k {cfg.k}",
-                       "implementation": "CPU restatement of the search path on the host cores (rank 0)"},
-            "cpu_baseline": {"value": round(v, 4), "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{per} queries per step"},
-            "e2e": {"value": round(v, 4), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+def W_recall(gt, res, k):
+    from chimera_b200 import workloads as W
+    return W.recall_at_k(gt, res, k)
+
+
+def run_reference(args, cfg, index, queries, torch, emb, ptr_full):
+    """The reference's own search path (oracle/ref_search.cu: its CUDA kernels,
+    host flow and AVX-512 full-bit scorer; an exact cuBLAS probe stands in for
+    cuVS CAGRA, which is not installable here), one query per call as
+    gpu_search times it (cpp/apps/search.cpp:96-106).  A step is
+    `--ref-sample` queries; value = queries / sum of their latencies."""
+    from oracle import oracle as O
+    import torch.cuda
+    W = args.warmup
+    steps = args.steps
+    per = args.ref_sample
+    wl = (f"{cfg.name}: {cfg.num_docs} docs, {int(index.n_tokens)} tokens, {cfg.n_clusters} clusters, "
+          f"ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, k_refine {cfg.k_refine}, k_full_bit {cfg.k_full_bit}, "
+          f"k {cfg.k}")
+    base = {"impl": "reference", "metric": "QPS at Recall@100 (C3 passage corpus)", "unit": "queries/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": W,
+            "higher_is_better": True, "data": "synthetic"}
+    if not O.ref_search_available():
+        print(json.dumps({**base, "unavailable": "oracle/_ref/libchimera_ref_search.so was not built "
+                                                 "(the reference tree was absent at build time)"}), flush=True)
+        return
+    nq_total = queries.shape[0]
+    n_run = (W + steps) * per
+    qidx = [i % nq_total for i in range(n_run)]
+    timed = sorted(set(qidx[W * per:]))
+    gt_list = ground_truth(torch, emb, ptr_full, queries, cfg.k, timed)
+    gt = dict(zip(timed, gt_list))
+    del emb
+    torch.cuda.empty_cache()
+    hidx = _host_index(index)
+    threads = os.cpu_count()
+    sess = O.RefSearchSession(hidx, index.centroids.cpu().numpy(), index.centroid_norms.cpu().numpy(), cfg.dim,
+                              cfg.nprobe, cfg.k_refine, threads)
+    qh = queries.cpu().numpy()
+    lat, res, hit = [], {}, 0
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        for n, qi in enumerate(qidx):
+            t0 = time.perf_counter()
+            r, _, _ = sess.search(qh[qi], cfg.nprobe, cfg.k_refine, cfg.k_full_bit, cfg.num_chunks, cfg.k)
+            dt = time.perf_counter() - t0
+            if n >= W * per:
+                lat.append(dt)
+                res[qi] = r
+    sess.close()
+    v = len(lat) / sum(lat)
+    ls = np.sort(np.array(lat) * 1e3)
+    pct = lambda p: float(np.interp(p / 100 * (len(ls) - 1), np.arange(len(ls)), ls))
+    rec = W_recall(np.stack([gt[q] for q in timed]), [res[q] for q in timed], cfg.k)
+    line = {**base, "value": round(v, 3), "ms_per_step": round(float(np.sum(ls)) / steps, 3),
+            "config": {"workload": wl, "implementation":
+                       "reference kernels (kernels.cu, unchanged) + exact-probe shim (cuBLAS SGEMM + select, "
+                       "standing in for cuVS CAGRA) + the reference's AVX-512 full-bit scorer on the host, "
+                       "one query per call (search_impl.cu:46-574)",
+                       "queries_per_step": per, "recall@100": round(rec, 4), "recall_queries": len(timed),
+                       "latency_ms_single_query": {"p50": round(pct(50), 3), "p99": round(pct(99), 3),
+                                                   "mean": round(float(ls.mean()), 3)}},
+            "cpu_baseline": {"value": round(v, 3), "unit": "queries/s", "cores": threads, "kind": "reference",
+                             "sample": f"{per} queries per step, one per call; the full-bit stage on "
+                                       f"{threads} host threads"},
+            "e2e": {"value": round(v, 3), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
 
 

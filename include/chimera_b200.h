@@ -185,10 +185,9 @@ chm_status chm_refine_1bit(const chm_index* index, int32_t nq, const float* lut,
  * the code bits against the query in 16-bit fixed point gives each (token,
  * query token) an estimate with a proven error bound; only tokens that can
  * hold a document's maximum get the exact LUT sum (about 1.01 per document
- * and query token).  Same scores as chm_refine_1bit, bit for bit.  Measured
- * slower than chm_refine_1bit on B200 at the C3 workload (the per-pair bound
- * bookkeeping costs as many instructions as the LUT sums it avoids), so
- * chm_search uses chm_refine_1bit.  rot [nq*32*128] rotated queries;
+ * and query token).  Same scores as chm_refine_1bit, bit for bit.  chm_search
+ * uses it for batches of 16 or more queries and chm_refine_1bit (one launch,
+ * no planning) for smaller ones.  rot [nq*32*128] rotated queries;
  * workspace from chm_refine_1bit_tc_workspace_bytes. */
 size_t chm_refine_1bit_tc_workspace_bytes(int32_t nq, int32_t k_refine);
 chm_status chm_refine_1bit_tc(const chm_index* index, int32_t nq, const float* lut,

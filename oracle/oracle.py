@@ -34,10 +34,25 @@ _i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
 _u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
 
 
+def reference_tree():
+    """The reference source tree used to build ``_ref``: the directory named by
+    $CHIMERA_REFERENCE, else a ``reference`` directory beside the repository
+    root; None when neither holds the reference's ``cpp/`` sources."""
+    cands = [os.environ.get("CHIMERA_REFERENCE", ""),
+             os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for c in cands:
+        if c and os.path.isdir(os.path.join(c, "cpp")):
+            return os.path.abspath(c)
+    return None
+
+
 def build(ref: bool = True) -> None:
-    """Compile liboracle.so (and _ref when the reference tree exists)."""
-    targets = ["oracle"] + (["ref"] if ref else [])
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    """Compile liboracle.so, and ``_ref`` from the reference tree when one is
+    found (``reference_tree``); without it a prebuilt ``_ref`` is kept."""
+    subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
+    tree = reference_tree() if ref else None
+    if tree:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + tree], check=True)
 
 
 class _Index(C.Structure):
@@ -174,6 +189,81 @@ def ref_gpu_query_stages(index, rot_q, cb1, labels, nprobe, k_refine, num_chunks
     R = nref.value
     return dict(lut=lut, n_candidates=ncand.value, n_refined=R, refined_docs=rd[:R].copy(),
                 refined_partial=rp[:R].copy(), onebit_scores=ob[:R].copy())
+
+
+REF_SEARCH_SO = os.path.join(HERE, "_ref", "libchimera_ref_search.so")
+_ref_search = None
+
+
+def ref_search_available() -> bool:
+    return os.path.exists(REF_SEARCH_SO)
+
+
+def ref_search_lib():
+    global _ref_search
+    if _ref_search is None:
+        ref()  # libchimera_ref.so first (the session links against it)
+        R = C.CDLL(REF_SEARCH_SO)
+        R.cref_session_create.argtypes = [
+            _u8p, _f32p, _i32p, C.c_int64, _u64p, C.c_int64, _i64p, C.c_int64, _u32p, _u8p, _f32p, C.c_int,
+            C.c_int, _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        R.cref_session_create.restype = C.c_void_p
+        R.cref_session_destroy.argtypes = [C.c_void_p]
+        R.cref_session_search.argtypes = [
+            C.c_void_p, _f32p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _i64p,
+            C.POINTER(C.c_int), C.POINTER(C.c_int64), C.POINTER(C.c_int), C.c_char_p, C.c_int]
+        R.cref_session_search.restype = C.c_int
+        _ref_search = R
+    return _ref_search
+
+
+class RefSearchSession:
+    """The reference's own search_one (its CUDA kernels, host flow and AVX-512
+    full-bit scorer, oracle/ref_search.cu) over a persistent index: one query
+    per call, exact-probe shim in place of cuVS CAGRA.  Needs a GPU."""
+
+    def __init__(self, index, centroids_rot, centroid_norms, dim, nprobe_max, k_refine_max, threads=None):
+        err = C.create_string_buffer(512)
+        self.index = index
+        self.dim = dim
+        n_tokens = index.factor1.shape[0]
+        self.h = ref_search_lib().cref_session_create(
+            np.ascontiguousarray(index.codes1.reshape(-1)), index.factor1, index.doc_ids, n_tokens,
+            np.ascontiguousarray(index.cluster_pos.astype(np.uint64)), index.cluster_pos.shape[0] - 1,
+            np.ascontiguousarray(index.doc_ptrs, dtype=np.int64), index.doc_ptrs.shape[0] - 1,
+            np.ascontiguousarray(index.tok2pos.view(np.uint32)), np.ascontiguousarray(index.full_codes.reshape(-1)),
+            index.full_factors, int(index.ex_bits), int(dim), np.ascontiguousarray(centroids_rot, np.float32),
+            np.ascontiguousarray(centroid_norms, np.float32), int(nprobe_max), int(k_refine_max),
+            int(threads or os.cpu_count()), err, 512)
+        if not self.h:
+            raise RuntimeError(f"reference session: {err.value.decode()}")
+        self._err = err
+
+    def search(self, query, nprobe, k_refine, k_full_bit, num_chunks, k, labels=None):
+        """query [32, dim] fp32 (host) -> (doc ids best first, n_candidates,
+        n_refined).  labels ([32, nprobe] host) replaces the probe shim."""
+        out = np.zeros(k, np.int64)
+        n = C.c_int(0)
+        ncand = C.c_int64(0)
+        nref = C.c_int(0)
+        lab = None if labels is None else np.ascontiguousarray(labels, np.uint32)
+        rc = ref_search_lib().cref_session_search(
+            self.h, np.ascontiguousarray(query, np.float32), None if lab is None else lab.ctypes.data, nprobe,
+            k_refine, k_full_bit, num_chunks, k, out, C.byref(n), C.byref(ncand), C.byref(nref), self._err, 512)
+        if rc != 0:
+            raise RuntimeError(f"reference search failed ({rc}): {self._err.value.decode()}")
+        return out[:n.value].copy(), ncand.value, nref.value
+
+    def close(self):
+        if self.h:
+            ref_search_lib().cref_session_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ---------------------------------------------------------------------------

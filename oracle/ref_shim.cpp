@@ -3,8 +3,8 @@
 // quantization.cpp), compiled from the reference sources where they lie by
 // oracle/Makefile into oracle/_ref/libchimera_ref.so.  Nothing in the product
 // links this file.  It exists so the plain-C restatement in chimera_oracle.c
-// and the CUDA kernels can be checked against the reference's real code, and
-// so the golden fixtures under tests/golden/ come from the reference itself.
+// and the CUDA kernels can be checked against the reference's real code (the
+// pins in tests/test_cpu_oracle.py run it on the same inputs as the oracle).
 //
 // Reference interfaces wrapped (paths inside the Chimera project):
 //   rabitqlib::choose_rotator_with_seed / FhtKacRotator::rotate
