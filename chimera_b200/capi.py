@@ -45,7 +45,7 @@ class ChmIndex(C.Structure):
         ("doc_ids", C.c_void_p), ("tok2pos", C.c_void_p), ("doc_ptrs", C.c_void_p),
         ("full_codes", C.c_void_p), ("full_factors", C.c_void_p), ("centroids", C.c_void_p),
         ("centroid_norms", C.c_void_p), ("flips", C.c_void_p), ("centroids_bf16", C.c_void_p),
-        ("centroid_norm_max", C.c_void_p),
+        ("centroid_norm_max", C.c_void_p), ("codes1_tok", C.c_void_p), ("factor1_tok", C.c_void_p),
     ]
 
 
@@ -94,6 +94,7 @@ EXPORTS = {
     "chm_build_assign": ([V, I64, I32, V, V, I64, V, V, SZ, V], C.c_int),
     "chm_build_encode": ([V, V, I64, I32, I32, V, V, V, V, V, V], C.c_int),
     "chm_row_norms": ([V, I64, V, V], C.c_int),
+    "chm_token_order_1bit": ([V, V, V, I64, V, V, V], C.c_int),
 }
 
 
@@ -153,9 +154,14 @@ class DeviceIndex:
     """Device-resident index arrays (torch tensors) + the chm_index view."""
 
     FIELDS = ("cluster_pos", "codes1", "factor1", "doc_ids", "tok2pos", "doc_ptrs", "full_codes",
-              "full_factors", "centroids", "centroid_norms", "flips", "centroids_bf16", "centroid_norm_max")
+              "full_factors", "centroids", "centroid_norms", "flips", "centroids_bf16", "centroid_norm_max",
+              "codes1_tok", "factor1_tok")
 
-    def __init__(self, *, dim, ex_bits, tensor_core_probe=True, **arrays):
+    def __init__(self, *, dim, ex_bits, tensor_core_probe=True, token_order=True, codes1_tok=None,
+                 factor1_tok=None, **arrays):
+        """`token_order`: keep a token-order copy of the 1-bit codes and
+        factors (20 B per token) for the refinement stage; given as
+        codes1_tok / factor1_tok, or gathered here through tok2pos."""
         import torch
         self.torch = torch
         self.dim = int(dim)
@@ -175,9 +181,18 @@ class DeviceIndex:
         self.n_clusters = int(self.cluster_pos.shape[0] - 1)
         lens = self.cluster_pos[1:] - self.cluster_pos[:-1]
         self.max_list_len = int(lens.max().item()) if self.n_clusters else 0
-        ptrs = [self._p(getattr(self, k)) for k in self.FIELDS]
+        self.codes1_tok = self.factor1_tok = None
+        if token_order:
+            if codes1_tok is None or factor1_tok is None:
+                codes1_tok = torch.empty(self.n_tokens, 16, dtype=torch.uint8, device=dev)
+                factor1_tok = torch.empty(self.n_tokens, dtype=torch.float32, device=dev)
+                check(lib().chm_token_order_1bit(_ptr(self.codes1), _ptr(self.factor1), _ptr(self.tok2pos),
+                                                 self.n_tokens, _ptr(codes1_tok), _ptr(factor1_tok), st),
+                      "token_order_1bit")
+            self.codes1_tok, self.factor1_tok = codes1_tok, factor1_tok
+        ptrs = [self._p(getattr(self, k)) if getattr(self, k) is not None else 0 for k in self.FIELDS]
         if not tensor_core_probe:
-            ptrs[-2] = ptrs[-1] = 0
+            ptrs[11] = ptrs[12] = 0
         self.view = ChmIndex(self.n_tokens, self.num_docs, self.n_clusters, self.ex_bits, self.dim,
                              self.max_list_len, 0, *ptrs)
 
@@ -191,13 +206,27 @@ class DeviceIndex:
         clone.view = v
         return clone
 
+    def with_token_order(self, on: bool):
+        """The same arrays with refinement reading the token-order 1-bit
+        copies (True) or gathering the cluster-ordered ones (False)."""
+        if on and self.codes1_tok is None:
+            raise ValueError("this index has no token-order 1-bit copies")
+        v = ChmIndex.from_buffer_copy(self.view)
+        v.codes1_tok = self._p(self.codes1_tok) if on else 0
+        v.factor1_tok = self._p(self.factor1_tok) if on else 0
+        clone = object.__new__(DeviceIndex)
+        clone.__dict__.update(self.__dict__)
+        clone.view = v
+        return clone
+
     @staticmethod
     def _p(t):
         return t.data_ptr()
 
     @classmethod
     def from_host(cls, *, cluster_pos, codes1, factor1, doc_ids, tok2pos, doc_ptrs, full_codes,
-                  full_factors, centroids_rot, flips, dim, ex_bits, device="cuda", tensor_core_probe=True):
+                  full_factors, centroids_rot, flips, dim, ex_bits, device="cuda", tensor_core_probe=True,
+                  token_order=True):
         """Upload host arrays in the reference layout (oracle.Index fields)."""
         import torch
         dev = torch.device(device)
@@ -205,7 +234,7 @@ class DeviceIndex:
         cents = t(centroids_rot, np.float32)
         norms = torch.empty(cents.shape[0], dtype=torch.float32, device=dev)
         check(lib().chm_row_norms(_ptr(cents), cents.shape[0], _ptr(norms), _stream(torch)), "row_norms")
-        return cls(dim=dim, ex_bits=ex_bits, tensor_core_probe=tensor_core_probe,
+        return cls(dim=dim, ex_bits=ex_bits, tensor_core_probe=tensor_core_probe, token_order=token_order,
                    cluster_pos=t(cluster_pos, np.int64),
                    codes1=t(codes1, np.uint8), factor1=t(factor1, np.float32),
                    doc_ids=t(doc_ids, np.int32), tok2pos=t(tok2pos, np.int32),
@@ -311,7 +340,8 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
                        codes1=codes1[inv].contiguous(), factor1=f1[inv].contiguous(),
                        doc_ids=owner[inv].contiguous(), tok2pos=tok2pos, doc_ptrs=doc_ptrs,
                        full_codes=full, full_factors=ff, centroids=rot_c, centroid_norms=cnorm,
-                       flips=flips), dict(assign=assign, inv=inv, token_codes1=codes1, token_f1=f1)
+                       flips=flips, codes1_tok=codes1, factor1_tok=f1), \
+        dict(assign=assign, inv=inv, token_codes1=codes1, token_f1=f1)
 
 
 class Searcher:

@@ -170,3 +170,35 @@ extern "C" chm_status chm_build_encode(const uint8_t* flips, const float* x, int
         flips, x, n, dim, trunc, fac, ex_bits, codes1, f1, full, ff, rot);
     return chm::launch_status("encode_kernel");
 }
+
+namespace chm {
+
+// Token-order copy of the cluster-ordered 1-bit arrays: four lanes per token,
+// each moving one 4-byte word of the code, so a warp reads eight 16-byte codes
+// and writes 128 contiguous bytes.
+__global__ void __launch_bounds__(256) token_order_1bit_kernel(const uint32_t* __restrict__ codes1,
+                                                               const float* __restrict__ factor1,
+                                                               const uint32_t* __restrict__ tok2pos, int64_t n,
+                                                               uint32_t* __restrict__ codes_tok,
+                                                               float* __restrict__ factor_tok) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t tok = i >> 2;
+    const int w = (int)(i & 3);
+    if (tok >= n) return;
+    const uint32_t pos = __ldg(tok2pos + tok);
+    codes_tok[tok * 4 + w] = __ldg(codes1 + (size_t)pos * 4 + w);
+    if (w == 0) factor_tok[tok] = __ldg(factor1 + pos);
+}
+
+}  // namespace chm
+
+extern "C" chm_status chm_token_order_1bit(const uint8_t* codes1, const float* factor1, const uint32_t* tok2pos,
+                                           int64_t n, uint8_t* codes_tok, float* factor_tok, void* stream) {
+    if (n < 0 || (n > 0 && (!codes1 || !factor1 || !tok2pos || !codes_tok || !factor_tok))) return CHM_ERR_INVALID;
+    if (n == 0) return CHM_OK;
+    const int64_t threads = n * 4;
+    chm::token_order_1bit_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint32_t*>(codes1), factor1, tok2pos, n, reinterpret_cast<uint32_t*>(codes_tok),
+        factor_tok);
+    return chm::launch_status("token_order_1bit_kernel");
+}

@@ -9,6 +9,19 @@ namespace chm {
 
 constexpr int kRefineWarps = 8;
 
+// The 1-bit arrays refinement reads: the token-order copies when the index
+// has them (a document is one contiguous span, tok2pos passed as NULL), else
+// the cluster-ordered arrays gathered through tok2pos.
+struct OneBitView {
+    const uint32_t* tok2pos;
+    const uint8_t* codes;
+    const float* factors;
+};
+inline OneBitView one_bit_view(const chm_index* idx) {
+    if (idx->codes1_tok && idx->factor1_tok) return OneBitView{nullptr, idx->codes1_tok, idx->factor1_tok};
+    return OneBitView{idx->tok2pos, idx->codes1, idx->factor1};
+}
+
 // One warp per refined document; all 32 query-token LUTs in shared memory.
 // Replaces gather_refined_doc_lengths/positions, one_bit_token_score and
 // one_bit_document_score (kernels.cu:430-617) without materialising the
@@ -51,7 +64,7 @@ __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_kernel(
 #pragma unroll
         for (int t = 0; t < kQ; ++t) m[t] = -FLT_MAX;
         for (int64_t tok = t0 + lane; tok < t1; tok += 32) {
-            const uint32_t pos = tok2pos[tok];
+            const size_t pos = tok2pos ? (size_t)tok2pos[tok] : (size_t)tok;
             const uint4 code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
             const float f = __ldg(factor1 + pos);
 #pragma unroll
@@ -112,7 +125,7 @@ __global__ void __launch_bounds__(kRefineWarps * 32) refine_1bit_long_kernel(
 #pragma unroll
         for (int t = 0; t < kQ; ++t) m[t] = -FLT_MAX;
         for (int64_t tok = t0 + threadIdx.x; tok < t1; tok += blockDim.x) {
-            const uint32_t pos = tok2pos[tok];
+            const size_t pos = tok2pos ? (size_t)tok2pos[tok] : (size_t)tok;
             const uint4 code = __ldg(reinterpret_cast<const uint4*>(codes1) + pos);
             const float f = __ldg(factor1 + pos);
 #pragma unroll
@@ -506,9 +519,10 @@ extern "C" chm_status chm_refine_1bit(const chm_index* idx, int32_t nq, const fl
     const size_t smem = sizeof(float) * chm::kQ * chm::kLutPerQ;
     CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineAll>, smem));
     dim3 g((k_refine + chm::kRefineWarps - 1) / chm::kRefineWarps, nq);
+    const chm::OneBitView v = chm::one_bit_view(idx);
     chm::refine_1bit_kernel<chm::kRefineAll><<<g, chm::kRefineWarps * 32, smem, (cudaStream_t)stream>>>(
-        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
-        k_refine, scores, nullptr);
+        idx->doc_ptrs, v.tok2pos, v.codes, v.factors, lut, cb1, refined_docs, num_refined, k_refine, scores,
+        nullptr);
     return chm::launch_status("refine_1bit_kernel");
 }
 
@@ -519,17 +533,17 @@ chm_status chm_refine_1bit_complete(const chm_index* idx, int32_t nq, const floa
                                     float* scores, const int32_t* list, const int32_t* list_count,
                                     const uint32_t* status, cudaStream_t st) {
     const size_t smem = sizeof(float) * chm::kQ * chm::kLutPerQ;
+    const chm::OneBitView v = chm::one_bit_view(idx);
     // a few long docs per query, a CTA each
     CHM_TRY(chm::set_smem(chm::refine_1bit_long_kernel, smem));
     chm::refine_1bit_long_kernel<<<dim3(16, nq), chm::kRefineWarps * 32, smem, st>>>(
-        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, k_refine, scores, list,
-        list_count);
+        idx->doc_ptrs, v.tok2pos, v.codes, v.factors, lut, cb1, refined_docs, k_refine, scores, list, list_count);
     CHM_TRY(chm::launch_status("refine_1bit_long_kernel"));
     // (rarely) every doc of a flagged query: a small grid whose warps stride over them
     CHM_TRY(chm::set_smem(chm::refine_1bit_kernel<chm::kRefineFlagged>, smem));
     chm::refine_1bit_kernel<chm::kRefineFlagged><<<dim3(4, nq), chm::kRefineWarps * 32, smem, st>>>(
-        idx->doc_ptrs, idx->tok2pos, idx->codes1, idx->factor1, lut, cb1, refined_docs, num_refined,
-        k_refine, scores, status);
+        idx->doc_ptrs, v.tok2pos, v.codes, v.factors, lut, cb1, refined_docs, num_refined, k_refine, scores,
+        status);
     return chm::launch_status("refine_1bit_flagged");
 }
 

@@ -294,8 +294,8 @@ static size_t rt_plan_smem(int cap) {
 }
 
 // One warp per item: its record and, per row, the code index (the cluster
-// position through tok2pos for 1-bit codes, the token id for full codes;
-// kRtNoRow past the item's tokens).
+// position through tok2pos when it is given, else the token id: full codes
+// and the token-order 1-bit codes; kRtNoRow past the item's tokens).
 template <bool kFull>
 __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
                                const int32_t* __restrict__ docs, int cap, const int2* __restrict__ items,
@@ -362,7 +362,7 @@ __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint3
         uint32_t v[kRtRows / 32];
 #pragma unroll
         for (int g = 0; g < kRtRows / 32; ++g)
-            v[g] = token[g] < 0 ? kRtNoRow : kFull ? (uint32_t)token[g] : __ldg(tok2pos + token[g]);
+            v[g] = token[g] < 0 ? kRtNoRow : tok2pos == nullptr ? (uint32_t)token[g] : __ldg(tok2pos + token[g]);
 #pragma unroll
         for (int g = 0; g < kRtRows / 32; ++g) rw[32 * g + lane] = v[g];
     }
@@ -841,9 +841,10 @@ struct RtSizer {
     }
 };
 
+// tok2pos: NULL when the rows' codes are in token order.
 template <bool kFull>
-static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, const int32_t* counts, int cap,
-                          const RtWork& w, cudaStream_t st) {
+static chm_status rt_plan(const chm_index* idx, const uint32_t* tok2pos, int nq, const int32_t* docs,
+                          const int32_t* counts, int cap, const RtWork& w, cudaStream_t st) {
     refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(w.status, nq, w.stats);
     CHM_TRY(launch_status("refine_status_clear_kernel"));
     const size_t plan_smem = rt_plan_smem(cap);
@@ -853,7 +854,7 @@ static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, con
     CHM_TRY(launch_status("refine_plan_kernel"));
     // one warp per item, 4 warps per block, 128 blocks per query striding over its items
     rt_fill_kernel<kFull><<<dim3(128u, (unsigned)nq), 128, 0, st>>>(
-        idx->doc_ptrs, idx->tok2pos, docs, cap, w.items, w.n_items, w.meta, w.rows);
+        idx->doc_ptrs, tok2pos, docs, cap, w.items, w.n_items, w.meta, w.rows);
     return launch_status("rt_fill_kernel");
 }
 
@@ -946,7 +947,12 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     chm::RtWork w;
     chm::rt_layout(a, nq, k_refine, &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
-    CHM_TRY(chm::rt_plan<false>(idx, nq, refined_docs, num_refined, k_refine, w, st));
+    // the token-order copies make each refined doc one contiguous span of codes
+    const bool tok_order = idx->codes1_tok != nullptr && idx->factor1_tok != nullptr;
+    const uint8_t* codes = tok_order ? idx->codes1_tok : idx->codes1;
+    const float* factors = tok_order ? idx->factor1_tok : idx->factor1;
+    CHM_TRY(chm::rt_plan<false>(idx, tok_order ? nullptr : idx->tok2pos, nq, refined_docs, num_refined, k_refine, w,
+                                st));
     chm::rt_query_kernel<false, 1><<<nq, 256, 0, st>>>(rot, cb1, w.qtile, w.qem);
     CHM_TRY(chm::launch_status("rt_query_kernel"));
     const size_t smem = chm::refine_tc_smem_bytes<false, 1>();
@@ -955,8 +961,8 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     dim3 grid;
     CHM_TRY(chm::rt_grid(chm::refine_tc_kernel<false, 1>, smem, nq, k_refine, &grid));
     chm::refine_tc_kernel<false, 1><<<grid, chm::kRtThreads, smem, st>>>(
-        w.meta, w.rows, idx->codes1, idx->factor1, cb1, rot, lut, w.qtile, w.qem, k_refine, w.n_items, scores,
-        w.status, w.stats);
+        w.meta, w.rows, codes, factors, cb1, rot, lut, w.qtile, w.qem, k_refine, w.n_items, scores, w.status,
+        w.stats);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
     return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, w.big, w.n_big,
                                     w.status, st);
@@ -983,7 +989,7 @@ extern "C" chm_status chm_fullbit_score_tc(const chm_index* idx, int32_t nq, con
     chm::RtWork w;
     chm::rt_layout(a, nq, fb_cap, &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
-    CHM_TRY(chm::rt_plan<true>(idx, nq, fb_docs, num_fb, fb_cap, w, st));
+    CHM_TRY(chm::rt_plan<true>(idx, nullptr, nq, fb_docs, num_fb, fb_cap, w, st));
     switch (w_bits) {
         case 2: CHM_TRY(chm::launch_fullbit_tc<2>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
         case 3: CHM_TRY(chm::launch_fullbit_tc<3>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;

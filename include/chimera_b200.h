@@ -60,6 +60,13 @@ typedef struct {
     const void* centroids_bf16;  /* [n_clusters * 128] bf16 copy for the tensor-core
                                     probe; NULL selects the exact SIMT probe */
     const float* centroid_norm_max; /* device scalar max ||c||^2 (with centroids_bf16) */
+    /* The 1-bit codes and factors again in token order (a document's tokens
+     * contiguous), read by the refinement stage as one span per document.
+     * Built from the cluster-ordered arrays by chm_token_order_1bit.  NULL:
+     * refinement gathers through tok2pos (the reference's layout,
+     * kernels.cu:580-600). */
+    const uint8_t* codes1_tok;   /* [n_tokens * 16] */
+    const float* factor1_tok;    /* [n_tokens] */
 } chm_index;
 
 typedef struct {
@@ -279,6 +286,13 @@ chm_status chm_build_assign(const float* x, int64_t n, int32_t dim, const float*
 chm_status chm_build_encode(const uint8_t* flips, const float* x, int64_t n, int32_t dim,
                             int32_t ex_bits, uint8_t* codes1, float* f1, uint8_t* full,
                             float* ff, float* rot, void* stream);
+
+/* Token-order copy of the cluster-ordered 1-bit arrays:
+ * codes_tok[t] = codes1[tok2pos[t]], factor_tok[t] = factor1[tok2pos[t]]
+ * (the inverse of reorder_by_cluster's permutation, build_index.cu:328-363).
+ * codes_tok [n*16], factor_tok [n]. */
+chm_status chm_token_order_1bit(const uint8_t* codes1, const float* factor1, const uint32_t* tok2pos, int64_t n,
+                                uint8_t* codes_tok, float* factor_tok, void* stream);
 
 /* ||x||^2 of n rows of width 128 as a sequential fma chain. */
 chm_status chm_row_norms(const float* x, int64_t n, float* out, void* stream);

@@ -46,11 +46,14 @@ def C_view(d):
     return C.byref(d.view)
 
 
+@pytest.mark.parametrize("layout", ["token", "cluster"])
 @pytest.mark.parametrize("name", ["mini", "small", "long"])
-def test_refine_tc_matches_simt_on_oracle_lists(name):
+def test_refine_tc_matches_simt_on_oracle_lists(name, layout):
+    """Both kernels on both 1-bit layouts: the token-order copies (one span
+    per doc) and the cluster-ordered arrays gathered through tok2pos."""
     c = _corpus.corpus(name)
     cfg = c["cfg"]
-    d = _corpus.device_index(c, torch)
+    d = _corpus.device_index(c, torch).with_token_order(layout == "token")
     nq = c["qrot"].shape[0]
     kr = cfg.k_refine
     lists = np.full((nq, kr), -1, np.int32)
