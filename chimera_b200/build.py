@@ -33,7 +33,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 CU_SOURCES = ["capi.cu", "query_prep.cu", "probe.cu", "stage1.cu", "refine.cu", "build.cu", "tcgemm.cu",
-              "shard.cu", "refine_tc.cu"]
+              "shard.cu", "refine_tc.cu", "stage1_bound.cu"]
 HOST_SOURCES = ["host/chimera_index.cpp", "host/io.cpp", "host/rng.cpp"]
 
 

@@ -40,12 +40,13 @@ class ChmError(RuntimeError):
 class ChmIndex(C.Structure):
     _fields_ = [
         ("n_tokens", C.c_int64), ("num_docs", C.c_int64), ("n_clusters", C.c_int64),
-        ("ex_bits", C.c_int32), ("dim", C.c_int32), ("max_list_len", C.c_int32), ("reserved", C.c_int32),
+        ("ex_bits", C.c_int32), ("dim", C.c_int32), ("max_list_len", C.c_int32), ("max_doc_len", C.c_int32),
         ("cluster_pos", C.c_void_p), ("codes1", C.c_void_p), ("factor1", C.c_void_p),
         ("doc_ids", C.c_void_p), ("tok2pos", C.c_void_p), ("doc_ptrs", C.c_void_p),
         ("full_codes", C.c_void_p), ("full_factors", C.c_void_p), ("centroids", C.c_void_p),
         ("centroid_norms", C.c_void_p), ("flips", C.c_void_p), ("centroids_bf16", C.c_void_p),
         ("centroid_norm_max", C.c_void_p), ("codes1_tok", C.c_void_p), ("factor1_tok", C.c_void_p),
+        ("tok_cluster", C.c_void_p),
     ]
 
 
@@ -95,6 +96,8 @@ EXPORTS = {
     "chm_build_encode": ([V, V, I64, I32, I32, V, V, V, V, V, V], C.c_int),
     "chm_row_norms": ([V, I64, V, V], C.c_int),
     "chm_token_order_1bit": ([V, V, V, I64, V, V, V], C.c_int),
+    "chm_token_clusters": ([V, I64, V, I64, V, V], C.c_int),
+    "chm_stage1_table_queries": ([V, I32, I32, I32, I32, V, SZ, V, V], C.c_int),
 }
 
 
@@ -155,13 +158,15 @@ class DeviceIndex:
 
     FIELDS = ("cluster_pos", "codes1", "factor1", "doc_ids", "tok2pos", "doc_ptrs", "full_codes",
               "full_factors", "centroids", "centroid_norms", "flips", "centroids_bf16", "centroid_norm_max",
-              "codes1_tok", "factor1_tok")
+              "codes1_tok", "factor1_tok", "tok_cluster")
 
     def __init__(self, *, dim, ex_bits, tensor_core_probe=True, token_order=True, codes1_tok=None,
-                 factor1_tok=None, **arrays):
+                 factor1_tok=None, tok_cluster=None, **arrays):
         """`token_order`: keep a token-order copy of the 1-bit codes and
-        factors (20 B per token) for the refinement stage; given as
-        codes1_tok / factor1_tok, or gathered here through tok2pos."""
+        factors (20 B per token) and every token's cluster (4 B per token),
+        given as codes1_tok / factor1_tok / tok_cluster or derived here from
+        the cluster-ordered arrays.  Refinement then reads each doc as one
+        span, and stage 1 can take its dense-bound path."""
         import torch
         self.torch = torch
         self.dim = int(dim)
@@ -181,7 +186,9 @@ class DeviceIndex:
         self.n_clusters = int(self.cluster_pos.shape[0] - 1)
         lens = self.cluster_pos[1:] - self.cluster_pos[:-1]
         self.max_list_len = int(lens.max().item()) if self.n_clusters else 0
-        self.codes1_tok = self.factor1_tok = None
+        self.codes1_tok = self.factor1_tok = self.tok_cluster = None
+        dl = self.doc_ptrs[1:] - self.doc_ptrs[:-1]
+        self.max_doc_len = int(dl.max().item()) if self.num_docs else 0
         if token_order:
             if codes1_tok is None or factor1_tok is None:
                 codes1_tok = torch.empty(self.n_tokens, 16, dtype=torch.uint8, device=dev)
@@ -189,12 +196,16 @@ class DeviceIndex:
                 check(lib().chm_token_order_1bit(_ptr(self.codes1), _ptr(self.factor1), _ptr(self.tok2pos),
                                                  self.n_tokens, _ptr(codes1_tok), _ptr(factor1_tok), st),
                       "token_order_1bit")
-            self.codes1_tok, self.factor1_tok = codes1_tok, factor1_tok
+            if tok_cluster is None:
+                tok_cluster = torch.empty(self.n_tokens, dtype=torch.int32, device=dev)
+                check(lib().chm_token_clusters(_ptr(self.cluster_pos), self.n_clusters, _ptr(self.tok2pos),
+                                               self.n_tokens, _ptr(tok_cluster), st), "token_clusters")
+            self.codes1_tok, self.factor1_tok, self.tok_cluster = codes1_tok, factor1_tok, tok_cluster
         ptrs = [self._p(getattr(self, k)) if getattr(self, k) is not None else 0 for k in self.FIELDS]
         if not tensor_core_probe:
             ptrs[11] = ptrs[12] = 0
         self.view = ChmIndex(self.n_tokens, self.num_docs, self.n_clusters, self.ex_bits, self.dim,
-                             self.max_list_len, 0, *ptrs)
+                             self.max_list_len, self.max_doc_len, *ptrs)
 
     def with_probe(self, tensor_core: bool):
         """The same arrays with the tensor-core (True) or SIMT (False) probe."""
@@ -208,12 +219,25 @@ class DeviceIndex:
 
     def with_token_order(self, on: bool):
         """The same arrays with refinement reading the token-order 1-bit
-        copies (True) or gathering the cluster-ordered ones (False)."""
+        copies (True) or gathering the cluster-ordered ones (False).  Without
+        them stage 1 also keeps to its hash-table path."""
         if on and self.codes1_tok is None:
             raise ValueError("this index has no token-order 1-bit copies")
         v = ChmIndex.from_buffer_copy(self.view)
         v.codes1_tok = self._p(self.codes1_tok) if on else 0
         v.factor1_tok = self._p(self.factor1_tok) if on else 0
+        clone = object.__new__(DeviceIndex)
+        clone.__dict__.update(self.__dict__)
+        clone.view = v
+        return clone
+
+    def with_dense_stage1(self, on: bool):
+        """The same arrays with stage 1's dense-bound path enabled (True) or
+        its hash-table path only (False)."""
+        if on and self.tok_cluster is None:
+            raise ValueError("this index has no token clusters")
+        v = ChmIndex.from_buffer_copy(self.view)
+        v.tok_cluster = self._p(self.tok_cluster) if on else 0
         clone = object.__new__(DeviceIndex)
         clone.__dict__.update(self.__dict__)
         clone.view = v
@@ -340,7 +364,7 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
                        codes1=codes1[inv].contiguous(), factor1=f1[inv].contiguous(),
                        doc_ids=owner[inv].contiguous(), tok2pos=tok2pos, doc_ptrs=doc_ptrs,
                        full_codes=full, full_factors=ff, centroids=rot_c, centroid_norms=cnorm,
-                       flips=flips, codes1_tok=codes1, factor1_tok=f1), \
+                       flips=flips, codes1_tok=codes1, factor1_tok=f1, tok_cluster=assign), \
         dict(assign=assign, inv=inv, token_codes1=codes1, token_f1=f1)
 
 

@@ -202,3 +202,33 @@ extern "C" chm_status chm_token_order_1bit(const uint8_t* codes1, const float* f
         factor_tok);
     return chm::launch_status("token_order_1bit_kernel");
 }
+
+namespace chm {
+
+// tok_cluster[t]: the last cluster c with cluster_pos[c] <= tok2pos[t]
+// (empty lists share their start with the next list, so the last such c is
+// the one whose list holds the position).
+__global__ void __launch_bounds__(256) token_clusters_kernel(const int64_t* __restrict__ cluster_pos,
+                                                             int64_t n_clusters, const uint32_t* __restrict__ tok2pos,
+                                                             int64_t n, uint32_t* __restrict__ tok_cluster) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    const int64_t pos = __ldg(tok2pos + t);
+    int64_t lo = 0, hi = n_clusters;  // invariant: cluster_pos[lo] <= pos < cluster_pos[hi]
+    while (hi - lo > 1) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (__ldg(cluster_pos + mid) <= pos) lo = mid; else hi = mid;
+    }
+    tok_cluster[t] = (uint32_t)lo;
+}
+
+}  // namespace chm
+
+extern "C" chm_status chm_token_clusters(const int64_t* cluster_pos, int64_t n_clusters, const uint32_t* tok2pos,
+                                         int64_t n, uint32_t* tok_cluster, void* stream) {
+    if (n < 0 || n_clusters <= 0 || n_clusters > 0xFFFFFFFFll) return CHM_ERR_INVALID;
+    if (n == 0) return CHM_OK;
+    chm::token_clusters_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        cluster_pos, n_clusters, tok2pos, n, tok_cluster);
+    return chm::launch_status("token_clusters_kernel");
+}

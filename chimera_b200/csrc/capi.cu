@@ -27,7 +27,7 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
                       int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
                       int64_t* num_candidates, void* ws, size_t ws_bytes, cudaStream_t st,
                       bool force_marks, uint32_t* flags_out, int log2_extra);
-size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra);
+size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra, int k_refine);
 
 __global__ void fold_flags_kernel(const uint32_t* __restrict__ flags, int32_t* __restrict__ num_results,
                                   int n) {
@@ -69,7 +69,7 @@ static void layout(A& a, const chm_index* idx, const chm_search_params* p, Searc
     const size_t probe_bytes = use_tc_probe(idx, p)
                                    ? chm_probe_tc_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe)
                                    : chm_probe_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe);
-    const size_t s1_bytes = stage1_bytes(idx, p->batch, p->nprobe, p->table_log2_extra);
+    const size_t s1_bytes = stage1_bytes(idx, p->batch, p->nprobe, p->table_log2_extra, p->k_refine);
     const size_t rt_bytes = chm_fullbit_score_tc_workspace_bytes(p->batch, p->k_refine);
     auto rot = a.template take<float>(ntok * kDim);
     auto cb1 = a.template take<float>(ntok);

@@ -148,7 +148,8 @@ struct chimera_index::Impl {
     bool ready = false;
 
     DevBuf d_cluster_pos, d_codes1, d_factor1, d_doc_ids, d_tok2pos, d_doc_ptrs, d_full, d_ff, d_cent,
-        d_cnorm, d_flips, d_cent_bf16, d_cnmax, d_ws, d_q, d_res, d_nres, d_codes1_tok, d_factor1_tok;
+        d_cnorm, d_flips, d_cent_bf16, d_cnmax, d_ws, d_q, d_res, d_nres, d_codes1_tok, d_factor1_tok,
+        d_tok_cluster;
     size_t ws_bytes = 0;
     int ws_batch = 0;
     int table_extra = 0;
@@ -166,7 +167,7 @@ struct chimera_index::Impl {
         }
         for (DevBuf* b : {&d_cluster_pos, &d_codes1, &d_factor1, &d_doc_ids, &d_tok2pos, &d_doc_ptrs, &d_full,
                           &d_ff, &d_cent, &d_cnorm, &d_flips, &d_cent_bf16, &d_cnmax, &d_ws, &d_q, &d_res,
-                          &d_nres, &d_codes1_tok, &d_factor1_tok})
+                          &d_nres, &d_codes1_tok, &d_factor1_tok, &d_tok_cluster})
             b->reset();
         ready = false;
         ws_bytes = 0;
@@ -232,7 +233,7 @@ struct chimera_index::Impl {
         if (clustered.size() != n * 28) throw std::runtime_error("Invalid in-memory clustered index payload");
         size_t free_mem = 0, total_mem = 0;
         check_cuda(cudaMemGetInfo(&free_mem, &total_mem), "cudaMemGetInfo");
-        const size_t need = clustered.size() + full_codes.size() + n * 24 + centroids_rot.size() * 4;
+        const size_t need = clustered.size() + full_codes.size() + n * 28 + centroids_rot.size() * 4;
         if (free_mem <= need)
             throw std::runtime_error("Insufficient GPU memory for the index: need " + std::to_string(need) +
                                      " bytes, have " + std::to_string(free_mem) + " bytes free");
@@ -264,16 +265,24 @@ struct chimera_index::Impl {
                                           static_cast<int64_t>(n), d_codes1_tok.as<uint8_t>(),
                                           d_factor1_tok.as<float>(), stream),
                      "token-order 1-bit copy");
+        // every token's cluster (stage 1's dense-bound path)
+        d_tok_cluster.alloc(n * sizeof(uint32_t));
+        throw_status(chm_token_clusters(d_cluster_pos.as<int64_t>(), static_cast<int64_t>(n_clusters),
+                                        d_tok2pos.as<uint32_t>(), static_cast<int64_t>(n), d_tok_cluster.as<uint32_t>(),
+                                        stream),
+                     "token clusters");
+        int32_t max_doc = 0;
+        for (int len : doc_lens) max_doc = std::max<int32_t>(max_doc, len);
         int32_t max_list = 0;
         for (size_t c = 0; c < n_clusters; ++c)
             max_list = std::max<int32_t>(max_list, static_cast<int32_t>(cluster_pos[c + 1] - cluster_pos[c]));
         view = chm_index{static_cast<int64_t>(n), static_cast<int64_t>(num_docs), static_cast<int64_t>(n_clusters),
-                         static_cast<int32_t>(ex_bits), static_cast<int32_t>(d), max_list, 0,
+                         static_cast<int32_t>(ex_bits), static_cast<int32_t>(d), max_list, max_doc,
                          d_cluster_pos.as<int64_t>(), d_codes1.as<uint8_t>(), d_factor1.as<float>(),
                          d_doc_ids.as<int32_t>(), d_tok2pos.as<uint32_t>(), d_doc_ptrs.as<int64_t>(),
                          d_full.as<uint8_t>(), d_ff.as<float>(), d_cent.as<float>(), d_cnorm.as<float>(),
                          d_flips.as<uint8_t>(), d_cent_bf16.p, d_cnmax.as<float>(), d_codes1_tok.as<uint8_t>(),
-                         d_factor1_tok.as<float>()};
+                         d_factor1_tok.as<float>(), d_tok_cluster.as<uint32_t>()};
         check_cuda(cudaStreamSynchronize(stream), "index upload");
         ready = true;
     }

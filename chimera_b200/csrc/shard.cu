@@ -82,7 +82,7 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
                       const uint32_t* labels, int32_t nprobe, int32_t k_refine, int32_t* refined_docs,
                       float* refined_partial, int32_t* num_refined, int64_t* num_candidates, void* ws,
                       size_t ws_bytes, cudaStream_t st, bool force_marks, uint32_t* flags_out, int log2_extra);
-size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra);
+size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra, int k_refine);
 
 }  // namespace chm
 
@@ -113,7 +113,8 @@ extern "C" chm_status chm_shard_localize(int32_t nq, int32_t cap, const int32_t*
 extern "C" size_t chm_stage1_ex_workspace_bytes(const chm_index* idx, int32_t nq, int32_t nprobe,
                                                 int32_t table_log2_extra) {
     if (!idx || nq <= 0 || nprobe <= 0 || table_log2_extra < 0 || table_log2_extra > 8) return 0;
-    return chm::stage1_bytes(idx, nq, nprobe, table_log2_extra);
+    // sized for the largest k_refine: the call's own k_refine is not an argument
+    return chm::stage1_bytes(idx, nq, nprobe, table_log2_extra, CHM_MAX_K_REFINE);
 }
 
 extern "C" chm_status chm_stage1_ex(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,

@@ -58,7 +58,26 @@ struct Stage1Ctx {
     uint64_t* tables;       // [nq][H]
     int log2h;
     uint32_t* flags;        // [nq] bit0: table overflow
+    const uint32_t* active; // [nq] nonzero: run this query (NULL: every query)
 };
+
+__device__ __forceinline__ bool inactive(const uint32_t* active, int q) { return active != nullptr && active[q] == 0u; }
+
+__global__ void set_ones_kernel(uint32_t* out, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = 1u;
+}
+
+// Clears the tables of the active queries (cudaMemsetAsync covers the all-active case).
+__global__ void __launch_bounds__(256) stage1_clear_kernel(uint64_t* __restrict__ tables, int log2h,
+                                                           const uint32_t* __restrict__ active) {
+    const int q = blockIdx.y;
+    if (inactive(active, q)) return;
+    uint4* t = reinterpret_cast<uint4*>(tables + ((size_t)q << log2h));
+    const size_t n = ((size_t)1 << log2h) / 2;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        t[i] = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+}
 
 // Exclusive prefix over list lengths of one query token's probed lists.
 __device__ void probe_prefix(const Stage1Ctx& c, const uint32_t* labels, int64_t* s_start,
@@ -115,6 +134,7 @@ __global__ void __launch_bounds__(kScoreThreads) stage1_score_kernel(Stage1Ctx c
     const int t = blockIdx.x / splits;
     const int split = blockIdx.x % splits;
     const int q = blockIdx.y;
+    if (inactive(c.active, q)) return;
     const float* lut = c.lut + ((size_t)q * kQ + t) * kLutPerQ;
     for (int i = threadIdx.x; i < kLutPerQ; i += blockDim.x) s_lut[i] = lut[i];
     probe_prefix(c, c.labels + ((size_t)q * kQ + t) * c.nprobe, s_start, s_prefix);
@@ -155,7 +175,7 @@ __global__ void __launch_bounds__(kScoreThreads) stage1_mark_kernel(
     const int t = blockIdx.x / splits;
     const int split = blockIdx.x % splits;
     const int q = blockIdx.y;
-    if ((int)n_pos[q] >= k_refine) return;
+    if (inactive(c.active, q) || (int)n_pos[q] >= k_refine) return;
     probe_prefix(c, c.labels + ((size_t)q * kQ + t) * c.nprobe, s_start, s_prefix);
     const int total = s_prefix[c.nprobe];
     const int per = (total + splits - 1) / splits;
@@ -204,7 +224,7 @@ __device__ __forceinline__ float doc_tree_sum(const uint64_t* ent, int n, uint32
 // more entries need the ordered tree.
 __global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
     const uint64_t* __restrict__ tables, int log2h, uint64_t* __restrict__ keys, int64_t key_cap,
-    uint32_t* __restrict__ n_pos, uint32_t* __restrict__ flags) {
+    uint32_t* __restrict__ n_pos, uint32_t* __restrict__ flags, const uint32_t* __restrict__ active) {
     __shared__ uint64_t s_ent[kCombineWarps][kBinCap];
     __shared__ uint64_t s_out[kCombineWarps][2 * kBinCap];
     __shared__ float s_scr[kCombineWarps][32];
@@ -212,6 +232,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) stage1_combine_kernel(
     // queries vary fastest across the grid so that concurrently running blocks
     // spread their output-counter atomics over many queries
     const int q = blockIdx.x;
+    if (inactive(active, q)) return;
     const uint32_t hmask = (1u << log2h) - 1;
     const uint32_t nbins = 1u << (log2h - kBinShift);
     const uint32_t nbins_mask = nbins - 1;
@@ -489,7 +510,7 @@ __global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
     int32_t* __restrict__ refined_docs, float* __restrict__ refined_partial,
     int32_t* __restrict__ num_refined, int64_t* __restrict__ num_candidates,
     uint32_t* __restrict__ flags, const uint64_t* __restrict__ ckeys, const uint32_t* __restrict__ ccnt,
-    const uint32_t* __restrict__ pivot) {
+    const uint32_t* __restrict__ pivot, const uint32_t* __restrict__ active) {
     extern __shared__ uint64_t s_dyn[];
     uint64_t* s_out = s_dyn;                                   // [sort_n]
     __shared__ uint32_t s_hist[4096];
@@ -498,6 +519,7 @@ __global__ void __launch_bounds__(kSelectThreads) stage1_select_kernel(
     __shared__ uint64_t s_prefix, s_pmask;
     __shared__ int s_need, s_done;
     const int q = blockIdx.x;
+    if (inactive(active, q)) return;
     // a long list's compacted keys (all keys of its top k_refine), unless they overflowed
     const bool compacted = pivot[q] != kNoPivot && ccnt[q] <= (uint32_t)kPreCap;
     const uint64_t* qk = compacted ? ckeys + (size_t)q * kPreCap : keys + (size_t)q * key_cap;
@@ -660,59 +682,90 @@ int64_t stage1_words(const chm_index* idx) { return (idx->num_docs + 31) / 32; }
 }  // namespace chm
 
 namespace chm {
-size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra) {
-    Sizer s;
+size_t bound_bytes(const chm_index* idx, int nq, int nprobe, int k_refine);
+bool bound_enabled(const chm_index* idx, int nprobe, int k_refine);
+chm_status bound_run(const chm_index* idx, int nq, const float* lut, const float* cb1, const uint32_t* labels,
+                     int nprobe, int k_refine, int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
+                     uint32_t* need_fb, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// Workspace: the hash-table path's arrays, then (when the index enables it)
+// the dense-bound path's.
+template <typename A>
+struct Stage1Layout {
+    uint64_t* tables;
+    uint64_t* keys;
+    uint32_t* bitmaps;
+    uint32_t* n_pos;
+    uint32_t* flags;
+    uint32_t* hist;
+    uint32_t* pivot;
+    uint32_t* ccnt;
+    uint64_t* ckeys;
+    uint32_t* need_fb;
+    void* bound_ws;
+    size_t bound_bytes;
+};
+
+template <typename A>
+static void stage1_layout(A& a, const chm_index* idx, int nq, int nprobe, int extra, size_t bbytes,
+                          Stage1Layout<A>* o) {
     const int l = stage1_log2h(idx, nprobe, extra);
-    s.take<uint64_t>((size_t)nq << l);
-    s.take<uint64_t>((size_t)nq * stage1_key_cap(idx));
-    s.take<uint32_t>((size_t)nq * stage1_words(idx));
-    s.take<uint32_t>((size_t)nq);
-    s.take<uint32_t>((size_t)nq);
-    s.take<uint32_t>(stage1_hist_words(nq));                        // histograms
-    s.take<uint32_t>((size_t)nq);                                   // pivots
-    s.take<uint32_t>((size_t)nq);                                   // compacted counts
-    s.take<uint64_t>((size_t)nq * kPreCap);                         // compacted keys
-    return s.off;
+    auto tables = a.template take<uint64_t>((size_t)nq << l);
+    auto keys = a.template take<uint64_t>((size_t)nq * stage1_key_cap(idx));
+    auto bitmaps = a.template take<uint32_t>((size_t)nq * stage1_words(idx));
+    auto n_pos = a.template take<uint32_t>((size_t)nq);
+    auto flags = a.template take<uint32_t>((size_t)nq);
+    auto hist = a.template take<uint32_t>(stage1_hist_words(nq));
+    auto pivot = a.template take<uint32_t>((size_t)nq);
+    auto ccnt = a.template take<uint32_t>((size_t)nq);
+    auto ckeys = a.template take<uint64_t>((size_t)nq * kPreCap);
+    auto need_fb = a.template take<uint32_t>((size_t)nq);
+    auto bws = a.template take<char>(bbytes);
+    if (o)
+        *o = Stage1Layout<A>{(uint64_t*)tables, (uint64_t*)keys, (uint32_t*)bitmaps, (uint32_t*)n_pos,
+                             (uint32_t*)flags, (uint32_t*)hist, (uint32_t*)pivot, (uint32_t*)ccnt, (uint64_t*)ckeys,
+                             (uint32_t*)need_fb, (void*)bws, bbytes};
+}
+
+struct S1Sizer {
+    Sizer s;
+    template <typename T>
+    void* take(size_t n) {
+        s.take<T>(n);
+        return nullptr;
+    }
+};
+
+size_t stage1_bytes(const chm_index* idx, int32_t nq, int32_t nprobe, int extra, int k_refine) {
+    S1Sizer s;
+    stage1_layout(s, idx, nq, nprobe, extra, bound_bytes(idx, nq, nprobe, k_refine), (Stage1Layout<S1Sizer>*)nullptr);
+    return s.s.off;
 }
 }  // namespace chm
 
 extern "C" size_t chm_stage1_workspace_bytes(const chm_index* idx, int32_t nq, int32_t nprobe,
                                              int32_t k_refine) {
-    (void)k_refine;
-    return chm::stage1_bytes(idx, nq, nprobe, 0);
+    return chm::stage1_bytes(idx, nq, nprobe, 0, k_refine);
 }
 
 namespace chm {
-// extra_log2h lets the host retry a query batch with a larger table.
-chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
-                      const uint32_t* labels, int32_t nprobe, int32_t k_refine,
-                      int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
-                      int64_t* num_candidates, void* ws, size_t ws_bytes, cudaStream_t st,
-                      bool force_marks, uint32_t* flags_out, int log2_extra) {
-    if (nq <= 0) return CHM_OK;
-    if (nprobe <= 0 || nprobe > CHM_MAX_NPROBE || k_refine <= 0 || k_refine > CHM_MAX_K_REFINE)
-        return CHM_ERR_INVALID;
-    if (idx->num_docs >= (1ll << 27)) return CHM_ERR_UNSUPPORTED;
-    const int l = stage1_log2h(idx, nprobe, log2_extra);
+// The hash-table path over the queries `active` selects (NULL: all).
+static chm_status stage1_table_run(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
+                                   const uint32_t* labels, int32_t nprobe, int32_t k_refine, int32_t* refined_docs,
+                                   float* refined_partial, int32_t* num_refined, int64_t* num_candidates,
+                                   const Stage1Layout<Arena>& w, int l, cudaStream_t st, bool force_marks,
+                                   const uint32_t* active) {
     const int64_t key_cap = stage1_key_cap(idx);
     const int64_t words = stage1_words(idx);
-    Arena a(ws, ws_bytes);
-    uint64_t* tables = a.take<uint64_t>((size_t)nq << l);
-    uint64_t* keys = a.take<uint64_t>((size_t)nq * key_cap);
-    uint32_t* bitmaps = a.take<uint32_t>((size_t)nq * words);
-    uint32_t* n_pos = a.take<uint32_t>((size_t)nq);
-    uint32_t* flags = a.take<uint32_t>((size_t)nq);
     const int slices = stage1_pre_slices(nq);
-    uint32_t* hist = a.take<uint32_t>(stage1_hist_words(nq));
-    uint32_t* pivot = a.take<uint32_t>((size_t)nq);
-    uint32_t* ccnt = a.take<uint32_t>((size_t)nq);
-    uint64_t* ckeys = a.take<uint64_t>((size_t)nq * kPreCap);
-    if (a.overflow) return CHM_ERR_CAPACITY;
-    CHM_CUDA(cudaMemsetAsync(tables, 0xFF, sizeof(uint64_t) * ((size_t)nq << l), st));
-    CHM_CUDA(cudaMemsetAsync(n_pos, 0, sizeof(uint32_t) * nq, st));
-    CHM_CUDA(cudaMemsetAsync(flags, 0, sizeof(uint32_t) * nq, st));
+    if (active == nullptr) {
+        CHM_CUDA(cudaMemsetAsync(w.tables, 0xFF, sizeof(uint64_t) * ((size_t)nq << l), st));
+    } else {
+        stage1_clear_kernel<<<dim3(256u, (unsigned)nq), 256, 0, st>>>(w.tables, l, active);
+        CHM_TRY(launch_status("stage1_clear_kernel"));
+    }
     Stage1Ctx c{idx->cluster_pos, idx->codes1, idx->factor1, idx->doc_ids, idx->n_clusters,
-                idx->num_docs, lut, cb1, labels, nprobe, tables, l, flags};
+                idx->num_docs, lut, cb1, labels, nprobe, w.tables, l, w.flags, active};
     const double mean_list = (double)idx->n_tokens / (double)(idx->n_clusters > 0 ? idx->n_clusters : 1);
     const double visits_per_t = nprobe * mean_list;
     int splits = (int)(visits_per_t / (kScoreThreads * 8));
@@ -725,31 +778,64 @@ chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const 
     // enough blocks for about 8 resident per SM over all queries; warps stride over bins
     const int64_t want_blocks = std::max<int64_t>(1, (int64_t)148 * 8 * 4 / std::max(1, nq));
     dim3 g2(nq, (unsigned)std::min<int64_t>(std::min<int64_t>(nbins / kCombineWarps, want_blocks), 65535));
-    stage1_combine_kernel<<<g2, kCombineWarps * 32, 0, st>>>(tables, l, keys, key_cap, n_pos, flags);
+    stage1_combine_kernel<<<g2, kCombineWarps * 32, 0, st>>>(w.tables, l, w.keys, key_cap, w.n_pos, w.flags, active);
     CHM_TRY(launch_status("stage1_combine_kernel"));
-    CHM_CUDA(cudaMemsetAsync(bitmaps, 0, sizeof(uint32_t) * (size_t)nq * words, st));
+    CHM_CUDA(cudaMemsetAsync(w.bitmaps, 0, sizeof(uint32_t) * (size_t)nq * words, st));
     // queries whose positives fall short of k_refine get the visited-doc bitmap
-    stage1_mark_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits, n_pos,
-                                                     force_marks ? (1 << 30) : k_refine, bitmaps, words);
+    stage1_mark_kernel<<<g1, kScoreThreads, 0, st>>>(c, splits, w.n_pos, force_marks ? (1 << 30) : k_refine,
+                                                     w.bitmaps, words);
     CHM_TRY(launch_status("stage1_mark_kernel"));
     int sort_cap = 1;
     while (sort_cap < k_refine) sort_cap <<= 1;
     const size_t smem = sizeof(uint64_t) * sort_cap;
     // static (histogram) + dynamic (sort buffer) can exceed the 48 KB default
     CHM_CUDA(cudaFuncSetAttribute(stage1_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    stage1_hist_kernel<<<dim3((unsigned)slices, (unsigned)nq), kPreThreads, 0, st>>>(keys, key_cap, n_pos, k_refine,
-                                                                                    hist);
+    stage1_hist_kernel<<<dim3((unsigned)slices, (unsigned)nq), kPreThreads, 0, st>>>(w.keys, key_cap, w.n_pos,
+                                                                                    k_refine, w.hist);
     CHM_TRY(launch_status("stage1_hist_kernel"));
-    stage1_pivot_kernel<<<nq, kSelectThreads, 0, st>>>(hist, slices, n_pos, key_cap, k_refine, pivot, ccnt);
+    stage1_pivot_kernel<<<nq, kSelectThreads, 0, st>>>(w.hist, slices, w.n_pos, key_cap, k_refine, w.pivot, w.ccnt);
     CHM_TRY(launch_status("stage1_pivot_kernel"));
-    stage1_compact_kernel<<<dim3((unsigned)slices, (unsigned)nq), kPreThreads, 0, st>>>(keys, key_cap, n_pos, pivot,
-                                                                                       ckeys, ccnt);
+    stage1_compact_kernel<<<dim3((unsigned)slices, (unsigned)nq), kPreThreads, 0, st>>>(w.keys, key_cap, w.n_pos,
+                                                                                       w.pivot, w.ckeys, w.ccnt);
     CHM_TRY(launch_status("stage1_compact_kernel"));
     stage1_select_kernel<<<nq, kSelectThreads, smem, st>>>(
-        keys, key_cap, n_pos, k_refine, bitmaps, words, tables, l, force_marks ? 1 : 0,
-        refined_docs, refined_partial, num_refined, num_candidates, flags, ckeys, ccnt, pivot);
-    CHM_TRY(launch_status("stage1_select_kernel"));
-    if (flags_out) CHM_CUDA(cudaMemcpyAsync(flags_out, flags, sizeof(uint32_t) * nq, cudaMemcpyDeviceToDevice, st));
+        w.keys, key_cap, w.n_pos, k_refine, w.bitmaps, words, w.tables, l, force_marks ? 1 : 0, refined_docs,
+        refined_partial, num_refined, num_candidates, w.flags, w.ckeys, w.ccnt, w.pivot, active);
+    return launch_status("stage1_select_kernel");
+}
+
+// extra_log2h lets the host retry a query batch with a larger table.
+chm_status stage1_run(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
+                      const uint32_t* labels, int32_t nprobe, int32_t k_refine,
+                      int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
+                      int64_t* num_candidates, void* ws, size_t ws_bytes, cudaStream_t st,
+                      bool force_marks, uint32_t* flags_out, int log2_extra) {
+    if (nq <= 0) return CHM_OK;
+    if (nprobe <= 0 || nprobe > CHM_MAX_NPROBE || k_refine <= 0 || k_refine > CHM_MAX_K_REFINE)
+        return CHM_ERR_INVALID;
+    if (idx->num_docs >= (1ll << 27)) return CHM_ERR_UNSUPPORTED;
+    const int l = stage1_log2h(idx, nprobe, log2_extra);
+    // the dense-bound path first (not for the candidate counts, which need
+    // every visited doc); the hash-table path redoes the queries it flags
+    const bool bound = !force_marks && bound_enabled(idx, nprobe, k_refine);
+    Arena a(ws, ws_bytes);
+    Stage1Layout<Arena> w;
+    stage1_layout(a, idx, nq, nprobe, log2_extra, bound ? bound_bytes(idx, nq, nprobe, k_refine) : 0, &w);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_CUDA(cudaMemsetAsync(w.n_pos, 0, sizeof(uint32_t) * nq, st));
+    CHM_CUDA(cudaMemsetAsync(w.flags, 0, sizeof(uint32_t) * nq, st));
+    if (bound) {
+        CHM_TRY(bound_run(idx, nq, lut, cb1, labels, nprobe, k_refine, refined_docs, refined_partial, num_refined,
+                          w.need_fb, w.bound_ws, w.bound_bytes, st));
+        CHM_TRY(stage1_table_run(idx, nq, lut, cb1, labels, nprobe, k_refine, refined_docs, refined_partial,
+                                 num_refined, num_candidates, w, l, st, force_marks, w.need_fb));
+    } else {
+        set_ones_kernel<<<(nq + 255) / 256, 256, 0, st>>>(w.need_fb, nq);  // for chm_stage1_table_queries
+        CHM_TRY(launch_status("set_ones_kernel"));
+        CHM_TRY(stage1_table_run(idx, nq, lut, cb1, labels, nprobe, k_refine, refined_docs, refined_partial,
+                                 num_refined, num_candidates, w, l, st, force_marks, nullptr));
+    }
+    if (flags_out) CHM_CUDA(cudaMemcpyAsync(flags_out, w.flags, sizeof(uint32_t) * nq, cudaMemcpyDeviceToDevice, st));
     return CHM_OK;
 }
 }  // namespace chm
@@ -762,4 +848,22 @@ extern "C" chm_status chm_stage1(const chm_index* idx, int32_t nq, const float* 
     return chm::stage1_run(idx, nq, lut, cb1, labels, nprobe, k_refine, refined_docs,
                            refined_partial, num_refined, num_candidates, ws, ws_bytes,
                            (cudaStream_t)stream, num_candidates != nullptr, nullptr, 0);
+}
+
+extern "C" chm_status chm_stage1_table_queries(const chm_index* idx, int32_t nq, int32_t nprobe, int32_t k_refine,
+                                               int32_t table_log2_extra, const void* ws, size_t ws_bytes,
+                                               uint32_t* out, void* stream) {
+    if (!idx || nq <= 0 || !out) return CHM_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool bound = chm::bound_enabled(idx, nprobe, k_refine);
+    if (!bound) {  // every query took the hash-table path
+        chm::set_ones_kernel<<<(nq + 255) / 256, 256, 0, st>>>(out, nq);
+        return chm::launch_status("set_ones_kernel");
+    }
+    chm::Arena a(const_cast<void*>(ws), ws_bytes);
+    chm::Stage1Layout<chm::Arena> w;
+    chm::stage1_layout(a, idx, nq, nprobe, table_log2_extra, chm::bound_bytes(idx, nq, nprobe, k_refine), &w);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_CUDA(cudaMemcpyAsync(out, w.need_fb, sizeof(uint32_t) * nq, cudaMemcpyDeviceToDevice, st));
+    return CHM_OK;
 }

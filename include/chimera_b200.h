@@ -45,7 +45,8 @@ typedef struct {
     int32_t ex_bits;             /* 1..7; full codes use 1 + ex_bits bits/dim */
     int32_t dim;                 /* raw embedding dimension, 64..128 */
     int32_t max_list_len;        /* longest inverted list */
-    int32_t reserved;
+    int32_t max_doc_len;         /* longest document (0: unknown; stage 1 then
+                                    uses its hash-table path only) */
     const int64_t* cluster_pos;  /* [n_clusters + 1] list offsets (ivf.bin) */
     const uint8_t* codes1;       /* [n_tokens * 16] 1-bit codes, cluster order */
     const float* factor1;        /* [n_tokens] 1-bit factors, cluster order */
@@ -67,6 +68,10 @@ typedef struct {
      * kernels.cu:580-600). */
     const uint8_t* codes1_tok;   /* [n_tokens * 16] */
     const float* factor1_tok;    /* [n_tokens] */
+    /* Cluster of every token, token order (IVF_PG's assignment,
+     * ivf_pg.cpp:110-126).  With codes1_tok, factor1_tok and max_doc_len it
+     * enables stage 1's dense-bound path; NULL: hash-table path only. */
+    const uint32_t* tok_cluster; /* [n_tokens] */
 } chm_index;
 
 typedef struct {
@@ -177,6 +182,16 @@ chm_status chm_stage1_ex(const chm_index* index, int32_t nq, const float* lut, c
                          int32_t* refined_docs, float* refined_partial, int32_t* num_refined,
                          uint32_t* flags, int32_t table_log2_extra, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* Which queries of the last chm_stage1 / chm_stage1_ex call on `workspace`
+ * (same index, nq, nprobe, k_refine and table_log2_extra) took the hash-table
+ * path: out[q] = 1 when the dense-bound path flagged query q (fewer positive
+ * docs than k_refine, an unproven boundary or a compaction overflow) or did
+ * not run, 0 when it produced the refined list.  Diagnostics; no reference
+ * counterpart.  out [nq] (device). */
+chm_status chm_stage1_table_queries(const chm_index* index, int32_t nq, int32_t nprobe, int32_t k_refine,
+                                    int32_t table_log2_extra, const void* workspace, size_t workspace_bytes,
+                                    uint32_t* out, void* stream);
 
 /* Segmented 1-bit MaxSim of the refined docs (replaces
  * gather_refined_doc_lengths/positions + one_bit_token_score +
@@ -293,6 +308,12 @@ chm_status chm_build_encode(const uint8_t* flips, const float* x, int64_t n, int
  * codes_tok [n*16], factor_tok [n]. */
 chm_status chm_token_order_1bit(const uint8_t* codes1, const float* factor1, const uint32_t* tok2pos, int64_t n,
                                 uint8_t* codes_tok, float* factor_tok, void* stream);
+
+/* Cluster of every token from the IVF layout: tok_cluster[t] = the cluster
+ * whose list [cluster_pos[c], cluster_pos[c+1]) holds position tok2pos[t].
+ * tok_cluster [n]. */
+chm_status chm_token_clusters(const int64_t* cluster_pos, int64_t n_clusters, const uint32_t* tok2pos, int64_t n,
+                              uint32_t* tok_cluster, void* stream);
 
 /* ||x||^2 of n rows of width 128 as a sequential fma chain. */
 chm_status chm_row_norms(const float* x, int64_t n, float* out, void* stream);
