@@ -138,11 +138,14 @@ def main():
                     help="queries searched by the CPU oracle and compared with the GPU results")
     ap.add_argument("--ref-sample", type=int, default=16, help="queries per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", choices=["probe"], default=None,
+    ap.add_argument("--micro", choices=["probe", "lut"], default=None,
                     help="operator microbench (BASELINE config C2) instead of the search bench")
+    ap.add_argument("--lut-codes", type=int, default=1 << 26, help="codes scored per step by --micro lut")
     args = ap.parse_args()
     if args.micro == "probe":
         return micro_probe(args)
+    if args.micro == "lut":
+        return micro_lut(args)
 
     import torch
     from chimera_b200 import capi, workloads as W, sharded as SH
@@ -336,6 +339,7 @@ def main():
                      "traffic_source": "ncu capture of the same kernel on the c3s case, scaled by refined tokens",
                      "peak_kind": kind},
         "stages_ms_per_step": {s["name"]: round(s["ms"], 3) for s in stages},
+        "stage1_table_path_queries": next(s.get("table_path_queries") for s in stages if s["name"] == "stage1"),
         "stages_algo_gbs": {s["name"]: round(s["algo_bytes"] / (s["ms"] / 1e3) / 1e9, 1)
                             for s in stages if s["algo_bytes"]},
         "gpu_launches": int(launches * args.steps),
@@ -413,6 +417,87 @@ def micro_probe(args):
                       "clocks": clk.summary()}), flush=True)
 
 
+def micro_lut(args):
+    """C2 LUT-scoring microbench: `--lut-codes` (64M) uniform random codes at
+    ex_bits 1, 2, 4 and 7 (stored widths w = 2, 3, 5, 8 bits per dim, the
+    doc_full.bin layout) and the 1-bit cluster code (w = 1), grouped in lists
+    of 64 codes with one fp32 scale factor per list (broadcast to its codes).
+    Every code is scored by the 32 tokens of one query, and each list keeps
+    the MaxSim over its codes: 128 queries x 8,192 lists, through
+    chm_fullbit_score_tc (w = 2..7), chm_fullbit_score (w = 8) and
+    chm_refine_1bit_tc (w = 1).  A step scores all codes once; value = code
+    bytes read (16 w + 4 per code) / time."""
+    import ctypes as C
+    import torch
+    from chimera_b200 import capi
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    L, P, st = capi.lib(), capi._ptr, capi._stream(torch)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    nq, per, tok = 128, 8192, 64
+    n = args.lut_codes
+    docs = n // tok
+    per = min(per, docs // nq)
+    n = nq * per * tok
+    dptr = torch.arange(0, n + 1, tok, dtype=torch.int64, device="cuda")
+    fb_docs = torch.arange(nq * per, dtype=torch.int32, device="cuda").view(nq, per)
+    num = torch.full((nq,), per, dtype=torch.int32, device="cuda")
+    scale = torch.rand(nq * per, generator=g, device="cuda") * 0.5 + 0.05
+    factors = scale.repeat_interleave(tok).contiguous()
+    q = torch.randn(nq * 32, 128, generator=g, device="cuda")
+    q /= q.norm(dim=1, keepdim=True)
+    hbm, _, kind = peaks()
+    out = {}
+    for ex in (0, 1, 2, 4, 7):
+        w = 1 + ex if ex else 1
+        codes = torch.randint(0, 256, (n, 16 * w), dtype=torch.uint8, generator=g, device="cuda")
+        rot = q.contiguous()
+        cb = torch.empty(nq * 32, device="cuda")
+        cbx = torch.empty(nq * 32, device="cuda")
+        lut = torch.empty(nq * 32, 512, device="cuda")
+        flips = torch.zeros(64, dtype=torch.uint8, device="cuda")
+        capi.check(L.chm_prepare_queries(P(flips), 128, max(ex, 1), P(q), nq * 32, P(rot), P(cb), P(cbx), P(lut), st),
+                   "prepare")
+        view = capi.ChmIndex()
+        view.n_tokens, view.num_docs, view.ex_bits, view.dim = n, nq * per, max(ex, 1), 128
+        view.doc_ptrs = dptr.data_ptr()
+        scores = torch.empty(nq, per, device="cuda")
+        if w == 1:
+            view.codes1_tok, view.factor1_tok = codes.data_ptr(), factors.data_ptr()
+            wb = L.chm_refine_1bit_tc_workspace_bytes(nq, per)
+            ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
+            run = lambda: capi.check(L.chm_refine_1bit_tc(C.byref(view), nq, P(lut), P(cb), P(rot), P(fb_docs),
+                                                          P(num), per, P(scores), P(ws), wb, st), "1-bit")
+        else:
+            view.full_codes, view.full_factors = codes.data_ptr(), factors.data_ptr()
+            wb = L.chm_fullbit_score_tc_workspace_bytes(nq, per)
+            ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
+            run = lambda: capi.check(L.chm_fullbit_score_tc(C.byref(view), nq, P(rot), P(cbx), P(fb_docs), P(num),
+                                                            per, P(scores), P(ws), wb, st), "full-bit")
+        for _ in range(args.warmup):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+            e0.record(torch.cuda.current_stream())
+            for _ in range(args.steps):
+                run()
+            e1.record(torch.cuda.current_stream())
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        gbs = n * (16 * w + 4) / (ms / 1e3) / 1e9
+        out[f"w{w}"] = {"ex_bits": ex if ex else None, "ms": round(ms, 3), "gbs": round(gbs, 1),
+                        "frac": round(gbs / hbm, 4), "clocks": clk.summary()}
+        del codes, ws
+        torch.cuda.empty_cache()
+    print(json.dumps({"metric": "LUT scoring HBM GB/s (C2 operator microbench)", "value": out["w5"]["gbs"],
+                      "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "higher_is_better": True, "dtype": "u8 codes, f32 math", "data": "synthetic",
+                      "config": {"workload": f"C2: {n} uniform random codes per width, lists of {tok} codes with "
+                                             f"per-list fp32 factors, 32 query tokens x {nq} queries",
+                                 "value_width": "w5 (ex_bits 4)"},
+                      "widths": out, "peak": hbm, "peak_kind": kind, "l2": "inputs larger than L2"}), flush=True)
+
+
 def profile_stages(torch, capi, index, searcher, q, cfg):
     """Runs the pipeline stage by stage on the launching stream with CUDA
     events between stages (same kernels as chm_search) and returns per-stage
@@ -471,6 +556,8 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         ("final_topk", 1, lambda: L.chm_final_topk(B, P(fd), P(fs), P(nf), p.k_refine, p.k, P(res), P(nres), st)),
     ]
     times = {n: 0.0 for n, _, _ in stages}
+    # (after the runs) which queries stage 1's hash-table path redid
+    table_q = torch.empty(B, dtype=torch.int32, device=dev)
     reps = 3
     stream = torch.cuda.current_stream()
     for r in range(reps + 1):
@@ -516,6 +603,11 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         elif n == "fullbit":
             s["algo_bytes"] = fb_tok * (16 * w + 4)
         out.append(s)
+    capi.check(L.chm_stage1_table_queries(v, B, p.nprobe, p.k_refine, 0, P(sws), sb, P(table_q), st), "table q")
+    torch.cuda.synchronize()
+    for s in out:
+        if s["name"] == "stage1":
+            s["table_path_queries"] = int(table_q.sum().item())
     # the batch's full-bit selection and scores, for the CPU baseline's check
     extra = dict(rot=rot.view(B, 32, 128), cbex=cbex.view(B, 32), fb_docs=fd, num_fb=nf, fb_scores=fs)
     return out, extra
@@ -640,9 +732,12 @@ def run_reference(args, cfg, index, queries, torch, emb, ptr_full):
                                                  "(the reference tree was absent at build time)"}), flush=True)
         return
     nq_total = queries.shape[0]
-    n_run = (W + steps) * per
-    qidx = [i % nq_total for i in range(n_run)]
-    timed = sorted(set(qidx[W * per:]))
+    # warm-up on the last queries; the timed steps run queries 0, 1, 2, ...,
+    # so that recall covers the first --recall-queries queries like our arm's
+    timed_idx = [i % nq_total for i in range(steps * per)]
+    warm_idx = [(nq_total - 1 - i) % nq_total for i in range(W * per)]
+    qidx = warm_idx + timed_idx
+    timed = sorted(set(timed_idx))
     gt_list = ground_truth(torch, emb, ptr_full, queries, cfg.k, timed)
     gt = dict(zip(timed, gt_list))
     del emb
@@ -666,12 +761,16 @@ def run_reference(args, cfg, index, queries, torch, emb, ptr_full):
     ls = np.sort(np.array(lat) * 1e3)
     pct = lambda p: float(np.interp(p / 100 * (len(ls) - 1), np.arange(len(ls)), ls))
     rec = W_recall(np.stack([gt[q] for q in timed]), [res[q] for q in timed], cfg.k)
+    same = [q for q in timed if q < args.recall_queries]
+    rec_same = W_recall(np.stack([gt[q] for q in same]), [res[q] for q in same], cfg.k) if same else None
     line = {**base, "value": round(v, 3), "ms_per_step": round(float(np.sum(ls)) / steps, 3),
             "config": {"workload": wl, "implementation":
                        "reference kernels (kernels.cu, unchanged) + exact-probe shim (cuBLAS SGEMM + select, "
                        "standing in for cuVS CAGRA) + the reference's AVX-512 full-bit scorer on the host, "
                        "one query per call (search_impl.cu:46-574)",
-                       "queries_per_step": per, "recall@100": round(rec, 4), "recall_queries": len(timed),
+                       "queries_per_step": per, "recall@100": round(rec_same, 4) if same else None,
+                       "recall_queries": len(same), "recall@100_all_timed": round(rec, 4),
+                       "timed_queries": len(timed),
                        "latency_ms_single_query": {"p50": round(pct(50), 3), "p99": round(pct(99), 3),
                                                    "mean": round(float(ls.mean()), 3)}},
             "cpu_baseline": {"value": round(v, 3), "unit": "queries/s", "cores": threads, "kind": "reference",

@@ -28,9 +28,10 @@
 //  final   : per query, the candidates by (P desc, doc asc); when
 //            boundary * (1 + eps) < the k_refine-th P, no doc left out can
 //            reach the refined list, which is then exactly the reference's.
-//            Otherwise -- and for queries with fewer than k_refine positive
-//            docs, whose zero-score fill needs the visited-doc bitmap -- the
-//            query is flagged for the hash-table path.
+//            An unproven boundary gets a second round with K' = 12,288 (or
+//            every doc); what is still unproven -- and queries with fewer than
+//            k_refine positive docs, whose zero-score fill needs the
+//            visited-doc bitmap -- is flagged for the hash-table path.
 #include "common.cuh"
 
 namespace chm {
@@ -43,6 +44,8 @@ constexpr int kBPreThreads = 256;
 constexpr int64_t kBPreCap = 65536;    // compacted keys per query (more: fallback)
 constexpr uint32_t kBNoPivot = 0xFFFFFFFFu;
 constexpr int kBMaxCand = 12288;       // K' bound (sort buffer 16384 keys)
+
+__device__ __forceinline__ bool b_inactive(const uint32_t* active, int q) { return active != nullptr && active[q] == 0u; }
 
 // LUT sum in the reference order (chunk c = 0..31 is nibble c & 1 of code
 // byte c / 2, kernels.cu:361-373).  The nibbles' byte offsets are formed four
@@ -221,9 +224,11 @@ __device__ uint32_t b_scan_excl(uint32_t v, uint32_t* s_warp, uint32_t* total) {
 // `want` (kBNoPivot when the positive docs number at most `want`).
 __global__ void __launch_bounds__(1024) bound_pivot_kernel(const uint32_t* __restrict__ hist, int slices,
                                                            const uint32_t* __restrict__ npos, int want,
-                                                           uint32_t* __restrict__ pivot, uint32_t* __restrict__ ccnt) {
+                                                           uint32_t* __restrict__ pivot, uint32_t* __restrict__ ccnt,
+                                                           const uint32_t* __restrict__ active) {
     __shared__ uint32_t s_warp[33];
     const int q = blockIdx.x;
+    if (b_inactive(active, q)) return;
     if (threadIdx.x == 0) {
         pivot[q] = kBNoPivot;
         ccnt[q] = 0;
@@ -256,8 +261,10 @@ __global__ void __launch_bounds__(1024) bound_pivot_kernel(const uint32_t* __res
 __global__ void __launch_bounds__(kBPreThreads) bound_compact_kernel(const float* __restrict__ S, int64_t M,
                                                                      const uint32_t* __restrict__ pivot,
                                                                      uint64_t* __restrict__ ckeys,
-                                                                     uint32_t* __restrict__ ccnt) {
+                                                                     uint32_t* __restrict__ ccnt,
+                                                                     const uint32_t* __restrict__ active) {
     const int q = blockIdx.y;
+    if (b_inactive(active, q)) return;
     const uint32_t d = pivot[q] == kBNoPivot ? 0u : pivot[q];
     const int64_t per = (M + gridDim.x - 1) / gridDim.x;
     const int64_t i0 = blockIdx.x * per, i1 = min(M, i0 + per);
@@ -318,7 +325,8 @@ __global__ void __launch_bounds__(1024) bound_select_kernel(const uint64_t* __re
                                                             const uint32_t* __restrict__ pivot, int kc,
                                                             int32_t* __restrict__ cand, int32_t* __restrict__ n_cand,
                                                             float* __restrict__ boundary,
-                                                            uint32_t* __restrict__ need_fb) {
+                                                            uint32_t* __restrict__ need_fb,
+                                                            const uint32_t* __restrict__ active) {
     extern __shared__ uint64_t s_keys[];  // [sort_n]
     __shared__ uint32_t s_hist[4096];
     __shared__ uint32_t s_warp[33];
@@ -326,6 +334,7 @@ __global__ void __launch_bounds__(1024) bound_select_kernel(const uint64_t* __re
     __shared__ uint64_t s_prefix, s_pmask;
     __shared__ int s_need, s_done;
     const int q = blockIdx.x;
+    if (b_inactive(active, q)) return;
     const uint32_t cc = ccnt[q];
     if (cc > (uint32_t)kBPreCap) {
         if (threadIdx.x == 0) {
@@ -424,6 +433,7 @@ struct ExactCtx {
     const int32_t* n_cand;   // [nq]
     int kc;
     uint64_t* keys;          // [nq][kc] (P << 32 | ~doc)
+    const uint32_t* active;  // [nq] nonzero: run this query (NULL: all)
 };
 
 __device__ __forceinline__ uint32_t map_hash(uint32_t c) { return (c * 0x9E3779B1u) >> 19; }  // 13 bits
@@ -439,6 +449,7 @@ __global__ void __launch_bounds__(kBxWarps * 32, 1) bound_exact_kernel(ExactCtx 
     float* s_cb1 = reinterpret_cast<float*>(s_m + kBxWarps * 32);                    // [32]
     const int q = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (b_inactive(c.active, q)) return;
     const int n = c.n_cand[q];
     if ((int)blockIdx.x * kBxWarps >= n) return;
     const float4* src = reinterpret_cast<const float4*>(c.lut + (size_t)q * kQ * kLutPerQ);
@@ -506,7 +517,8 @@ __global__ void __launch_bounds__(kBxWarps * 32, 1) bound_exact_kernel(ExactCtx 
 }
 
 // Per query: the candidates by (P desc, doc asc); the refined list when the
-// boundary proves that no doc left out can reach it, else need_fb.
+// boundary proves that no doc left out can reach it, else need_fb (and
+// retry[q] = 1 when a larger candidate set could still prove it).
 __global__ void __launch_bounds__(1024) bound_final_kernel(const uint64_t* __restrict__ keys,
                                                            const int32_t* __restrict__ n_cand, int kc,
                                                            const uint32_t* __restrict__ npos,
@@ -514,18 +526,22 @@ __global__ void __launch_bounds__(1024) bound_final_kernel(const uint64_t* __res
                                                            int k_refine, int32_t* __restrict__ refined_docs,
                                                            float* __restrict__ refined_partial,
                                                            int32_t* __restrict__ num_refined,
-                                                           uint32_t* __restrict__ need_fb) {
+                                                           uint32_t* __restrict__ need_fb,
+                                                           const uint32_t* __restrict__ active,
+                                                           uint32_t* __restrict__ retry) {
     extern __shared__ uint64_t s_keys[];
     __shared__ int s_ok;
     const int q = blockIdx.x;
-    if (need_fb[q]) return;
+    if (b_inactive(active, q)) return;
+    // round 1: a compaction overflow (flagged by the select kernel) stands
+    if (active == nullptr && need_fb[q]) return;
     // fewer positive docs than k_refine: the zero-score fill needs the visited
     // docs (the hash-table path's bitmap)
-    if ((int64_t)npos[q] < k_refine) {
+    const int n = n_cand[q];
+    if ((int64_t)npos[q] < k_refine || n < k_refine) {  // n < k_refine: a round-2 overflow
         if (threadIdx.x == 0) need_fb[q] = 1u;
         return;
     }
-    const int n = n_cand[q];
     int sort_n = 1;
     while (sort_n < n) sort_n <<= 1;
     for (int i = threadIdx.x; i < sort_n; i += blockDim.x) s_keys[i] = i < n ? keys[(size_t)q * kc + i] : 0ull;
@@ -535,8 +551,13 @@ __global__ void __launch_bounds__(1024) bound_final_kernel(const uint64_t* __res
         const float tau = __uint_as_float((uint32_t)(s_keys[k_refine - 1] >> 32));
         const float b = boundary[q];
         s_ok = (b == 0.0f || (double)b * (1.0 + eps) < (double)tau) ? 1 : 0;
-        if (!s_ok) need_fb[q] = 1u;
-        else num_refined[q] = k_refine;
+        if (!s_ok) {
+            need_fb[q] = 1u;
+            if (retry) retry[q] = 1u;
+        } else {
+            need_fb[q] = 0u;  // round 2 starts from a flagged query
+            num_refined[q] = k_refine;
+        }
     }
     __syncthreads();
     if (!s_ok) return;
@@ -563,6 +584,8 @@ int bound_kc(const chm_index* idx, int k_refine) {
     kc = std::min<int64_t>(kc, idx->num_docs);
     return (int)std::max<int64_t>(kc, k_refine);
 }
+// The second round's candidate count.
+int bound_kc2(const chm_index* idx) { return (int)std::min<int64_t>(kBMaxCand, idx->num_docs); }
 
 constexpr int kBPreSlots = 640;
 int bound_slices(int nq) { return std::max(1, std::min(64, kBPreSlots / std::max(1, nq))); }
@@ -578,11 +601,13 @@ struct BoundWork {
     int32_t* n_cand;
     float* boundary;
     uint64_t* keys;
+    uint32_t* retry;
 };
 
 template <typename A>
 void bound_layout(A& a, const chm_index* idx, int nq, int k_refine, BoundWork* w) {
-    const int kc = bound_kc(idx, k_refine);
+    (void)k_refine;
+    const int kc = bound_kc2(idx);  // room for the second round's candidates
     auto S = a.template take<float>((size_t)nq * idx->num_docs);
     auto hist = a.template take<uint32_t>((size_t)std::max(nq, kBPreSlots) * 4096);
     auto npos = a.template take<uint32_t>((size_t)nq);
@@ -593,9 +618,11 @@ void bound_layout(A& a, const chm_index* idx, int nq, int k_refine, BoundWork* w
     auto n_cand = a.template take<int32_t>((size_t)nq);
     auto boundary = a.template take<float>((size_t)nq);
     auto keys = a.template take<uint64_t>((size_t)nq * kc);
+    auto retry = a.template take<uint32_t>((size_t)nq);
     if (w)
         *w = BoundWork{(float*)S, (uint32_t*)hist, (uint32_t*)npos, (uint32_t*)pivot, (uint32_t*)ccnt,
-                       (uint64_t*)ckeys, (int32_t*)cand, (int32_t*)n_cand, (float*)boundary, (uint64_t*)keys};
+                       (uint64_t*)ckeys, (int32_t*)cand, (int32_t*)n_cand, (float*)boundary, (uint64_t*)keys,
+                       (uint32_t*)retry};
 }
 
 struct BoundSizer {
@@ -638,35 +665,49 @@ chm_status bound_run(const chm_index* idx, int nq, const float* lut, const float
     const int slices = bound_slices(nq);
     bound_hist_kernel<<<dim3((unsigned)slices, (unsigned)nq), kBPreThreads, 0, st>>>(w.S, M, w.hist, w.npos);
     CHM_TRY(launch_status("bound_hist_kernel"));
-    bound_pivot_kernel<<<nq, 1024, 0, st>>>(w.hist, slices, w.npos, kc, w.pivot, w.ccnt);
-    CHM_TRY(launch_status("bound_pivot_kernel"));
-    bound_compact_kernel<<<dim3((unsigned)slices, (unsigned)nq), kBPreThreads, 0, st>>>(w.S, M, w.pivot, w.ckeys,
-                                                                                       w.ccnt);
-    CHM_TRY(launch_status("bound_compact_kernel"));
-    int sort_cap = 1;
-    while (sort_cap < kc + 1) sort_cap <<= 1;
-    const size_t sel_smem = sizeof(uint64_t) * sort_cap;
-    CHM_CUDA(cudaFuncSetAttribute(bound_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_smem));
-    bound_select_kernel<<<nq, 1024, sel_smem, st>>>(w.ckeys, w.ccnt, w.pivot, kc, w.cand, w.n_cand, w.boundary,
-                                                    need_fb);
-    CHM_TRY(launch_status("bound_select_kernel"));
-    ExactCtx x{idx->doc_ptrs, idx->codes1_tok, idx->factor1_tok, idx->tok_cluster, idx->n_clusters, lut, cb1,
-               labels, nprobe, w.cand, w.n_cand, kc, w.keys};
-    const size_t ex_smem = (size_t)kQ * kLutPerQ * 4 + (size_t)kMapSlots * 8 + kBxWarps * 32 * 4 + kQ * 4;
-    CHM_CUDA(cudaFuncSetAttribute(bound_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex_smem));
-    // one resident CTA per SM; about two waves over the batch
-    const int gx = (int)std::max<int64_t>(1, std::min<int64_t>((kc + kBxWarps - 1) / kBxWarps,
-                                                               (2 * 148 + nq - 1) / nq));
-    bound_exact_kernel<<<dim3((unsigned)gx, (unsigned)nq), kBxWarps * 32, ex_smem, st>>>(x);
-    CHM_TRY(launch_status("bound_exact_kernel"));
-    int fsort = 1;
-    while (fsort < kc) fsort <<= 1;
-    const size_t fin_smem = sizeof(uint64_t) * fsort;
-    CHM_CUDA(cudaFuncSetAttribute(bound_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fin_smem));
+    CHM_CUDA(cudaMemsetAsync(w.retry, 0, sizeof(uint32_t) * nq, st));
     const double eps = ((double)idx->max_doc_len * kQ + 8.0) * 0x1p-24 * 1.25;
-    bound_final_kernel<<<nq, 1024, fin_smem, st>>>(w.keys, w.n_cand, kc, w.npos, w.boundary, eps, k_refine,
-                                                   refined_docs, refined_partial, num_refined, need_fb);
-    return launch_status("bound_final_kernel");
+    const int kc2 = bound_kc2(idx);
+    // round 1 over every query with K' = kc; round 2 over the queries whose
+    // boundary round 1 could not prove, with K' = kc2
+    for (int round = 0; round < 2; ++round) {
+        const int k = round == 0 ? kc : kc2;
+        const uint32_t* active = round == 0 ? nullptr : w.retry;
+        if (round == 1 && kc2 <= kc) break;
+        bound_pivot_kernel<<<nq, 1024, 0, st>>>(w.hist, slices, w.npos, k, w.pivot, w.ccnt, active);
+        CHM_TRY(launch_status("bound_pivot_kernel"));
+        bound_compact_kernel<<<dim3((unsigned)slices, (unsigned)nq), kBPreThreads, 0, st>>>(w.S, M, w.pivot,
+                                                                                           w.ckeys, w.ccnt, active);
+        CHM_TRY(launch_status("bound_compact_kernel"));
+        int sort_cap = 1;
+        while (sort_cap < k + 1) sort_cap <<= 1;
+        const size_t sel_smem = sizeof(uint64_t) * sort_cap;
+        CHM_CUDA(cudaFuncSetAttribute(bound_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sel_smem));
+        bound_select_kernel<<<nq, 1024, sel_smem, st>>>(w.ckeys, w.ccnt, w.pivot, k, w.cand, w.n_cand, w.boundary,
+                                                        need_fb, active);
+        CHM_TRY(launch_status("bound_select_kernel"));
+        ExactCtx x{idx->doc_ptrs, idx->codes1_tok, idx->factor1_tok, idx->tok_cluster, idx->n_clusters, lut, cb1,
+                   labels, nprobe, w.cand, w.n_cand, k, w.keys, active};
+        const size_t ex_smem = (size_t)kQ * kLutPerQ * 4 + (size_t)kMapSlots * 8 + kBxWarps * 32 * 4 + kQ * 4;
+        CHM_CUDA(cudaFuncSetAttribute(bound_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)ex_smem));
+        // one resident CTA per SM; about two waves over the batch
+        const int gx = (int)std::max<int64_t>(1, std::min<int64_t>((k + kBxWarps - 1) / kBxWarps,
+                                                                   (2 * 148 + nq - 1) / nq));
+        bound_exact_kernel<<<dim3((unsigned)gx, (unsigned)nq), kBxWarps * 32, ex_smem, st>>>(x);
+        CHM_TRY(launch_status("bound_exact_kernel"));
+        int fsort = 1;
+        while (fsort < k) fsort <<= 1;
+        const size_t fin_smem = sizeof(uint64_t) * fsort;
+        CHM_CUDA(cudaFuncSetAttribute(bound_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)fin_smem));
+        bound_final_kernel<<<nq, 1024, fin_smem, st>>>(w.keys, w.n_cand, k, w.npos, w.boundary, eps, k_refine,
+                                                       refined_docs, refined_partial, num_refined, need_fb, active,
+                                                       round == 0 ? w.retry : nullptr);
+        CHM_TRY(launch_status("bound_final_kernel"));
+    }
+    return CHM_OK;
 }
 
 }  // namespace chm

@@ -69,6 +69,9 @@ CONFIGS = {
     "mini": Config("mini", 300, ("normal", 64, 20, 8, 180), 64, 6, 128, 4, 16, 60, 20, 5, 10),
     "small": Config("small", 2000, ("normal", 64, 20, 8, 180), 256, 16, 512, 4, 24, 300, 60,
                     5, 20),
+    # sparse probing (4 of 4,096 lists per query token, as C3 probes 128 of
+    # 262,144): a doc rarely has two tokens in one query token's lists
+    "sparse": Config("sparse", 1500, ("normal", 64, 20, 8, 180), 256, 16, 4096, 4, 4, 100, 30, 5, 20),
     # long documents (several 128-token tiles each), ex_bits 2
     "long": Config("long", 300, ("lognormal", 200, 0.6, 100, 600), 64, 6, 256, 2, 16, 120, 30, 5, 10),
 }

@@ -3,8 +3,8 @@ path and the oracle: the refined lists (docs, order, partial-score bits) are
 identical whichever path produces them, and on realistic corpora the
 dense-bound path, not the fallback, produces most of them.  A boundary that
 cannot be proven (forced here by an inflated max_doc_len, which widens the
-rounding slack) sends every query to the hash-table path with the same
-result."""
+rounding slack) gets a second, larger candidate round.  Queries with fewer
+positive docs than k_refine go to the hash-table path (the zero-score fill)."""
 import ctypes as C
 
 import numpy as np
@@ -56,7 +56,7 @@ def _same(a, b):
         np.testing.assert_array_equal(rp_a[q, :nr_a[q]], rp_b[q, :nr_b[q]], err_msg=f"query {q}")
 
 
-@pytest.mark.parametrize("name", ["mini", "small", "long"])
+@pytest.mark.parametrize("name", ["mini", "small", "long", "sparse"])
 def test_dense_bound_equals_table_path_and_oracle(name):
     c = _corpus.corpus(name)
     d = _corpus.device_index(c, torch)
@@ -72,24 +72,32 @@ def test_dense_bound_equals_table_path_and_oracle(name):
         np.testing.assert_array_equal(rp[q, :nr[q]], o["refined_partial"].view(np.uint32))
 
 
-def test_dense_bound_produces_most_lists():
-    """On the small corpus (2,000 docs, k_refine 300) the boundary is proven
-    for most queries, so the dense-bound path really produces their lists."""
-    c = _corpus.corpus("small")
+@pytest.mark.parametrize("name", ["sparse", "small"])
+def test_dense_bound_produces_most_lists(name):
+    """The dense-bound path, not the fallback, produces most refined lists:
+    with sparse probing in its first round (K' = 1.5 k_refine); on the small
+    corpus, where every doc has several tokens in each query token's lists
+    and the sum of visits overestimates, in its second round (K' = every
+    doc)."""
+    c = _corpus.corpus(name)
     d = _corpus.device_index(c, torch)
-    tq = _stage1(c, d)[3]
-    assert (tq == 0).sum() >= len(tq) // 2, tq
+    got = _stage1(c, d)
+    assert (got[3] == 0).sum() >= len(got[3]) // 2, got[3]
+    _same(got, _stage1(c, d.with_dense_stage1(False)))
 
 
-def test_unprovable_boundary_falls_back():
-    """k_refine 20 keeps 84 candidates, far fewer than any query's positive
-    docs, so every query has a boundary to prove; a slack of 40x proves none."""
+def test_unproven_first_round_goes_to_second_round():
+    """k_refine 20 keeps 84 first-round candidates, far fewer than any query's
+    positive docs, and a rounding slack of 40x proves no boundary; the second
+    round takes every doc of this corpus (2,000 <= 12,288) as a candidate,
+    which needs no boundary, so the dense-bound path still produces every
+    list -- identical to the hash-table path's."""
     c = _corpus.corpus("small")
     d = _corpus.device_index(c, torch)
     wide = d.with_dense_stage1(True)
     wide.view.max_doc_len = 1 << 24
     got = _stage1(c, wide, k_refine=20)
-    assert got[3].all()
+    assert not got[3].any()
     _same(got, _stage1(c, d.with_dense_stage1(False), k_refine=20))
 
 
