@@ -211,11 +211,12 @@ def main():
         search_full = searcher.search
         parallelism = "single GPU"
     else:
-        backend = SH.CudaShardBackend(index, bases, rank, batch=B, **params)
-        pipe = SH.ShardedPipeline(backend, SH.TorchComm(), params)
+        # the sharded protocol in native code: stage kernels and NCCL
+        # collectives on one stream, one host call per batch
+        pipe = SH.NativeShardSearcher(index, bases, rank, world, batch=B, **params)
         search_device = lambda qb, i: pipe.search_device(qb)
         search_full = pipe.search
-        parallelism = f"document shards x{world} (NCCL all_gather/all_reduce)"
+        parallelism = f"document shards x{world} (chm_search_sharded: NCCL all_gather/all_reduce on the stream)"
 
     # every rank serves the same query stream (strong scaling: the corpus and
     # the queries are fixed, the documents are split across the ranks)
@@ -298,6 +299,18 @@ def main():
         if rank == 0:
             recall = round(W.recall_at_k(np.stack(gt), r_all, cfg.k), 4)
 
+    # ---- per-step device times of one sharded batch (exchange included) -----
+    shard_steps = None
+    if world > 1:
+        barrier()
+        pipe.search_device(batches[args.warmup], timed=True)
+        torch.cuda.synchronize()
+        loc = pipe.step_ms()
+        shard_steps = {k: round(max_over_ranks(v), 3) for k, v in loc.items()}
+        tot = sum(shard_steps.values())
+        xch = sum(v for k, v in shard_steps.items() if k.startswith(("gather", "reduce")))
+        shard_steps["exchange_share"] = round(xch / tot, 4) if tot > 0 else None
+
     # ---- per-stage profile on this rank's (shard) index, exchange excluded --
     prof_searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
     stages, stages_extra = profile_stages(torch, capi, index, prof_searcher, batches[args.warmup], cfg)
@@ -314,9 +327,9 @@ def main():
     if world == 1:
         launches = sum(s["launches"] for s in stages) + 1  # + chm_search's status fold
     else:
-        # prepare, probe, stage1 (7), merge, 2 x localize, refine, select, full-bit (8), final
-        refine_launches = next(s["launches"] for s in stages if s["name"] == "refine_1bit")
-        launches = 1 + probe_launches + 7 + 1 + 2 + refine_launches + 1 + 8 + 1
+        # chm_search's kernels plus the sharded path's merge, two localizes and
+        # label memset-free fold (the collectives are NCCL's own kernels)
+        launches = sum(s["launches"] for s in stages) + 1 + 3
     line = {
         "metric": "QPS at Recall@100 (C3 passage corpus)",
         "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -340,6 +353,7 @@ def main():
                      "peak_kind": kind},
         "stages_ms_per_step": {s["name"]: round(s["ms"], 3) for s in stages},
         "stage1_table_path_queries": next(s.get("table_path_queries") for s in stages if s["name"] == "stage1"),
+        "sharded_steps_ms_max_over_ranks": shard_steps,
         "stages_algo_gbs": {s["name"]: round(s["algo_bytes"] / (s["ms"] / 1e3) / 1e9, 1)
                             for s in stages if s["algo_bytes"]},
         "gpu_launches": int(launches * args.steps),
@@ -353,6 +367,7 @@ def main():
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
+        pipe.close()
         dist.destroy_process_group()
 
 
@@ -543,7 +558,8 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         ("prepare", 1, lambda: L.chm_prepare_queries(P(index.flips), index.dim, index.ex_bits, P(q), ntok, P(rot),
                                                     P(cb1), P(cbex), P(lut), st)),
         ("probe", 6 if use_tc else 2, probe),
-        ("stage1", 7, lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe, p.k_refine, P(rd), P(rp),
+        ("stage1", stage1_launches(index, p), lambda: L.chm_stage1(v, B, P(lut), P(cb1), P(labels), p.nprobe,
+                                                                   p.k_refine, P(rd), P(rp),
                                            P(nr), None, P(sws), sb, st)),
         # chm_search's choice: the tensor-core filter on batches of 16 or more
         ("refine_1bit", 7, lambda: L.chm_refine_1bit_tc(v, B, P(lut), P(cb1), P(rot), P(rd), P(nr), p.k_refine, P(ob),
@@ -611,6 +627,20 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
     # the batch's full-bit selection and scores, for the CPU baseline's check
     extra = dict(rot=rot.view(B, 32, 128), cbex=cbex.view(B, 32), fb_docs=fd, num_fb=nf, fb_scores=fs)
     return out, extra
+
+
+def stage1_launches(index, p):
+    """Kernels one chm_stage1 call launches: the hash-table path's 8 (clear or
+    memset, score, combine, mark, hist, pivot, compact, select; masked to the
+    queries it redoes), and with the dense-bound path enabled its score and
+    histogram plus pivot, compact, select, exact and final per round (a
+    second round when 12,288 candidates exceed the first round's)."""
+    v = index.view
+    if not (v.tok_cluster and v.codes1_tok and v.max_doc_len > 0 and p.nprobe <= 128):
+        return 7  # the hash-table path alone (its tables cleared by a memset)
+    kc = min(max(p.k_refine + max(p.k_refine // 2, 64), p.k_refine), 12288, index.num_docs)
+    rounds = 2 if min(12288, index.num_docs) > kc else 1
+    return 8 + 2 + 5 * rounds
 
 
 def latency_percentiles(torch, queries, search_device, barrier, n=64):

@@ -2,6 +2,8 @@
 
 * ``lib/libchimera_b200.so`` -- the CUDA kernels and the C ABI
   (include/chimera_b200.h), compiled for sm_100a only.
+* ``lib/libchimera_nccl.so`` -- the document-sharded search over NCCL
+  (include/chimera_b200_sharded.h).
 * ``lib/libchimera_core.so`` -- the drop-in C++ ``Chimera::chimera_index``
   (include/chimera/chimera_index.cuh) over the C ABI.
 * ``chimera*.so`` (this directory) -- the pybind11 module ``chimera``.
@@ -83,6 +85,16 @@ def build_cuda(verbose=False):
     so = os.path.join(LIB, "libchimera_b200.so")
     if _stale(so, objs):
         _run([NVCC] + ARCH + ["-shared", "-o", so] + objs + ["-lcudart"])  # driver API via entry points
+    # the document-sharded search over NCCL: its own library, so that the core
+    # one has no NCCL dependency
+    src = os.path.join(CSRC, "sharded.cu")
+    obj = os.path.join(OBJ, "sharded.cu.o")
+    if _stale(obj, [src] + hdrs):
+        _run([NVCC] + NVCC_FLAGS + ["-c", src, "-o", obj])
+    nso = os.path.join(LIB, "libchimera_nccl.so")
+    if _stale(nso, [obj, so]):
+        _run([NVCC] + ARCH + ["-shared", "-o", nso, obj, "-L" + LIB, "-lchimera_b200", "-lnccl", "-lcudart",
+                              "-Xlinker", "-rpath,$ORIGIN"])
     return so
 
 

@@ -117,6 +117,40 @@ def lib():
     return _lib_handle
 
 
+NCCL_PATH = os.path.join(HERE, "lib", "libchimera_nccl.so")
+_nccl_handle = None
+SH_STEPS = ("prepare", "probe", "gather_labels", "stage1", "gather_lists", "merge", "refine_1bit",
+            "reduce_onebit", "select_fullbit", "fullbit", "reduce_fullbit", "final_topk")
+
+
+class ShardInfo(C.Structure):
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("doc_base", C.c_void_p)]
+
+
+def nccl_lib():
+    """The document-sharded search over NCCL (include/chimera_b200_sharded.h)."""
+    global _nccl_handle
+    if _nccl_handle is None:
+        lib()
+        if not os.path.exists(NCCL_PATH):
+            raise RuntimeError(f"chimera_b200 NCCL library missing: {NCCL_PATH} (run `python -m chimera_b200.build`)")
+        L = C.CDLL(NCCL_PATH)
+        L.chm_comm_unique_id.argtypes = [V]
+        L.chm_comm_unique_id.restype = C.c_int
+        L.chm_comm_init.argtypes = [V, I32, I32, I32, C.POINTER(V)]
+        L.chm_comm_init.restype = C.c_int
+        L.chm_comm_init_all.argtypes = [I32, V, V]
+        L.chm_comm_init_all.restype = C.c_int
+        L.chm_comm_destroy.argtypes = [V]
+        L.chm_comm_destroy.restype = C.c_int
+        L.chm_search_sharded_workspace_bytes.argtypes = [V, V, I32]
+        L.chm_search_sharded_workspace_bytes.restype = SZ
+        L.chm_search_sharded.argtypes = [V, V, V, V, V, I64, V, V, V, SZ, V, V]
+        L.chm_search_sharded.restype = C.c_int
+        _nccl_handle = L
+    return _nccl_handle
+
+
 def host_rng():
     global _rng_handle
     if _rng_handle is None:

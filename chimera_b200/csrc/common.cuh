@@ -15,6 +15,7 @@ constexpr int kLutPerQ = 512;  // 32 chunks x 16 entries (config.cuh:16-20)
 
 // Thread-local record of the last CUDA error, surfaced by chm_last_error().
 void set_last_error(const char* where, cudaError_t err);
+void set_last_message(const char* msg);
 
 inline chm_status launch_status(const char* where) {
     cudaError_t e = cudaGetLastError();

@@ -148,6 +148,94 @@ class ShardedPipeline:
         return res, nres
 
 
+class NativeShardSearcher:
+    """The sharded search in native code (chm_search_sharded, lib/
+    libchimera_nccl.so): the same protocol as ShardedPipeline with the NCCL
+    collectives enqueued on the search stream between the stage kernels, one
+    call per batch from the host.  Every rank creates one with the same
+    parameters; the NCCL unique id travels over `group` (torch.distributed)."""
+
+    def __init__(self, index, doc_bases, rank, world, *, nprobe, k_refine, k_full_bit, num_chunks, k, batch,
+                 group=None):
+        import torch
+        import torch.distributed as dist
+        self.torch = torch
+        self.ix = index
+        self.L = capi.nccl_lib()
+        self.rank, self.world = rank, world
+        self.params = capi.SearchParams(nprobe, k_refine, k_full_bit, num_chunks, k, batch, 0)
+        self._bases = (C.c_int64 * (world + 1))(*[int(b) for b in doc_bases])
+        self.shard = capi.ShardInfo(rank, world, C.cast(self._bases, C.c_void_p))
+        uid = (C.c_uint8 * 128)()
+        if rank == 0:
+            capi.check(self.L.chm_comm_unique_id(C.cast(uid, C.c_void_p)), "chm_comm_unique_id")
+        if world > 1:
+            dev = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+            t = torch.tensor(list(uid), dtype=torch.uint8, device=dev)
+            dist.broadcast(t, src=0, group=group)
+            uid = (C.c_uint8 * 128)(*t.cpu().tolist())
+        self.comm = C.c_void_p()
+        capi.check(self.L.chm_comm_init(C.cast(uid, C.c_void_p), world, rank, torch.cuda.current_device(),
+                                         C.byref(self.comm)),
+                   "chm_comm_init")
+        self._ws = None
+        self._alloc()
+        self.timing = (C.c_float * len(capi.SH_STEPS))()
+
+    def _alloc(self):
+        nb = self.L.chm_search_sharded_workspace_bytes(C.byref(self.ix.view), C.byref(self.params), self.world)
+        if nb == 0:
+            raise ValueError("invalid search parameters")
+        self._ws = self.torch.empty(nb, dtype=self.torch.uint8, device=self.ix.factor1.device)
+        self.ws_bytes = nb
+
+    def search_device(self, queries, results=None, num_results=None, timed=False):
+        torch = self.torch
+        q = queries.contiguous()
+        nq = int(q.shape[0])
+        k = self.params.k
+        if results is None:
+            results = torch.empty(nq, k, dtype=torch.int64, device=q.device)
+        if num_results is None:
+            num_results = torch.empty(nq, dtype=torch.int32, device=q.device)
+        capi.check(self.L.chm_search_sharded(C.byref(self.ix.view), C.byref(self.params), C.byref(self.shard),
+                                             self.comm, capi._ptr(q), nq, capi._ptr(results),
+                                             capi._ptr(num_results), capi._ptr(self._ws), self.ws_bytes,
+                                             capi._stream(torch),
+                                             C.cast(self.timing, C.c_void_p) if timed else None),
+                   "search_sharded")
+        return results, num_results
+
+    def step_ms(self):
+        """Per-step device milliseconds of the last batch of a timed call."""
+        return {n: float(self.timing[i]) for i, n in enumerate(capi.SH_STEPS)}
+
+    def search(self, queries):
+        """search_device with the overflow retry (every rank sees the same
+        counts: the flags were all-reduced)."""
+        res, nres = self.search_device(queries)
+        extra = 0
+        bad = (nres < 0).nonzero().flatten()
+        while bad.numel() > 0 and extra < 6:
+            extra += 1
+            saved = self.params.table_log2_extra
+            self.params.table_log2_extra = extra
+            self._alloc()
+            r2, n2 = self.search_device(queries[bad])
+            res[bad], nres[bad] = r2, n2
+            self.params.table_log2_extra = saved
+            self._alloc()
+            bad = (nres < 0).nonzero().flatten()
+        if bad.numel() > 0:
+            raise capi.ChmError(capi.CHM_ERR_CAPACITY, "search_sharded")
+        return res, nres
+
+    def close(self):
+        if self.comm:
+            capi.nccl_lib().chm_comm_destroy(self.comm)
+            self.comm = C.c_void_p()
+
+
 class CudaShardBackend:
     """The stage kernels of one rank (C ABI, current CUDA stream)."""
 

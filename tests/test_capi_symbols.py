@@ -29,3 +29,13 @@ def test_binding_table_covers_header():
 
 def test_version_string():
     assert capi.lib().chm_version().startswith(b"chimera_b200")
+
+
+def test_sharded_library_exports_its_header():
+    """lib/libchimera_nccl.so (the document-sharded search over NCCL) loads
+    and exports every function include/chimera_b200_sharded.h declares."""
+    lib = capi.nccl_lib()
+    names = declared("chimera_b200_sharded.h")
+    assert "chm_search_sharded" in names and len(names) >= 6
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing

@@ -4,7 +4,9 @@ index.
 
 * one GPU: G shards as host threads sharing the device, exchanging tensors
   through a host barrier (no kernel waits on another kernel);
-* two GPUs (skipped with fewer): one process per GPU over NCCL.
+* two GPUs (skipped with fewer): one process per GPU over NCCL, through the
+  Python protocol and through chm_search_sharded (native);
+* one GPU, native: chm_search_sharded as a world of one.
 """
 import os
 import socket
@@ -138,10 +140,41 @@ def _nccl_worker(rank, world, port, out_dir):
         res, nres = SH.ShardedPipeline(be, SH.TorchComm(), params).search(q)
         torch.cuda.synchronize()
         ok = torch.equal(res, want) and torch.equal(nres, wn)
+        # the same protocol in native code (chm_search_sharded)
+        ns = SH.NativeShardSearcher(shard, bases, rank, world, batch=q.shape[0], **params)
+        res2, nres2 = ns.search(q)
+        torch.cuda.synchronize()
+        ns.close()
+        ok = ok and torch.equal(res2, want) and torch.equal(nres2, wn)
         with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
             f.write("ok" if ok else "mismatch")
     finally:
         dist.destroy_process_group()
+
+
+def test_native_sharded_single_rank_matches_chm_search():
+    """chm_search_sharded (the protocol in native code, NCCL collectives on
+    the search stream) as a world of one: the same results as chm_search, in
+    batches of 5 and 16 (both refinement paths), and per-step timings."""
+    from chimera_b200 import capi
+    from chimera_b200 import sharded as SH
+    from tests._corpus import corpus, device_index
+    c = corpus("small")
+    cfg = c["cfg"]
+    d = device_index(c, torch)
+    q = torch.from_numpy(np.ascontiguousarray(c["queries"], np.float32)).cuda()
+    want, wn = capi.Searcher(d, k=cfg.k, batch=q.shape[0], **cfg.search_kwargs()).search(q)
+    for batch in (5, 16):
+        s = SH.NativeShardSearcher(d, [0, cfg.num_docs], 0, 1, batch=batch, k=cfg.k, **cfg.search_kwargs())
+        try:
+            res, nres = s.search(q)
+            torch.cuda.synchronize()
+            assert torch.equal(nres, wn) and torch.equal(res, want), batch
+            s.search_device(q, timed=True)
+            ms = s.step_ms()
+            assert set(ms) == set(capi.SH_STEPS) and all(v >= 0 for v in ms.values())
+        finally:
+            s.close()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
