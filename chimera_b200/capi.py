@@ -98,6 +98,8 @@ EXPORTS = {
     "chm_token_order_1bit": ([V, V, V, I64, V, V, V], C.c_int),
     "chm_token_clusters": ([V, I64, V, I64, V, V], C.c_int),
     "chm_stage1_table_queries": ([V, I32, I32, I32, I32, V, SZ, V, V], C.c_int),
+    "chm_build_cluster_order_workspace_bytes": ([I64, I64], SZ),
+    "chm_build_cluster_order": ([V, I64, I64, V, I64, V, V, V, V, V, V, V, V, V, V, SZ, V], C.c_int),
 }
 
 
@@ -373,12 +375,6 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
                                 _ptr(rot_c), _ptr(cb1_c), _ptr(cbex_c), None, st), "rotate centroids")
     cnorm = torch.empty(n_clusters, dtype=torch.float32, device=dev)
     check(L.chm_row_norms(_ptr(rot_c), n_clusters, _ptr(cnorm), st), "row_norms")
-    # IVF_PG::build_from_assignments: stable counting sort (ivf_pg.cpp:110-126)
-    a64 = assign.to(torch.int64)
-    inv = torch.sort(a64, stable=True).indices
-    counts = torch.bincount(a64, minlength=n_clusters)
-    cluster_pos = torch.zeros(n_clusters + 1, dtype=torch.int64, device=dev)
-    cluster_pos[1:] = torch.cumsum(counts, 0)
     # rotation + RaBitQ encoding
     fb = DIM * (1 + ex_bits) // 8
     codes1 = torch.empty(n, 16, dtype=torch.uint8, device=dev)
@@ -388,17 +384,30 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
     check(L.chm_build_encode(_ptr(flips), _ptr(emb.contiguous()), n, dim, ex_bits, _ptr(codes1), _ptr(f1),
                              _ptr(full), _ptr(ff), None, st), "build_encode")
     phase("encode")
-    dl = torch.from_numpy(doclens).to(dev)
-    doc_ptrs = torch.zeros(len(doclens) + 1, dtype=torch.int64, device=dev)
-    doc_ptrs[1:] = torch.cumsum(dl, 0)
-    owner = torch.repeat_interleave(torch.arange(len(doclens), device=dev, dtype=torch.int32), dl)
+    doc_ptrs = torch.from_numpy(np.concatenate([[0], np.cumsum(doclens)]).astype(np.int64)).to(dev)
+    # IVF_PG::build_from_assignments + reorder_by_cluster (ivf_pg.cpp:110-126,
+    # build_index.cu:328-363) on the GPU
+    cluster_pos = torch.empty(n_clusters + 1, dtype=torch.int64, device=dev)
+    inv = torch.empty(n, dtype=torch.int32, device=dev)
+    codes1_cl = torch.empty(n, 16, dtype=torch.uint8, device=dev)
+    f1_cl = torch.empty(n, dtype=torch.float32, device=dev)
+    doc_ids = torch.empty(n, dtype=torch.int32, device=dev)
     tok2pos = torch.empty(n, dtype=torch.int32, device=dev)
-    tok2pos[inv] = torch.arange(n, dtype=torch.int32, device=dev)
-    return DeviceIndex(dim=dim, ex_bits=ex_bits, cluster_pos=cluster_pos,
-                       codes1=codes1[inv].contiguous(), factor1=f1[inv].contiguous(),
-                       doc_ids=owner[inv].contiguous(), tok2pos=tok2pos, doc_ptrs=doc_ptrs,
-                       full_codes=full, full_factors=ff, centroids=rot_c, centroid_norms=cnorm,
-                       flips=flips, codes1_tok=codes1, factor1_tok=f1, tok_cluster=assign), \
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    wsb = L.chm_build_cluster_order_workspace_bytes(n, n_clusters)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+    check(L.chm_build_cluster_order(_ptr(assign), n, n_clusters, _ptr(doc_ptrs), len(doclens), _ptr(codes1),
+                                    _ptr(f1), _ptr(cluster_pos), _ptr(inv), _ptr(codes1_cl), _ptr(f1_cl),
+                                    _ptr(doc_ids), _ptr(tok2pos), _ptr(status), _ptr(ws), wsb, st), "cluster order")
+    del ws
+    bad = int(status.item())
+    if bad:
+        raise ChmError(CHM_ERR_CAPACITY if bad & 2 else CHM_ERR_INVALID, "cluster order")
+    phase("cluster order")
+    return DeviceIndex(dim=dim, ex_bits=ex_bits, cluster_pos=cluster_pos, codes1=codes1_cl, factor1=f1_cl,
+                       doc_ids=doc_ids, tok2pos=tok2pos, doc_ptrs=doc_ptrs, full_codes=full, full_factors=ff,
+                       centroids=rot_c, centroid_norms=cnorm, flips=flips, codes1_tok=codes1, factor1_tok=f1,
+                       tok_cluster=assign), \
         dict(assign=assign, inv=inv, token_codes1=codes1, token_f1=f1)
 
 

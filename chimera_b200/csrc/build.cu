@@ -232,3 +232,304 @@ extern "C" chm_status chm_token_clusters(const int64_t* cluster_pos, int64_t n_c
         cluster_pos, n_clusters, tok2pos, n, tok_cluster);
     return chm::launch_status("token_clusters_kernel");
 }
+
+// ---- IVF lists and the cluster-ordered 1-bit arrays ----------------------
+// IVF_PG::build_from_assignments (ivf_pg.cpp:110-126): a stable counting sort
+// of the tokens by cluster, and reorder_by_cluster (build_index.cu:328-363):
+// the 1-bit codes, factors and owning docs in that order plus each token's
+// position.  On the GPU: per-cluster counts -> an exclusive scan -> a scatter
+// by atomic slot -> a sort of each list's token ids (restores the stable,
+// ascending order) -> a gather.
+namespace chm {
+
+constexpr int kScanPer = 4;                       // elements per thread
+constexpr int kScanBlock = 1024 * kScanPer;       // elements per scan block
+constexpr int kListSmall = 4096;                  // lists sorted by a 256-thread CTA
+constexpr int kListBig = 32768;                   // lists sorted by a 1024-thread CTA (128 KB; a power of
+                                                  // two: the bitonic sort pads to one)
+
+__global__ void cluster_count_kernel(const uint32_t* __restrict__ assign, int64_t n, int64_t nc,
+                                     uint32_t* __restrict__ counts, uint32_t* __restrict__ bad) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t c = assign[t];
+        if ((int64_t)c < nc) atomicAdd(counts + c, 1u);
+        else atomicOr(bad, 1u);
+    }
+}
+
+// Exclusive scan of a 1024-thread block's values, one per thread.
+__device__ uint64_t scan_block_excl(uint64_t v, uint64_t* s_warp, uint64_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint64_t x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint64_t y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const uint64_t w = s_warp[lane];
+        uint64_t z = w;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, z, off);
+            if (lane >= off) z += y;
+        }
+        s_warp[lane] = z - w;
+        if (lane == 31) s_warp[32] = z;
+    }
+    __syncthreads();
+    const uint64_t r = s_warp[warp] + x - v;
+    *total = s_warp[32];
+    __syncthreads();
+    return r;
+}
+
+// Pass 1: each block's exclusive prefix of its kScanBlock counts, and the block's sum.
+__global__ void __launch_bounds__(1024) scan_blocks_kernel(const uint32_t* __restrict__ counts, int64_t nc,
+                                                           int64_t* __restrict__ pos, uint64_t* __restrict__ sums) {
+    __shared__ uint64_t s_warp[33];
+    const int64_t base = (int64_t)blockIdx.x * kScanBlock + (int64_t)threadIdx.x * kScanPer;
+    uint64_t v[kScanPer], run = 0;
+#pragma unroll
+    for (int j = 0; j < kScanPer; ++j) {
+        v[j] = base + j < nc ? counts[base + j] : 0;
+        run += v[j];
+    }
+    uint64_t total;
+    uint64_t off = scan_block_excl(run, s_warp, &total);
+#pragma unroll
+    for (int j = 0; j < kScanPer; ++j) {
+        if (base + j < nc) pos[base + j] = (int64_t)off;
+        off += v[j];
+    }
+    if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+// Pass 2 (one block): the blocks' exclusive offsets (at most kScanBlock blocks).
+__global__ void __launch_bounds__(1024) scan_sums_kernel(uint64_t* __restrict__ sums, int nblocks,
+                                                         int64_t* __restrict__ pos_end) {
+    __shared__ uint64_t s_warp[33];
+    const int base = threadIdx.x * kScanPer;
+    uint64_t v[kScanPer], run = 0;
+#pragma unroll
+    for (int j = 0; j < kScanPer; ++j) {
+        v[j] = base + j < nblocks ? sums[base + j] : 0;
+        run += v[j];
+    }
+    uint64_t total;
+    uint64_t off = scan_block_excl(run, s_warp, &total);
+#pragma unroll
+    for (int j = 0; j < kScanPer; ++j) {
+        if (base + j < nblocks) sums[base + j] = off;
+        off += v[j];
+    }
+    if (threadIdx.x == 0) *pos_end = (int64_t)total;
+}
+
+// Pass 3: add each block's offset.
+__global__ void __launch_bounds__(1024) scan_add_kernel(int64_t* __restrict__ pos, int64_t nc,
+                                                        const uint64_t* __restrict__ sums) {
+    const int64_t base = (int64_t)blockIdx.x * kScanBlock + (int64_t)threadIdx.x * kScanPer;
+    const int64_t add = (int64_t)sums[blockIdx.x];
+#pragma unroll
+    for (int j = 0; j < kScanPer; ++j)
+        if (base + j < nc) pos[base + j] += add;
+}
+
+__global__ void cluster_scatter_kernel(const uint32_t* __restrict__ assign, int64_t n, int64_t nc,
+                                       const int64_t* __restrict__ cluster_pos, uint32_t* __restrict__ fill,
+                                       uint32_t* __restrict__ inv) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t c = assign[t];
+        if ((int64_t)c >= nc) continue;  // counted as bad; its token gets no position
+        const uint32_t slot = atomicAdd(fill + c, 1u);
+        inv[cluster_pos[c] + slot] = (uint32_t)t;
+    }
+}
+
+// Ascending bitonic sort of n (power of two) keys in shared memory.
+__device__ void sort_asc_u32(uint32_t* a, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint32_t x = a[i], y = a[l];
+                    const bool asc = (i & k) == 0;
+                    if (asc ? (x > y) : (x < y)) {
+                        a[i] = y;
+                        a[l] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Sorts list c's token ids in place (cap: shared-memory keys).
+__device__ void sort_list(uint32_t* __restrict__ inv, int64_t start, int len, uint32_t* s) {
+    int n = 1;
+    while (n < len) n <<= 1;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = i < len ? inv[start + i] : 0xFFFFFFFFu;
+    __syncthreads();
+    sort_asc_u32(s, n);
+    for (int i = threadIdx.x; i < len; i += blockDim.x) inv[start + i] = s[i];
+    __syncthreads();
+}
+
+// CTAs stride over the clusters; lists longer than kListSmall are queued for
+// the big-list kernel.
+__global__ void __launch_bounds__(256) cluster_sort_small_kernel(uint32_t* __restrict__ inv,
+                                                                 const int64_t* __restrict__ cluster_pos, int64_t nc,
+                                                                 uint32_t* __restrict__ big,
+                                                                 uint32_t* __restrict__ n_big) {
+    __shared__ uint32_t s[kListSmall];
+    for (int64_t c = blockIdx.x; c < nc; c += gridDim.x) {
+        const int64_t start = cluster_pos[c];
+        const int64_t len = cluster_pos[c + 1] - start;
+        if (len <= 1) continue;
+        if (len > kListSmall) {
+            if (threadIdx.x == 0) big[atomicAdd(n_big, 1u)] = (uint32_t)c;
+            continue;
+        }
+        sort_list(inv, start, (int)len, s);
+    }
+}
+
+__global__ void __launch_bounds__(1024) cluster_sort_big_kernel(uint32_t* __restrict__ inv,
+                                                                const int64_t* __restrict__ cluster_pos,
+                                                                const uint32_t* __restrict__ big,
+                                                                const uint32_t* __restrict__ n_big,
+                                                                uint32_t* __restrict__ bad) {
+    extern __shared__ uint32_t s_big[];
+    const uint32_t nb = *n_big;
+    for (uint32_t i = blockIdx.x; i < nb; i += gridDim.x) {
+        const uint32_t c = big[i];
+        const int64_t start = cluster_pos[c];
+        const int64_t len = cluster_pos[c + 1] - start;
+        if (len > kListBig) {
+            if (threadIdx.x == 0) atomicOr(bad, 2u);
+            continue;
+        }
+        sort_list(inv, start, (int)len, s_big);
+    }
+}
+
+// Each document's id over its tokens.
+__global__ void token_docs_kernel(const int64_t* __restrict__ doc_ptrs, int64_t num_docs, int32_t* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t d = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; d < num_docs;
+         d += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        for (int64_t t = doc_ptrs[d] + lane; t < doc_ptrs[d + 1]; t += 32) out[t] = (int32_t)d;
+    }
+}
+
+// position -> token: the token's position, and the cluster-ordered code,
+// factor and owning doc.  Only the positions the lists hold (*pos_end, n
+// unless an assignment was out of range) are read.
+__global__ void cluster_gather_kernel(const uint32_t* __restrict__ inv, int64_t n, const int64_t* __restrict__ pos_end,
+                                      const uint4* __restrict__ codes_tok, const float* __restrict__ f_tok,
+                                      const int32_t* __restrict__ tok_doc, uint4* __restrict__ codes1,
+                                      float* __restrict__ factor1, int32_t* __restrict__ doc_ids,
+                                      uint32_t* __restrict__ tok2pos) {
+    const int64_t m = min(n, *pos_end);
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < m; p += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t t = inv[p];
+        if ((int64_t)t >= n) continue;
+        tok2pos[t] = (uint32_t)p;
+        codes1[p] = codes_tok[t];
+        factor1[p] = f_tok[t];
+        doc_ids[p] = tok_doc[t];
+    }
+}
+
+struct OrderWork {
+    uint32_t* counts;  // [nc]
+    uint32_t* fill;    // [nc]
+    uint64_t* sums;    // [kScanBlock]
+    uint32_t* big;     // [nc]
+    uint32_t* n_big;
+    uint32_t* bad;
+    int32_t* tok_doc;  // [n]
+};
+
+template <typename A>
+void order_layout(A& a, int64_t n, int64_t nc, OrderWork* w) {
+    auto counts = a.template take<uint32_t>((size_t)nc);
+    auto fill = a.template take<uint32_t>((size_t)nc);
+    auto sums = a.template take<uint64_t>((size_t)kScanBlock);
+    auto big = a.template take<uint32_t>((size_t)nc);
+    auto n_big = a.template take<uint32_t>(2);
+    auto tok_doc = a.template take<int32_t>((size_t)n);
+    if (w)
+        *w = OrderWork{(uint32_t*)counts, (uint32_t*)fill, (uint64_t*)sums, (uint32_t*)big, (uint32_t*)n_big,
+                       (uint32_t*)n_big + 1, (int32_t*)tok_doc};
+}
+
+struct OrderSizer {
+    Sizer s;
+    template <typename T>
+    void* take(size_t n) {
+        s.take<T>(n);
+        return nullptr;
+    }
+};
+
+}  // namespace chm
+
+extern "C" size_t chm_build_cluster_order_workspace_bytes(int64_t n, int64_t n_clusters) {
+    if (n <= 0 || n_clusters <= 0) return 0;
+    chm::OrderSizer s;
+    chm::order_layout(s, n, n_clusters, nullptr);
+    return s.s.off;
+}
+
+extern "C" chm_status chm_build_cluster_order(const uint32_t* assign, int64_t n, int64_t n_clusters,
+                                              const int64_t* doc_ptrs, int64_t num_docs, const uint8_t* codes_tok,
+                                              const float* factor_tok, int64_t* cluster_pos, uint32_t* inv,
+                                              uint8_t* codes1, float* factor1, int32_t* doc_ids, uint32_t* tok2pos,
+                                              uint32_t* status, void* ws, size_t ws_bytes, void* stream) {
+    if (n <= 0 || n > 0xFFFFFFFFll || n_clusters <= 0 || num_docs <= 0 ||
+        n_clusters > (int64_t)chm::kScanBlock * chm::kScanBlock)
+        return CHM_ERR_INVALID;
+    cudaStream_t st = (cudaStream_t)stream;
+    chm::Arena a(ws, ws_bytes);
+    chm::OrderWork w;
+    chm::order_layout(a, n, n_clusters, &w);
+    if (a.overflow) return CHM_ERR_CAPACITY;
+    CHM_CUDA(cudaMemsetAsync(w.counts, 0, sizeof(uint32_t) * n_clusters, st));
+    CHM_CUDA(cudaMemsetAsync(w.fill, 0, sizeof(uint32_t) * n_clusters, st));
+    CHM_CUDA(cudaMemsetAsync(w.n_big, 0, sizeof(uint32_t) * 2, st));
+    const int grid = 148 * 16;
+    chm::cluster_count_kernel<<<grid, 256, 0, st>>>(assign, n, n_clusters, w.counts, w.bad);
+    CHM_TRY(chm::launch_status("cluster_count_kernel"));
+    const int nblocks = (int)((n_clusters + chm::kScanBlock - 1) / chm::kScanBlock);
+    chm::scan_blocks_kernel<<<nblocks, 1024, 0, st>>>(w.counts, n_clusters, cluster_pos, w.sums);
+    CHM_TRY(chm::launch_status("scan_blocks_kernel"));
+    chm::scan_sums_kernel<<<1, 1024, 0, st>>>(w.sums, nblocks, cluster_pos + n_clusters);
+    CHM_TRY(chm::launch_status("scan_sums_kernel"));
+    chm::scan_add_kernel<<<nblocks, 1024, 0, st>>>(cluster_pos, n_clusters, w.sums);
+    CHM_TRY(chm::launch_status("scan_add_kernel"));
+    chm::cluster_scatter_kernel<<<grid, 256, 0, st>>>(assign, n, n_clusters, cluster_pos, w.fill, inv);
+    CHM_TRY(chm::launch_status("cluster_scatter_kernel"));
+    chm::cluster_sort_small_kernel<<<(unsigned)std::min<int64_t>(n_clusters, 148 * 8), 256, 0, st>>>(
+        inv, cluster_pos, n_clusters, w.big, w.n_big);
+    CHM_TRY(chm::launch_status("cluster_sort_small_kernel"));
+    const size_t big_smem = sizeof(uint32_t) * chm::kListBig;
+    CHM_CUDA(cudaFuncSetAttribute(chm::cluster_sort_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)big_smem));
+    chm::cluster_sort_big_kernel<<<148, 1024, big_smem, st>>>(inv, cluster_pos, w.big, w.n_big, w.bad);
+    CHM_TRY(chm::launch_status("cluster_sort_big_kernel"));
+    chm::token_docs_kernel<<<grid, 256, 0, st>>>(doc_ptrs, num_docs, w.tok_doc);
+    CHM_TRY(chm::launch_status("token_docs_kernel"));
+    chm::cluster_gather_kernel<<<grid, 256, 0, st>>>(inv, n, cluster_pos + n_clusters,
+                                                     reinterpret_cast<const uint4*>(codes_tok), factor_tok,
+                                                     w.tok_doc, reinterpret_cast<uint4*>(codes1), factor1, doc_ids,
+                                                     tok2pos);
+    CHM_TRY(chm::launch_status("cluster_gather_kernel"));
+    if (status) CHM_CUDA(cudaMemcpyAsync(status, w.bad, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+    return CHM_OK;
+}

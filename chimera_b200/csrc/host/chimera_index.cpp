@@ -74,6 +74,19 @@ struct DevBuf {
         alloc(count * sizeof(T));
         check_cuda(cudaMemcpy(p, src, count * sizeof(T), cudaMemcpyHostToDevice), "upload");
     }
+    template <typename T>
+    void download(std::vector<T>& dst, size_t count) const {
+        dst.resize(count);
+        if (count) check_cuda(cudaMemcpy(dst.data(), p, count * sizeof(T), cudaMemcpyDeviceToHost), "download");
+    }
+    // Takes over o's allocation.
+    void take(DevBuf& o) {
+        reset();
+        p = o.p;
+        bytes = o.bytes;
+        o.p = nullptr;
+        o.bytes = 0;
+    }
 };
 
 void validate_search_options(const SearchOptions& o) {  // chimera_index.cu:27-36
@@ -146,10 +159,11 @@ struct chimera_index::Impl {
     std::vector<float> centroids_rot;     // [n_clusters * 128]
     bool has_index = false;
     bool ready = false;
+    bool host_current = true;  // false after a device build: save() downloads the arrays
 
     DevBuf d_cluster_pos, d_codes1, d_factor1, d_doc_ids, d_tok2pos, d_doc_ptrs, d_full, d_ff, d_cent,
         d_cnorm, d_flips, d_cent_bf16, d_cnmax, d_ws, d_q, d_res, d_nres, d_codes1_tok, d_factor1_tok,
-        d_tok_cluster;
+        d_tok_cluster, d_inv;
     size_t ws_bytes = 0;
     int ws_batch = 0;
     int table_extra = 0;
@@ -167,7 +181,7 @@ struct chimera_index::Impl {
         }
         for (DevBuf* b : {&d_cluster_pos, &d_codes1, &d_factor1, &d_doc_ids, &d_tok2pos, &d_doc_ptrs, &d_full,
                           &d_ff, &d_cent, &d_cnorm, &d_flips, &d_cent_bf16, &d_cnmax, &d_ws, &d_q, &d_res,
-                          &d_nres, &d_codes1_tok, &d_factor1_tok, &d_tok_cluster})
+                          &d_nres, &d_codes1_tok, &d_factor1_tok, &d_tok_cluster, &d_inv})
             b->reset();
         ready = false;
         ws_bytes = 0;
@@ -188,6 +202,27 @@ struct chimera_index::Impl {
         centroids_rot.clear();
         n = d = n_clusters = ex_bits = 0;
         has_index = false;
+        host_current = true;
+    }
+
+    // The host copies save() writes, from the device index a device build left.
+    void ensure_host() {
+        if (host_current) return;
+        std::vector<int64_t> cpos;
+        d_cluster_pos.download(cpos, n_clusters + 1);
+        cluster_pos.assign(cpos.begin(), cpos.end());
+        d_inv.download(inv_list, n);
+        d_codes1_tok.download(one_bit_codes, n * 2);
+        d_factor1_tok.download(one_bit_factors, n);
+        d_full.download(full_codes, n * full_stride());
+        d_ff.download(full_factors, n);
+        d_cent.download(centroids_rot, n_clusters * kPadded);
+        clustered.resize(n * 28);  // cluster_1bit.bin: codes, factors, doc ids, token positions
+        check_cuda(cudaMemcpy(clustered.data(), d_codes1.p, n * 16, cudaMemcpyDeviceToHost), "download");
+        check_cuda(cudaMemcpy(clustered.data() + n * 16, d_factor1.p, n * 4, cudaMemcpyDeviceToHost), "download");
+        check_cuda(cudaMemcpy(clustered.data() + n * 20, d_doc_ids.p, n * 4, cudaMemcpyDeviceToHost), "download");
+        check_cuda(cudaMemcpy(clustered.data() + n * 24, d_tok2pos.p, n * 4, cudaMemcpyDeviceToHost), "download");
+        host_current = true;
     }
 
     static void select_device() {
@@ -198,26 +233,6 @@ struct chimera_index::Impl {
     }
 
     size_t full_stride() const { return kPadded * (1 + ex_bits) / 8; }
-
-    void make_clustered(const std::vector<uint64_t>& codes_tok, const std::vector<float>& f1_tok) {
-        // reorder_by_cluster, build_index.cu:328-363
-        std::vector<int> token_doc(n);
-        size_t t = 0;
-        for (size_t doc = 0; doc < doc_lens.size(); ++doc)
-            for (int j = 0; j < doc_lens[doc]; ++j) token_doc[t++] = static_cast<int>(doc);
-        clustered.assign(n * (16 + 4 + 4 + 4), 0);
-        char* codes = clustered.data();
-        float* fac = reinterpret_cast<float*>(codes + n * 16);
-        int* docs = reinterpret_cast<int*>(codes + n * 20);
-        uint32_t* t2p = reinterpret_cast<uint32_t*>(codes + n * 24);
-        for (size_t pos = 0; pos < n; ++pos) {
-            const uint32_t tok = inv_list[pos];
-            std::memcpy(codes + pos * 16, reinterpret_cast<const char*>(codes_tok.data()) + size_t(tok) * 16, 16);
-            fac[pos] = f1_tok[tok];
-            docs[pos] = token_doc[tok];
-            t2p[tok] = static_cast<uint32_t>(pos);
-        }
-    }
 
     void init_device() {
         if (ready) return;
@@ -248,16 +263,7 @@ struct chimera_index::Impl {
         d_ff.upload(full_factors.data(), full_factors.size());
         d_cent.upload(centroids_rot.data(), centroids_rot.size());
         d_flips.upload(flips.data(), flips.size());
-        d_cnorm.alloc(n_clusters * sizeof(float));
         check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
-        throw_status(chm_row_norms(d_cent.as<float>(), static_cast<int64_t>(n_clusters), d_cnorm.as<float>(), stream),
-                     "centroid norms");
-        d_cent_bf16.alloc(n_clusters * kPadded * 2);
-        d_cnmax.alloc(sizeof(float));
-        throw_status(chm_to_bf16(d_cent.as<float>(), static_cast<int64_t>(n_clusters * kPadded), d_cent_bf16.p, stream),
-                     "centroid bf16 copy");
-        throw_status(chm_max_value(d_cnorm.as<float>(), static_cast<int64_t>(n_clusters), d_cnmax.as<float>(), stream),
-                     "centroid norm max");
         // token-order copies of the 1-bit arrays: refinement reads each doc as one span
         d_codes1_tok.alloc(n * 16);
         d_factor1_tok.alloc(n * sizeof(float));
@@ -271,18 +277,34 @@ struct chimera_index::Impl {
                                         d_tok2pos.as<uint32_t>(), static_cast<int64_t>(n), d_tok_cluster.as<uint32_t>(),
                                         stream),
                      "token clusters");
-        int32_t max_doc = 0;
-        for (int len : doc_lens) max_doc = std::max<int32_t>(max_doc, len);
         int32_t max_list = 0;
         for (size_t c = 0; c < n_clusters; ++c)
             max_list = std::max<int32_t>(max_list, static_cast<int32_t>(cluster_pos[c + 1] - cluster_pos[c]));
-        view = chm_index{static_cast<int64_t>(n), static_cast<int64_t>(num_docs), static_cast<int64_t>(n_clusters),
-                         static_cast<int32_t>(ex_bits), static_cast<int32_t>(d), max_list, max_doc,
-                         d_cluster_pos.as<int64_t>(), d_codes1.as<uint8_t>(), d_factor1.as<float>(),
-                         d_doc_ids.as<int32_t>(), d_tok2pos.as<uint32_t>(), d_doc_ptrs.as<int64_t>(),
-                         d_full.as<uint8_t>(), d_ff.as<float>(), d_cent.as<float>(), d_cnorm.as<float>(),
-                         d_flips.as<uint8_t>(), d_cent_bf16.p, d_cnmax.as<float>(), d_codes1_tok.as<uint8_t>(),
-                         d_factor1_tok.as<float>(), d_tok_cluster.as<uint32_t>()};
+        finalize_device(max_list);
+    }
+
+    // Centroid norms, their bf16 copy and max, and the chm_index view over the
+    // device arrays (cluster- and token-order 1-bit data, full codes,
+    // token clusters) a load or a device build left.
+    void finalize_device(int32_t max_list) {
+        d_cnorm.alloc(n_clusters * sizeof(float));
+        throw_status(chm_row_norms(d_cent.as<float>(), static_cast<int64_t>(n_clusters), d_cnorm.as<float>(), stream),
+                     "centroid norms");
+        d_cent_bf16.alloc(n_clusters * kPadded * 2);
+        d_cnmax.alloc(sizeof(float));
+        throw_status(chm_to_bf16(d_cent.as<float>(), static_cast<int64_t>(n_clusters * kPadded), d_cent_bf16.p, stream),
+                     "centroid bf16 copy");
+        throw_status(chm_max_value(d_cnorm.as<float>(), static_cast<int64_t>(n_clusters), d_cnmax.as<float>(), stream),
+                     "centroid norm max");
+        int32_t max_doc = 0;
+        for (int len : doc_lens) max_doc = std::max<int32_t>(max_doc, len);
+        view = chm_index{static_cast<int64_t>(n), static_cast<int64_t>(doc_lens.size()),
+                         static_cast<int64_t>(n_clusters), static_cast<int32_t>(ex_bits), static_cast<int32_t>(d),
+                         max_list, max_doc, d_cluster_pos.as<int64_t>(), d_codes1.as<uint8_t>(),
+                         d_factor1.as<float>(), d_doc_ids.as<int32_t>(), d_tok2pos.as<uint32_t>(),
+                         d_doc_ptrs.as<int64_t>(), d_full.as<uint8_t>(), d_ff.as<float>(), d_cent.as<float>(),
+                         d_cnorm.as<float>(), d_flips.as<uint8_t>(), d_cent_bf16.p, d_cnmax.as<float>(),
+                         d_codes1_tok.as<uint8_t>(), d_factor1_tok.as<float>(), d_tok_cluster.as<uint32_t>()};
         check_cuda(cudaStreamSynchronize(stream), "index upload");
         ready = true;
     }
@@ -410,30 +432,50 @@ void chimera_index::build(const std::vector<float>& embeddings, size_t dimension
                                   static_cast<int32_t>(d), static_cast<int32_t>(ex_bits), codes1.as<uint8_t>(),
                                   f1.as<float>(), full.as<uint8_t>(), ff.as<float>(), nullptr, st),
                  "encoding");
-    std::vector<uint32_t> assign(n);
-    m.one_bit_codes.resize(n * 2);
-    m.one_bit_factors.resize(n);
-    m.full_codes.resize(n * fstride);
-    m.full_factors.resize(n);
-    m.centroids_rot.resize(n_clusters * kPadded);
-    check_cuda(cudaMemcpyAsync(assign.data(), assign_d.p, n * 4, cudaMemcpyDeviceToHost, st), "copy");
-    check_cuda(cudaMemcpyAsync(m.one_bit_codes.data(), codes1.p, n * 16, cudaMemcpyDeviceToHost, st), "copy");
-    check_cuda(cudaMemcpyAsync(m.one_bit_factors.data(), f1.p, n * 4, cudaMemcpyDeviceToHost, st), "copy");
-    check_cuda(cudaMemcpyAsync(m.full_codes.data(), full.p, n * fstride, cudaMemcpyDeviceToHost, st), "copy");
-    check_cuda(cudaMemcpyAsync(m.full_factors.data(), ff.p, n * 4, cudaMemcpyDeviceToHost, st), "copy");
-    check_cuda(cudaMemcpyAsync(m.centroids_rot.data(), cent_rot.p, n_clusters * kPadded * 4, cudaMemcpyDeviceToHost,
-                               st),
-               "copy");
+    // IVF_PG::build_from_assignments + reorder_by_cluster (ivf_pg.cpp:110-126,
+    // build_index.cu:328-363) on the device; the result stays there as the
+    // search index (host copies are made only if the index is saved)
+    std::vector<int64_t> ptrs(doc_lens.size() + 1, 0);
+    for (size_t i = 0; i < doc_lens.size(); ++i) ptrs[i + 1] = ptrs[i] + doc_lens[i];
+    m.d_doc_ptrs.upload(ptrs.data(), ptrs.size());
+    m.d_cluster_pos.alloc((n_clusters + 1) * sizeof(int64_t));
+    m.d_inv.alloc(n * sizeof(uint32_t));
+    m.d_codes1.alloc(n * 16);
+    m.d_factor1.alloc(n * sizeof(float));
+    m.d_doc_ids.alloc(n * sizeof(int32_t));
+    m.d_tok2pos.alloc(n * sizeof(uint32_t));
+    DevBuf status, ows;
+    status.alloc(sizeof(uint32_t));
+    const size_t owb = chm_build_cluster_order_workspace_bytes(static_cast<int64_t>(n), static_cast<int64_t>(n_clusters));
+    ows.alloc(owb);
+    throw_status(chm_build_cluster_order(assign_d.as<uint32_t>(), static_cast<int64_t>(n),
+                                         static_cast<int64_t>(n_clusters), m.d_doc_ptrs.as<int64_t>(),
+                                         static_cast<int64_t>(doc_lens.size()), codes1.as<uint8_t>(), f1.as<float>(),
+                                         m.d_cluster_pos.as<int64_t>(), m.d_inv.as<uint32_t>(), m.d_codes1.as<uint8_t>(),
+                                         m.d_factor1.as<float>(), m.d_doc_ids.as<int32_t>(),
+                                         m.d_tok2pos.as<uint32_t>(), status.as<uint32_t>(), ows.p, owb, st),
+                 "cluster order");
+    uint32_t bad = 0;
+    check_cuda(cudaMemcpyAsync(&bad, status.p, sizeof(bad), cudaMemcpyDeviceToHost, st), "copy");
+    std::vector<int64_t> cpos(n_clusters + 1);
+    check_cuda(cudaMemcpyAsync(cpos.data(), m.d_cluster_pos.p, cpos.size() * 8, cudaMemcpyDeviceToHost, st), "copy");
     check_cuda(cudaStreamSynchronize(st), "index build");
-    // IVF_PG::build_from_assignments (ivf_pg.cpp:110-126): stable counting sort
-    m.cluster_pos.assign(n_clusters + 1, 0);
-    for (size_t i = 0; i < n; ++i) ++m.cluster_pos[assign[i] + 1];
-    for (size_t c = 0; c < n_clusters; ++c) m.cluster_pos[c + 1] += m.cluster_pos[c];
-    m.inv_list.resize(n);
-    std::vector<size_t> wp(m.cluster_pos.begin(), m.cluster_pos.end() - 1);
-    for (size_t i = 0; i < n; ++i) m.inv_list[wp[assign[i]]++] = static_cast<uint32_t>(i);
-    m.make_clustered(m.one_bit_codes, m.one_bit_factors);
+    if (bad) throw std::runtime_error(bad & 2 ? "An inverted list exceeds 32768 tokens" : "Invalid assignment");
+    m.cluster_pos.assign(cpos.begin(), cpos.end());
+    m.d_full.take(full);
+    m.d_ff.take(ff);
+    m.d_cent.take(cent_rot);
+    m.d_flips.take(flips_d);
+    m.d_codes1_tok.take(codes1);
+    m.d_factor1_tok.take(f1);
+    m.d_tok_cluster.take(assign_d);
+    int32_t max_list = 0;
+    for (size_t c = 0; c < n_clusters; ++c)
+        max_list = std::max<int32_t>(max_list, static_cast<int32_t>(cpos[c + 1] - cpos[c]));
+    check_cuda(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking), "cudaStreamCreate");
     m.has_index = true;
+    m.host_current = false;
+    m.finalize_device(max_list);
 }
 
 std::vector<size_t> chimera_index::search(const std::vector<float>& query, size_t k) {
@@ -467,8 +509,9 @@ std::vector<std::vector<size_t>> chimera_index::search_batch(const float* querie
 }
 
 void chimera_index::save(const std::string& index_dir) const {
-    const Impl& m = *impl_;
+    Impl& m = *impl_;
     if (!m.has_index) throw std::runtime_error("Cannot save an empty Chimera index");
+    m.ensure_host();
     namespace fs = std::filesystem;
     std::error_code ec;
     fs::create_directories(index_dir, ec);

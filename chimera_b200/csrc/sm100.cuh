@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features used by the tensor-core
-// kernels: mbarriers (with bounded waits), TMA tile loads (no multicast),
+// kernels: mbarriers (with bounded waits), TMA tile loads into this CTA only,
 // TMEM allocation and tcgen05 MMA / commit / load.
 #pragma once
 #include <cuda.h>

@@ -21,8 +21,8 @@
 // GEMM kernel: one CTA = 128 query rows x a range of 128-centroid tiles.
 // Warp 0 issues TMA loads (A once, B through a 4-stage ring), warp 1 owns
 // TMEM and issues tcgen05.mma (M=128, N=128, K=16 x 8) into two TMEM
-// accumulators, warps 4-7 drain TMEM with tcgen05.ld.  No cluster multicast
-// is used anywhere.
+// accumulators, warps 4-7 drain TMEM with tcgen05.ld.  Every TMA load goes to
+// the issuing CTA alone (no cluster-wide delivery).
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 

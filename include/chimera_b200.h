@@ -302,6 +302,24 @@ chm_status chm_build_encode(const uint8_t* flips, const float* x, int64_t n, int
                             int32_t ex_bits, uint8_t* codes1, float* f1, uint8_t* full,
                             float* ff, float* rot, void* stream);
 
+/* IVF lists and the cluster-ordered 1-bit arrays from the assignment
+ * (IVF_PG::build_from_assignments, ivf_pg.cpp:110-126: a stable counting sort
+ * of the tokens by cluster; reorder_by_cluster, build_index.cu:328-363).
+ * assign [n] cluster of every token; doc_ptrs [num_docs + 1]; codes_tok
+ * [n*16] and factor_tok [n] the encoder's 1-bit output in token order.
+ * Writes cluster_pos [n_clusters + 1], inv [n] (position -> token, ivf.bin),
+ * codes1 [n*16], factor1 [n], doc_ids [n] (cluster order) and tok2pos [n].
+ * status (device u32, may be NULL): bit 0 an assignment out of range (its
+ * token gets no position), bit 1 a list longer than 32,768 tokens (left
+ * unsorted); 0 on success.
+ * n_clusters <= 16,777,216. */
+size_t chm_build_cluster_order_workspace_bytes(int64_t n, int64_t n_clusters);
+chm_status chm_build_cluster_order(const uint32_t* assign, int64_t n, int64_t n_clusters, const int64_t* doc_ptrs,
+                                   int64_t num_docs, const uint8_t* codes_tok, const float* factor_tok,
+                                   int64_t* cluster_pos, uint32_t* inv, uint8_t* codes1, float* factor1,
+                                   int32_t* doc_ids, uint32_t* tok2pos, uint32_t* status, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* Token-order copy of the cluster-ordered 1-bit arrays:
  * codes_tok[t] = codes1[tok2pos[t]], factor_tok[t] = factor1[tok2pos[t]]
  * (the inverse of reorder_by_cluster's permutation, build_index.cu:328-363).

@@ -115,3 +115,45 @@ def test_cli_build_and_search(tmp_path):
     # latency line leaves std::cout in fixed 3-digit mode (search.cpp:33)
     assert lines[1] == f"[SEARCH] recall@{cfg.k}=1.000"
     assert any(l.startswith("[SEARCH] batched qps=") for l in lines)
+
+
+def _reference_layout_files(c):
+    """The five index files in the reference's layout (chimera_index::save,
+    build_index.cu:503-557; IndexHeader, chimera_index.cuh:75-81), written
+    here from the oracle-built arrays of the corpus."""
+    cfg = c["cfg"]
+    n = c["emb"].shape[0]
+    dl = np.asarray(c["doclens"], np.int32)
+    ix = c["index"]
+    files = {}
+    files["doclens.bin"] = struct.pack("<i", len(dl)) + dl.tobytes()
+    files["doc_1bit.bin"] = (struct.pack("<5Q", n, c["dim"], cfg.n_clusters, cfg.ex_bits, 128) +
+                             np.asarray(c["flips"], np.uint8).tobytes() +
+                             np.ascontiguousarray(c["codes1_tok"], np.uint8).tobytes() +
+                             np.asarray(c["f1_tok"], np.float32).tobytes() + np.asarray(c["ff"], np.float32).tobytes())
+    files["doc_full.bin"] = np.ascontiguousarray(c["full"], np.uint8).tobytes()
+    files["cluster_1bit.bin"] = (np.ascontiguousarray(ix.codes1, np.uint8).tobytes() +
+                                 np.asarray(ix.factor1, np.float32).tobytes() +
+                                 np.asarray(ix.doc_ids, np.int32).tobytes() +
+                                 np.asarray(c["tok2pos"], np.uint32).tobytes())
+    files["ivf.bin"] = (struct.pack("<Q", n) + np.asarray(c["inv"], np.uint32).tobytes() +
+                        np.asarray(c["cluster_pos"], np.uint64).tobytes())
+    return files
+
+
+@pytest.mark.gpu
+def test_saved_files_are_the_reference_layout_byte_for_byte(tmp_path):
+    """ChimeraIndex.build (assignment, encoding and the IVF reorder on the GPU,
+    the index kept on the device) then save(): each of the five
+    reference-format files equals, byte for byte, the file the reference's
+    layout gives for the oracle-built index of the same corpus."""
+    chimera = _chimera()
+    c = _corpus.corpus("small")
+    cfg = c["cfg"]
+    idx = chimera.ChimeraIndex.build(np.ascontiguousarray(c["emb"]), [int(x) for x in c["doclens"]],
+                                     cfg.n_clusters, cfg.ex_bits)
+    idx.save(str(tmp_path / "ix"))
+    for name, want in _reference_layout_files(c).items():
+        got = open(tmp_path / "ix" / name, "rb").read()
+        assert len(got) == len(want), name
+        assert got == want, name
