@@ -94,6 +94,9 @@ class ClockSampler:
 # scaled here by this run's refined tokens.
 NCU_TRAFFIC_PER_UNIT = {"refine_1bit": 100.2}
 
+METRIC = {"c3": "QPS at Recall@100 (C3 passage corpus)", "c4": "QPS at Recall@100 (C4 long-document corpus)",
+          "c5": "QPS at Recall@100 (C5 large sharded corpus)", "c1": "QPS at Recall@100 (C1 small corpus)"}
+
 
 def peaks():
     try:
@@ -331,7 +334,7 @@ def main():
         # label memset-free fold (the collectives are NCCL's own kernels)
         launches = sum(s["launches"] for s in stages) + 1 + 3
     line = {
-        "metric": "QPS at Recall@100 (C3 passage corpus)",
+        "metric": METRIC.get(cfg.name, f"QPS at Recall@100 ({cfg.name})"),
         "value": round(qps, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32+u8", "data": "synthetic",
@@ -754,7 +757,7 @@ def run_reference(args, cfg, index, queries, torch, emb, ptr_full):
     wl = (f"{cfg.name}: {cfg.num_docs} docs, {int(index.n_tokens)} tokens, {cfg.n_clusters} clusters, "
           f"ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, k_refine {cfg.k_refine}, k_full_bit {cfg.k_full_bit}, "
           f"k {cfg.k}")
-    base = {"impl": "reference", "metric": "QPS at Recall@100 (C3 passage corpus)", "unit": "queries/s",
+    base = {"impl": "reference", "metric": METRIC.get(cfg.name, f"QPS at Recall@100 ({cfg.name})"), "unit": "queries/s",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": W,
             "higher_is_better": True, "data": "synthetic"}
     if not O.ref_search_available():

@@ -10,6 +10,8 @@
 // global top k_refine.  chm_shard_localize turns global ids into this rank's
 // local ids (-1 where another shard owns the document), which the refine and
 // full-bit kernels skip.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace chm {
@@ -113,8 +115,11 @@ extern "C" chm_status chm_shard_localize(int32_t nq, int32_t cap, const int32_t*
 extern "C" size_t chm_stage1_ex_workspace_bytes(const chm_index* idx, int32_t nq, int32_t nprobe,
                                                 int32_t table_log2_extra) {
     if (!idx || nq <= 0 || nprobe <= 0 || table_log2_extra < 0 || table_log2_extra > 8) return 0;
-    // sized for the largest k_refine: the call's own k_refine is not an argument
-    return chm::stage1_bytes(idx, nq, nprobe, table_log2_extra, CHM_MAX_K_REFINE);
+    // sized for any k_refine (the call's own is not an argument): the
+    // dense-bound pass, when it runs (k_refine <= num_docs), needs the same
+    // bytes for every k_refine
+    const int64_t kr = std::max<int64_t>(1, std::min<int64_t>(CHM_MAX_K_REFINE, idx->num_docs));
+    return chm::stage1_bytes(idx, nq, nprobe, table_log2_extra, (int)kr);
 }
 
 extern "C" chm_status chm_stage1_ex(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,

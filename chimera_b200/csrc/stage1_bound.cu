@@ -572,10 +572,12 @@ __global__ void __launch_bounds__(1024) bound_final_kernel(const uint64_t* __res
 // The probed-cluster map holds 32 x nprobe clusters at most half full.
 constexpr int kBMaxNprobe = kMapSlots / (2 * kQ);
 
+// k_refine above the doc count leaves every query with fewer positive docs
+// than k_refine (the hash-table path's zero-score fill), so the pass is skipped.
 bool bound_enabled(const chm_index* idx, int nprobe, int k_refine) {
     return idx->tok_cluster && idx->codes1_tok && idx->factor1_tok && idx->max_doc_len > 0 &&
            idx->num_docs > 0 && nprobe > 0 && nprobe <= kBMaxNprobe && k_refine > 0 &&
-           k_refine <= CHM_MAX_K_REFINE;
+           k_refine <= CHM_MAX_K_REFINE && (int64_t)k_refine <= idx->num_docs;
 }
 
 int bound_kc(const chm_index* idx, int k_refine) {
@@ -606,8 +608,8 @@ struct BoundWork {
 
 template <typename A>
 void bound_layout(A& a, const chm_index* idx, int nq, int k_refine, BoundWork* w) {
-    (void)k_refine;
-    const int kc = bound_kc2(idx);  // room for the second round's candidates
+    // room for either round's candidates
+    const int kc = std::max(bound_kc(idx, k_refine), bound_kc2(idx));
     auto S = a.template take<float>((size_t)nq * idx->num_docs);
     auto hist = a.template take<uint32_t>((size_t)std::max(nq, kBPreSlots) * 4096);
     auto npos = a.template take<uint32_t>((size_t)nq);
