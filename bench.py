@@ -88,11 +88,11 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-# DRAM bytes per unit of work of the dominant kernel, from the full ncu capture
-# in profiles/refine_tc_c3s_b32_full.md (c3s corpus, 32 queries: the 1-bit
-# tensor-core refinement read + wrote 865 MB for 8.63 M refined tokens),
-# scaled here by this run's refined tokens.
-NCU_TRAFFIC_PER_UNIT = {"refine_1bit": 100.2}
+# DRAM bytes per unit of work of the dominant kernel, from the ncu capture in
+# profiles/stage1_bound_refine_c3s_b32.md (c3s corpus, 32 queries: the 1-bit
+# tensor-core refinement over token-order codes read + wrote 153.9 MB for
+# 6.30 M refined tokens), scaled here by this run's refined tokens.
+NCU_TRAFFIC_PER_UNIT = {"refine_1bit": 24.4}
 
 METRIC = {"c3": "QPS at Recall@100 (C3 passage corpus)", "c4": "QPS at Recall@100 (C4 long-document corpus)",
           "c5": "QPS at Recall@100 (C5 large sharded corpus)", "c1": "QPS at Recall@100 (C1 small corpus)"}
@@ -141,6 +141,8 @@ def main():
                     help="queries searched by the CPU oracle and compared with the GPU results")
     ap.add_argument("--ref-sample", type=int, default=16, help="queries per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--streamed", action="store_true",
+                    help="generate and build the corpus chunk by chunk (always on for c5)")
     ap.add_argument("--micro", choices=["probe", "lut"], default=None,
                     help="operator microbench (BASELINE config C2) instead of the search bench")
     ap.add_argument("--lut-codes", type=int, default=1 << 26, help="codes scored per step by --micro lut")
@@ -167,36 +169,55 @@ def main():
 
     cfg = W.CONFIGS[args.config]
     t0 = time.time()
-    emb, doclens, queries = W.generate_torch(cfg, seed=0)
-    log(f"[bench] corpus {cfg.name}: {emb.shape[0]} tokens, {cfg.num_docs} docs ({time.time() - t0:.1f}s)")
+    # corpora whose raw embeddings do not fit one device (C5: 600M tokens x
+    # 512 B) are generated chunk by chunk (the same values) and built in chunks
+    streamed = args.streamed or cfg.name == "c5"
+    sc = None
+    if streamed:
+        sc = W.StreamedCorpus(cfg, seed=0)
+        emb, doclens = None, sc.doclens
+        queries = sc.queries()
+        n_tok = sc.n
+    else:
+        emb, doclens, queries = W.generate_torch(cfg, seed=0)
+        n_tok = int(emb.shape[0])
+    log(f"[bench] corpus {cfg.name}: {n_tok} tokens, {cfg.num_docs} docs ({time.time() - t0:.1f}s)"
+        + (", streamed" if streamed else ""))
     dl_host = doclens.cpu().numpy()
-    ptr_full = torch.from_numpy(W.doc_ptrs(dl_host)).to(emb.device)
+    ptr_full = torch.from_numpy(W.doc_ptrs(dl_host)).to(queries.device)
     t0 = time.time()
-    if world == 1 or args.impl == "reference":
-        index, _ = capi.build_index(emb, dl_host, cfg.n_clusters, cfg.ex_bits)
+    whole = world == 1 or args.impl == "reference"
+    if whole:
         bases = [0, cfg.num_docs]
     else:
         # document shard: docs [bases[rank], bases[rank+1]) with the centroids
         # sampled from the whole corpus (the single-GPU build's centroids)
         bases = SH.shard_bounds(cfg.num_docs, world)
-        lo, hi = bases[rank], bases[rank + 1]
-        t_lo, t_hi = int(ptr_full[lo]), int(ptr_full[hi])
-        ids = torch.from_numpy(capi.sample_centroids(int(emb.shape[0]), cfg.n_clusters, 42)).to(emb.device)
-        cents = emb[ids].contiguous()
-        index, _ = capi.build_index(emb[t_lo:t_hi].contiguous(), dl_host[lo:hi], cfg.n_clusters, cfg.ex_bits,
-                                    centroids=cents)
-        del cents
+    lo, hi = bases[rank if not whole else 0], bases[rank + 1 if not whole else 1]
+    t_lo, t_hi = int(ptr_full[lo]), int(ptr_full[hi])
+    ids = torch.from_numpy(capi.sample_centroids(n_tok, cfg.n_clusters, 42)).to(queries.device)
+    cents = emb[ids].contiguous() if emb is not None else sc.gather(ids)
+    if emb is not None:
+        chunks = lambda: iter([(0, t_hi - t_lo, emb[t_lo:t_hi])])
+    else:
+        chunks = lambda: ((s - t_lo, e - t_lo, x) for s, e, x in sc.chunks(t_lo, t_hi))
+    index = capi.build_index_streamed(chunks, t_hi - t_lo, cfg.dim, dl_host[lo:hi], cfg.n_clusters, cfg.ex_bits,
+                                      cents)[0]
+    del cents, ids
     torch.cuda.synchronize()
-    log(f"[bench] index built in {time.time() - t0:.1f}s (rank {rank}, docs {bases[rank]}..{bases[rank + 1]})")
+    log(f"[bench] index built in {time.time() - t0:.1f}s (rank {rank}, docs {lo}..{hi})")
 
     if args.impl == "reference":
-        run_reference(args, cfg, index, queries, torch, emb, ptr_full)
+        run_reference(args, cfg, index, queries, torch, emb, ptr_full, sc)
         return
 
     # exact MaxSim ground truth for the recall check, before the corpus is freed
     nq_total = queries.shape[0]
     nrec = min(args.recall_queries, nq_total)
-    gt = ground_truth(torch, emb, ptr_full, queries, cfg.k, list(range(nrec))) if (nrec > 0 and rank == 0) else None
+    gt = None
+    if nrec > 0 and rank == 0:
+        gt = (ground_truth(torch, emb, ptr_full, queries, cfg.k, list(range(nrec))) if emb is not None else
+              W.ground_truth_streamed(sc, queries[:nrec], cfg.k))
     del emb
     torch.cuda.empty_cache()
 
@@ -315,7 +336,10 @@ def main():
         shard_steps["exchange_share"] = round(xch / tot, 4) if tot > 0 else None
 
     # ---- per-stage profile on this rank's (shard) index, exchange excluded --
-    prof_searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
+    # (one GPU: the timed searcher itself, whose workspace is the largest
+    # allocation of a big batch)
+    torch.cuda.empty_cache()
+    prof_searcher = searcher if world == 1 else capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
     stages, stages_extra = profile_stages(torch, capi, index, prof_searcher, batches[args.warmup], cfg)
     del prof_searcher
 
@@ -544,7 +568,10 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
         return L.chm_probe(P(rot), ntok, P(index.centroids), P(index.centroid_norms), index.n_clusters, p.nprobe,
                            P(labels), P(pws), pb, st)
     sb = L.chm_stage1_workspace_bytes(C.byref(index.view), B, p.nprobe, p.k_refine)
-    sws = torch.empty(sb, dtype=torch.uint8, device=dev)
+    # the search workspace (idle here) holds stage 1's, which dominates it
+    ws_search = getattr(searcher, "_ws", None)
+    sws = ws_search if ws_search is not None and ws_search.numel() >= sb else \
+        torch.empty(sb, dtype=torch.uint8, device=dev)
     rd = torch.empty(B, p.k_refine, dtype=torch.int32, device=dev)
     rp = torch.empty(B, p.k_refine, device=dev)
     nr = torch.empty(B, dtype=torch.int32, device=dev)
@@ -738,12 +765,17 @@ def oracle_parity(args, cfg, index, queries, torch, gpu_results, gt):
             "oracle_qps": round(P / secs, 3)}
 
 
+def W_module():
+    from chimera_b200 import workloads
+    return workloads
+
+
 def W_recall(gt, res, k):
     from chimera_b200 import workloads as W
     return W.recall_at_k(gt, res, k)
 
 
-def run_reference(args, cfg, index, queries, torch, emb, ptr_full):
+def run_reference(args, cfg, index, queries, torch, emb, ptr_full, sc=None):
     """The reference's own search path (oracle/ref_search.cu: its CUDA kernels,
     host flow and AVX-512 full-bit scorer; an exact cuBLAS probe stands in for
     cuVS CAGRA, which is not installable here), one query per call as
@@ -771,7 +803,10 @@ def run_reference(args, cfg, index, queries, torch, emb, ptr_full):
     warm_idx = [(nq_total - 1 - i) % nq_total for i in range(W * per)]
     qidx = warm_idx + timed_idx
     timed = sorted(set(timed_idx))
-    gt_list = ground_truth(torch, emb, ptr_full, queries, cfg.k, timed)
+    if emb is not None:
+        gt_list = ground_truth(torch, emb, ptr_full, queries, cfg.k, timed)
+    else:
+        gt_list = W_module().ground_truth_streamed(sc, queries[timed], cfg.k)
     gt = dict(zip(timed, gt_list))
     del emb
     torch.cuda.empty_cache()

@@ -322,10 +322,27 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
     `centroids` ([n_clusters, dim] raw device tensor) replaces the sampling:
     a document shard is built with the centroids sampled from the whole
     corpus, so every shard shares the global cluster ids."""
+    n, dim = int(emb.shape[0]), int(emb.shape[1])
+    if centroids is None:
+        ids = __import__("torch").from_numpy(sample_centroids(n, n_clusters, 42)).to(emb.device)
+        centroids = emb[ids].contiguous()
+    return build_index_streamed(lambda: iter([(0, n, emb)]), n, dim, doclens, n_clusters, ex_bits, centroids,
+                                seed=seed, stream=stream)
+
+
+def build_index_streamed(chunks, n: int, dim: int, doclens, n_clusters: int, ex_bits: int, centroids,
+                         seed: int = 42, stream=None):
+    """build_index over embeddings that arrive in chunks, for corpora whose
+    raw embeddings do not fit on the device at once.  `chunks()` yields
+    (s, e, x): x the [e - s, dim] f32 device rows of tokens s..e-1, in order,
+    covering 0..n-1; `centroids` the [n_clusters, dim] raw centroids (for the
+    whole corpus: sample_centroids' token ids).  Every token is assigned and
+    encoded on its own, so the result equals build_index's on the
+    concatenated rows."""
     import time
 
     import torch
-    dev = emb.device
+    dev = centroids.device
     st = _stream(torch, stream)
     verbose = bool(os.environ.get("CHM_VERBOSE"))
     t0 = [time.time()]
@@ -336,54 +353,64 @@ def build_index(emb, doclens, n_clusters: int, ex_bits: int, seed: int = 42, str
             now = time.time()
             print(f"[build] {name}: {now - t0[0]:.2f}s", flush=True)
             t0[0] = now
-    n, dim = int(emb.shape[0]), int(emb.shape[1])
     doclens = np.asarray(doclens, np.int64)
     if doclens.sum() != n:
         raise ValueError("Document lengths do not sum to the number of embeddings")
+    if tuple(centroids.shape) != (n_clusters, dim):
+        raise ValueError("centroids must be [n_clusters, dim]")
     flips_np = fhtkac_flips(seed)
     flips = torch.from_numpy(flips_np).to(dev)
-    if centroids is None:
-        ids = torch.from_numpy(sample_centroids(n, n_clusters, 42)).to(dev)
-        cent_in = emb[ids].contiguous()
-    else:
-        if tuple(centroids.shape) != (n_clusters, dim):
-            raise ValueError("centroids must be [n_clusters, dim]")
-        cent_in = centroids.to(device=dev, dtype=torch.float32).contiguous()
+    cent_in = centroids.to(device=dev, dtype=torch.float32).contiguous()
     if dim < DIM:
-        x128 = torch.zeros(n, DIM, dtype=torch.float32, device=dev)
-        x128[:, :dim] = emb
         cent_raw = torch.zeros(n_clusters, DIM, dtype=torch.float32, device=dev)
         cent_raw[:, :dim] = cent_in
     else:
-        x128 = emb.contiguous()
         cent_raw = cent_in
     cn_raw = torch.empty(n_clusters, dtype=torch.float32, device=dev)
     L = lib()
     check(L.chm_row_norms(_ptr(cent_raw), n_clusters, _ptr(cn_raw), st), "row_norms")
-    assign = torch.empty(n, dtype=torch.int32, device=dev)
-    wsb = L.chm_build_assign_workspace_bytes(n, n_clusters)
-    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
-    check(L.chm_build_assign(_ptr(x128), n, dim, _ptr(cent_raw), _ptr(cn_raw), n_clusters, _ptr(assign),
-                             _ptr(ws), wsb, st), "build_assign")
-    del ws
-    phase("assign")
     # rotated centroids (padded dim) for the probe
     rot_c = torch.empty(n_clusters, DIM, dtype=torch.float32, device=dev)
     cb1_c = torch.empty(n_clusters, dtype=torch.float32, device=dev)
     cbex_c = torch.empty(n_clusters, dtype=torch.float32, device=dev)
     check(L.chm_prepare_queries(_ptr(flips), dim, ex_bits, _ptr(cent_in), n_clusters,
                                 _ptr(rot_c), _ptr(cb1_c), _ptr(cbex_c), None, st), "rotate centroids")
+    del cb1_c, cbex_c
     cnorm = torch.empty(n_clusters, dtype=torch.float32, device=dev)
     check(L.chm_row_norms(_ptr(rot_c), n_clusters, _ptr(cnorm), st), "row_norms")
-    # rotation + RaBitQ encoding
+    # per chunk: exact nearest centroid, rotation + RaBitQ encoding
     fb = DIM * (1 + ex_bits) // 8
+    assign = torch.empty(n, dtype=torch.int32, device=dev)
     codes1 = torch.empty(n, 16, dtype=torch.uint8, device=dev)
     f1 = torch.empty(n, dtype=torch.float32, device=dev)
     full = torch.empty(n, fb, dtype=torch.uint8, device=dev)
     ff = torch.empty(n, dtype=torch.float32, device=dev)
-    check(L.chm_build_encode(_ptr(flips), _ptr(emb.contiguous()), n, dim, ex_bits, _ptr(codes1), _ptr(f1),
-                             _ptr(full), _ptr(ff), None, st), "build_encode")
-    phase("encode")
+    ws, wsb, done = None, 0, 0
+    for s, e, x in chunks():
+        m = e - s
+        if s != done or m <= 0 or tuple(x.shape) != (m, dim):
+            raise ValueError("chunks must cover the tokens in order with [e - s, dim] rows")
+        done = e
+        x = x.contiguous()
+        if dim < DIM:
+            x128 = torch.zeros(m, DIM, dtype=torch.float32, device=dev)
+            x128[:, :dim] = x
+        else:
+            x128 = x
+        need = L.chm_build_assign_workspace_bytes(m, n_clusters)
+        if need > wsb:
+            ws, wsb = None, 0
+            ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+            wsb = need
+        check(L.chm_build_assign(_ptr(x128), m, dim, _ptr(cent_raw), _ptr(cn_raw), n_clusters, _ptr(assign[s:e]),
+                                 _ptr(ws), wsb, st), "build_assign")
+        check(L.chm_build_encode(_ptr(flips), _ptr(x), m, dim, ex_bits, _ptr(codes1[s:e]), _ptr(f1[s:e]),
+                                 _ptr(full[s:e]), _ptr(ff[s:e]), None, st), "build_encode")
+        del x, x128
+    if done != n:
+        raise ValueError("chunks must cover every token")
+    del ws, cent_raw, cn_raw
+    phase("assign + encode")
     doc_ptrs = torch.from_numpy(np.concatenate([[0], np.cumsum(doclens)]).astype(np.int64)).to(dev)
     # IVF_PG::build_from_assignments + reorder_by_cluster (ivf_pg.cpp:110-126,
     # build_index.cu:328-363) on the GPU

@@ -82,13 +82,13 @@ struct __align__(1024) RtSmem {
     float fac[3][kRtRows];
     int row_doc[2][kRtRows];         // item-local doc of each row (-1: past the item's tokens)
     alignas(16) int rec[3][kRtRecWords];
-    uint32_t mx[kRtMaxDocs][32];     // max estimate per (doc, query token) as an ordered key, then the threshold
+    alignas(16) uint32_t mx[kRtMaxDocs][32];  // max estimate per (doc, query token) as an ordered key, then the threshold
     uint32_t maxf[kRtMaxDocs];       // max |factor| per doc (float bits, >= 0)
     uint32_t exact[kRtMaxDocs][32];  // exact max per (doc, query token), ordered keys
     uint32_t cand[kRtMaxCand];       // (row << 5 | t)
     int n_cand;
     float em[32];                    // margin per unit |factor|
-    float cb1[32];
+    alignas(16) float cb1[32];
     uint64_t bar;
     uint32_t tmem_base;
 };
@@ -114,6 +114,22 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// lut_ip with the LUT in global memory (L2-resident): the 32 entries are
+// loaded first, all in flight at once, then added in the reference order.
+__device__ __forceinline__ float lut_ip_ldg(const float* __restrict__ lut, uint4 code) {
+    const uint32_t w[4] = {code.x, code.y, code.z, code.w};
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int n = 0; n < 8; ++n) v[q * 8 + n] = __ldg(lut + (q * 8 + n) * 16 + ((w[q] >> (n * 4)) & 0xF));
+    }
+    float ip = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 32; ++c) ip = fadd(ip, v[c]);
+    return ip;
 }
 
 // byte offset of (row, k) in a K-major SW128 tile with 128-byte rows
@@ -633,18 +649,28 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
         const int T = rec.ntok;
         const int ld = tid < T ? s.row_doc[k & 1][tid] : -1;
         const float f = tid < T ? s.fac[rs][tid] : 0.0f;
+        // (x * 2^-14 is exact, so the fma rounds exactly as the subtraction
+        // of the product would)
         float da[32];
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-            const float ipa = (float)((int)hi[t] * 256 + (int)lo[t]) * inv_fix;
-            da[t] = __fmul_rn(__fsub_rn(ipa, s.cb1[t]), f);
+        for (int t4 = 0; t4 < 8; ++t4) {
+            const float4 c4 = reinterpret_cast<const float4*>(s.cb1)[t4];
+            const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int t = 4 * t4 + e;
+                const float a = (float)((int)hi[t] * 256 + (int)lo[t]);
+                da[t] = __fmul_rn(__fmaf_rn(a, inv_fix, -cc[e]), f);
+            }
         }
         // ---- pass 1: per (doc, query token) max of the estimates and per doc
         // max |factor|.  For each doc among the warp's rows (docs are runs of
         // rows): a transposing butterfly over the 32 x 32 estimates (other
         // docs' lanes as -inf) leaves lane t with the doc's max for query
-        // token t, then one shared atomic per lane.  The max is only used
-        // for the threshold below, where +0 and -0 give the same value.
+        // token t, then one shared atomic per lane.  (A warp reduction per
+        // query token over the run's lanes measured nine times slower.)  The
+        // max is only used for the threshold below, where +0 and -0 give the
+        // same value.
         {
             const uint32_t grp = __match_any_sync(0xffffffffu, ld);
             for (uint32_t rem = __ballot_sync(0xffffffffu, ld >= 0); rem;) {
@@ -688,8 +714,14 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
         __syncthreads();
         uint32_t cmask = 0;
         if (ld >= 0) {
+            const uint4* th = reinterpret_cast<const uint4*>(s.mx[ld]);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) cmask |= (da[t] >= __uint_as_float(s.mx[ld][t]) ? 1u : 0u) << t;
+            for (int t4 = 0; t4 < 8; ++t4) {
+                const uint4 v = th[t4];
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) cmask |= (da[4 * t4 + e] >= __uint_as_float(w[e]) ? 1u : 0u) << (4 * t4 + e);
+            }
         }
         const int cnt = __popc(cmask);
         int incl = cnt;
@@ -737,7 +769,7 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
                     ip = reduce16_avx512(acc);
                 } else {
                     // refine_1bit_kernel's LUT sum
-                    ip = lut_ip(lut + ((size_t)q * kQ + t) * kLutPerQ, s.raw[k % Sh::kRaw][row]);
+                    ip = lut_ip_ldg(lut + ((size_t)q * kQ + t) * kLutPerQ, s.raw[k % Sh::kRaw][row]);
                 }
                 const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[rs][row]);
                 atomicMax(&s.exact[s.row_doc[k & 1][row]][t], float_key_asc(dist));

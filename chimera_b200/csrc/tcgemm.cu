@@ -15,14 +15,16 @@
 //                  bound E, which proves no excluded centroid can enter.
 //                  Rows that fail (or overflow a buffer) are recomputed
 //                  exactly over all centroids.
-// The assignment keeps the 16 best approximate centroids per row in
-// registers instead of a threshold, with the same certificate.
+// The assignment keeps the 16 best approximate centroids per row and
+// epilogue group in registers instead of a threshold, with the same
+// certificate over the 32 candidates.
 //
 // GEMM kernel: one CTA = 128 query rows x a range of 128-centroid tiles.
 // Warp 0 issues TMA loads (A once, B through a 4-stage ring), warp 1 owns
 // TMEM and issues tcgen05.mma (M=128, N=128, K=16 x 8) into two TMEM
-// accumulators, warps 4-7 drain TMEM with tcgen05.ld.  Every TMA load goes to
-// the issuing CTA alone (no cluster-wide delivery).
+// accumulators, warps 4-7 and 8-11 drain alternate accumulators with
+// tcgen05.ld.  Every TMA load goes to the issuing CTA alone (no cluster-wide
+// delivery).
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
@@ -39,7 +41,7 @@ namespace chm {
 constexpr int kTM = 128, kTN = 128, kK = 128;
 constexpr int kStages = 4;
 // warp 0 TMA, warp 1 MMA, warps 4-7 and 8-11 two epilogue groups that drain
-// alternate accumulators (one group for the top-16 mode)
+// alternate accumulators
 constexpr int kTcThreads = 384;
 constexpr int kBoxBytes = 128 * 64 * 2;             // one 128 x 64 bf16 TMA box
 constexpr int kTileBytes = 2 * kBoxBytes;           // 128 x 128 bf16
@@ -61,7 +63,7 @@ struct TcArgs {
     uint64_t* surv;           // kFilter: [rows][splits][cap]
     int32_t* surv_cnt;        // kFilter: [rows][splits]
     int cap;
-    uint64_t* top;            // kTop16: [rows][splits][16]
+    uint64_t* top;            // kTop16: [rows][splits][2 epilogue groups][16]
     uint32_t* err;
 };
 
@@ -163,11 +165,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
         // all issued MMAs complete before TMEM is released
         sm100::mma_commit(&s.mma_done);
         if (!sm100::mbar_wait(&s.mma_done, 0)) failed = true;
-    } else if (warp >= 4 && (MODE != kTop16 || warp < 8)) {
+    } else if (warp >= 4) {
         // ---- epilogue: TMEM -> registers -> filter / store / top-16 ----
-        // group g drains the tiles it = g, g + ngroups, ...; with two groups
-        // that is accumulator buffer g, so the two run side by side
-        constexpr int ngroups = (MODE == kTop16) ? 1 : 2;
+        // group g drains the tiles it = g, g + 2, ...: accumulator buffer g,
+        // so the two run side by side (top-16: each group keeps its own 16)
+        constexpr int ngroups = 2;
         const int g = (warp - 4) >> 2;
         const int q4 = (warp - 4) & 3;  // TMEM lane quarter: warp % 4
         const int rl = q4 * 32 + lane;  // row within the tile
@@ -293,7 +295,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
         }
         if (MODE == kTop16 && vrow) {
 #pragma unroll
-            for (int j = 0; j < kTopA; ++j) p.top[((size_t)row * p.splits + blockIdx.x) * kTopA + j] = best[j];
+            for (int j = 0; j < kTopA; ++j)
+                p.top[(((size_t)row * p.splits + blockIdx.x) * 2 + g) * kTopA + j] = best[j];
         }
     }
     if (failed) atomicOr(p.err, 1u);
@@ -745,7 +748,7 @@ chm_status chm_tc_probe(const float* rot, int64_t rows, const float* centroids, 
 size_t chm_tc_assign_workspace_bytes(int64_t rows, int64_t nc) {
     chm::Sizer s;
     s.take<__nv_bfloat16>((size_t)rows * chm::kK);
-    s.take<uint64_t>((size_t)rows * chm::kTopA);
+    s.take<uint64_t>((size_t)rows * chm::kTopA * 2);
     s.take<int32_t>((size_t)rows);
     s.take<uint32_t>(4);
     s.take<float>((size_t)chm::kFallbackRows * nc);
@@ -758,7 +761,7 @@ chm_status chm_tc_assign(const float* x128, int64_t rows, const float* centroids
     using namespace chm;
     Arena a(ws, ws_bytes);
     auto* xb = a.take<__nv_bfloat16>((size_t)rows * kK);
-    auto* top = a.take<uint64_t>((size_t)rows * kTopA);
+    auto* top = a.take<uint64_t>((size_t)rows * kTopA * 2);  // [rows][2 epilogue groups][16]
     auto* fl = a.take<int32_t>((size_t)rows);
     auto* cnt = a.take<uint32_t>(4);
     auto* scratch = a.take<float>((size_t)kFallbackRows * nc);
@@ -774,7 +777,7 @@ chm_status chm_tc_assign(const float* x128, int64_t rows, const float* centroids
     t.top = top;
     t.err = cnt + 1;
     CHM_TRY(launch_tc<kTop16>(xb, rows, cent_bf16, nc, 1, t, st));
-    assign_rerank_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x128, rows, centroids, cn, top, 1,
+    assign_rerank_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x128, rows, centroids, cn, top, 2,
                                                                              cnmax, assign, fl, cnt);
     CHM_TRY(launch_status("assign_rerank_kernel"));
     exact_rows_kernel<<<kFallbackRows, 1024, 0, st>>>(x128, centroids, cn, nc, 1, fl, cnt, scratch, assign);

@@ -159,6 +159,149 @@ def generate_torch(cfg: Config, seed: int = 0, device: str = "cuda", chunk: int 
     return emb, doclens, queries.contiguous()
 
 
+class StreamedCorpus:
+    """generate_torch's corpus, produced chunk by chunk for corpora whose
+    embeddings do not fit on one device (C5: about 600M tokens x 512 B).
+
+    A first pass draws everything in generate_torch's order and records the
+    generator state at the start of every embedding chunk; any chunk can then
+    be regenerated with the same values.  The doc lengths, the embeddings
+    (chunk by chunk) and the queries equal generate_torch's with the same
+    seed and chunk size."""
+
+    def __init__(self, cfg: Config, seed: int = 0, device: str = "cuda", chunk: int = 1 << 22):
+        import torch
+        self.cfg, self.chunk, self.device = cfg, chunk, device
+        self._torch = torch
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        kind = cfg.doclen[0]
+        if kind == "normal":
+            _, mu, sd, lo, hi = cfg.doclen
+            x = torch.randn(cfg.num_docs, generator=g, device=device, dtype=torch.float64) * sd + mu
+        else:
+            _, median, sigma, lo, hi = cfg.doclen
+            x = torch.exp(torch.randn(cfg.num_docs, generator=g, device=device,
+                                      dtype=torch.float64) * sigma + math.log(median))
+        self.doclens = torch.clamp(torch.round(x), lo, hi).to(torch.int32)
+        self.n = int(self.doclens.sum().item())
+        self.centres = torch.randn(cfg.components, cfg.dim, generator=g, device=device)
+        # the chunks' draws, recorded and skipped (the values are drawn and dropped
+        # so that the generator advances exactly as generate_torch's does)
+        self.states = []
+        for s in range(0, self.n, chunk):
+            e = min(self.n, s + chunk)
+            self.states.append(g.get_state())
+            torch.randint(0, cfg.components, (e - s,), generator=g, device=device)
+            torch.randn(e - s, cfg.dim, generator=g, device=device)
+        self.ptr = torch.zeros(cfg.num_docs + 1, dtype=torch.int64, device=device)
+        self.ptr[1:] = torch.cumsum(self.doclens.to(torch.int64), 0)
+        targets = torch.randint(0, cfg.num_docs, (cfg.num_queries,), generator=g, device=device)
+        self._take = torch.clamp(self.doclens[targets].to(torch.int64), max=cfg.qlen)
+        j = torch.arange(cfg.qlen, device=device)
+        self._src = self.ptr[targets][:, None] + torch.minimum(j[None, :], self._take[:, None] - 1)
+        shape = (cfg.num_queries, cfg.qlen, cfg.dim)
+        self._noise = torch.randn(shape, generator=g, device=device)
+        self._pad = torch.randn(shape, generator=g, device=device)
+        self._queries = None
+
+    @property
+    def num_chunks(self) -> int:
+        return len(self.states)
+
+    def chunk_at(self, i: int):
+        """Tokens [i * chunk, min(n, (i + 1) * chunk)) as a [m, dim] f32 tensor."""
+        torch = self._torch
+        cfg = self.cfg
+        s = i * self.chunk
+        e = min(self.n, s + self.chunk)
+        g = torch.Generator(device=self.device)
+        g.set_state(self.states[i])
+        comp = torch.randint(0, cfg.components, (e - s,), generator=g, device=self.device)
+        v = self.centres[comp] + cfg.within_sd * torch.randn(e - s, cfg.dim, generator=g, device=self.device)
+        return v / v.norm(dim=1, keepdim=True)
+
+    def chunks(self, lo: int = 0, hi: int | None = None):
+        """Yields (s, e, x): the tokens of [lo, hi) in order, x = rows s..e-1."""
+        hi = self.n if hi is None else hi
+        for i in range(lo // self.chunk, (hi + self.chunk - 1) // self.chunk):
+            s0 = i * self.chunk
+            x = self.chunk_at(i)
+            s, e = max(lo, s0), min(hi, s0 + x.shape[0])
+            if s < e:
+                yield s, e, x[s - s0:e - s0]
+
+    def gather(self, ids):
+        """Rows `ids` (device int64 tensor of token ids) in one pass over the chunks."""
+        torch = self._torch
+        ids = ids.to(self.device)
+        out = torch.empty(ids.shape[0], self.cfg.dim, device=self.device)
+        order = torch.argsort(ids)
+        sid = ids[order]
+        for i in range(self.num_chunks):
+            s0 = i * self.chunk
+            a = int(torch.searchsorted(sid, s0).item())
+            b = int(torch.searchsorted(sid, s0 + self.chunk).item())
+            if a < b:
+                out[order[a:b]] = self.chunk_at(i)[sid[a:b] - s0]
+        return out
+
+    def queries(self):
+        """generate_torch's queries [Q, 32, dim]."""
+        if self._queries is None:
+            torch = self._torch
+            cfg = self.cfg
+            base = self.gather(self._src.reshape(-1)).reshape(cfg.num_queries, cfg.qlen, cfg.dim)
+            noisy = base + cfg.query_noise * self._noise
+            noisy = noisy / noisy.norm(dim=2, keepdim=True)
+            pad = self._pad / self._pad.norm(dim=2, keepdim=True)
+            j = torch.arange(cfg.qlen, device=self.device)
+            self._queries = torch.where((j[None, :] < self._take[:, None])[..., None], noisy, pad).contiguous()
+        return self._queries
+
+
+def ground_truth_streamed(corpus: "StreamedCorpus", queries, k: int, group: int = 32):
+    """Exact fp32 MaxSim top-k of `queries` ([Q, 32, dim] device tensor) over
+    the streamed corpus, one pass over its chunks: per chunk and group of
+    queries the token scores, a per-(query token, doc) max, and per complete
+    doc the sum over query tokens, merged into a running top-k.  A doc that
+    continues into the next chunk carries its partial maxima over."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    Q, L, D = queries.shape
+    ptr = corpus.ptr
+    groups = [list(range(a, min(Q, a + group))) for a in range(0, Q, group)]
+    top_v = [torch.full((len(gq), k), -float("inf"), device=queries.device) for gq in groups]
+    top_i = [torch.zeros((len(gq), k), dtype=torch.int64, device=queries.device) for gq in groups]
+    carry = [None] * len(groups)
+    for s, e, x in corpus.chunks():
+        d0 = int(torch.searchsorted(ptr, s, right=True).item()) - 1
+        d1 = int(torch.searchsorted(ptr, e - 1, right=True).item()) - 1
+        owner = torch.repeat_interleave(torch.arange(d1 - d0 + 1, device=x.device),
+                                        torch.clamp(torch.minimum(ptr[d0 + 1:d1 + 2], torch.tensor(e, device=x.device))
+                                                    - torch.maximum(ptr[d0:d1 + 1], torch.tensor(s, device=x.device)),
+                                                    min=0))
+        last_complete = int(ptr[d1 + 1].item()) == e
+        ndoc = d1 - d0 + 1
+        for gi, gq in enumerate(groups):
+            qg = queries[gq].reshape(-1, D)
+            sc = qg @ x.T                                                  # [G*32, m]
+            best = torch.full((qg.shape[0], ndoc), -float("inf"), device=x.device)
+            best.scatter_reduce_(1, owner.unsqueeze(0).expand(qg.shape[0], -1), sc, reduce="amax")
+            del sc
+            if carry[gi] is not None:
+                best[:, 0] = torch.maximum(best[:, 0], carry[gi])
+            nc = ndoc if last_complete else ndoc - 1
+            carry[gi] = None if last_complete else best[:, ndoc - 1].clone()
+            if nc > 0:
+                score = best[:, :nc].view(len(gq), L, nc).sum(1)
+                v = torch.cat([top_v[gi], score], 1)
+                i = torch.cat([top_i[gi], torch.arange(d0, d0 + nc, device=x.device).expand(len(gq), -1)], 1)
+                tv, ti = torch.topk(v, k, dim=1)
+                top_v[gi], top_i[gi] = tv, torch.gather(i, 1, ti)
+    return [row.cpu().numpy() for gi in range(len(groups)) for row in top_i[gi]]
+
+
 def doc_ptrs(doclens) -> np.ndarray:
     d = np.asarray(doclens, np.int64)
     p = np.zeros(d.shape[0] + 1, np.int64)
