@@ -40,6 +40,116 @@ struct IndexHeader {  // cpp/include/chimera/chimera_index.cuh:75-81
     size_t padded_dimension;
 };
 
+// The rotated centroids inside a cuVS CAGRA file (centroids.carga, written
+// by the reference's IVF_PG::save, ivf_pg.cpp:136-137, over the rotated
+// centroids, build_index.cu:440-446).  cuVS serialises the index's arrays as
+// NumPy .npy blocks (magic "\x93NUMPY", a header dict with 'descr' and
+// 'shape', then the raw data); the dataset block is the little-endian fp32
+// array of shape (n_clusters, d), d <= 128, when the file was written with
+// the dataset included (cuVS's default).  Scans the file's .npy blocks for
+// it; false when there is none.
+bool read_carga_centroids(const std::string& path, size_t n_clusters, std::vector<float>& out) {
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    if (!f) return false;
+    const std::streamoff size = f.tellg();
+    static const char kMagic[6] = {'\x93', 'N', 'U', 'M', 'P', 'Y'};
+    std::vector<char> buf(1 << 20);
+    std::streamoff pos = 0;
+    while (pos + 10 <= size) {
+        // next magic at or after pos
+        f.seekg(pos);
+        const std::streamoff want = std::min<std::streamoff>((std::streamoff)buf.size(), size - pos);
+        f.read(buf.data(), want);
+        if (!f) return false;
+        std::streamoff hit = -1;
+        for (std::streamoff i = 0; i + 6 <= want; ++i)
+            if (std::memcmp(buf.data() + i, kMagic, 6) == 0) {
+                hit = pos + i;
+                break;
+            }
+        if (hit < 0) {
+            if (pos + want >= size) return false;
+            pos += want - 5;  // a magic may straddle the block boundary
+            continue;
+        }
+        // preamble: magic, major, minor, header length (2 bytes in 1.x, 4 after)
+        unsigned char pre[12] = {0};
+        f.seekg(hit);
+        f.read(reinterpret_cast<char*>(pre), 12);
+        if (!f) return false;
+        const int major = pre[6];
+        size_t hlen = 0, off = 0;
+        if (major == 1) {
+            hlen = pre[8] | (size_t(pre[9]) << 8);
+            off = 10;
+        } else {
+            hlen = pre[8] | (size_t(pre[9]) << 8) | (size_t(pre[10]) << 16) | (size_t(pre[11]) << 24);
+            off = 12;
+        }
+        if (hlen > (1 << 16)) {  // not a real header: keep scanning
+            pos = hit + 1;
+            continue;
+        }
+        std::string hdr(hlen, '\0');
+        f.seekg(hit + (std::streamoff)off);
+        f.read(&hdr[0], (std::streamsize)hlen);
+        if (!f) return false;
+        const std::streamoff data = hit + (std::streamoff)(off + hlen);
+        auto field = [&](const char* key) {
+            const size_t k = hdr.find(key);
+            return k == std::string::npos ? std::string() : hdr.substr(k + std::strlen(key));
+        };
+        std::string descr = field("'descr':");
+        descr = descr.substr(0, descr.find(','));
+        std::string shape = field("'shape':");
+        const size_t lp = shape.find('('), rp = shape.find(')');
+        std::vector<size_t> dims;
+        if (lp != std::string::npos && rp != std::string::npos && rp > lp) {
+            std::string inner = shape.substr(lp + 1, rp - lp - 1);
+            size_t i = 0;
+            while (i < inner.size()) {
+                while (i < inner.size() && (inner[i] < '0' || inner[i] > '9')) ++i;
+                size_t v = 0;
+                bool any = false;
+                while (i < inner.size() && inner[i] >= '0' && inner[i] <= '9') {
+                    v = v * 10 + size_t(inner[i++] - '0');
+                    any = true;
+                }
+                if (any) dims.push_back(v);
+            }
+        }
+        size_t item = 0;
+        if (descr.find("f4") != std::string::npos || descr.find("i4") != std::string::npos ||
+            descr.find("u4") != std::string::npos)
+            item = 4;
+        else if (descr.find("8") != std::string::npos)
+            item = 8;
+        else if (descr.find("2") != std::string::npos)
+            item = 2;
+        else if (descr.find("1") != std::string::npos)
+            item = 1;
+        size_t count = dims.empty() ? 0 : 1;
+        for (size_t d : dims) count *= d;
+        const std::string fo = field("'fortran_order':");
+        const size_t fo0 = fo.find_first_not_of(' ');
+        const bool fortran = fo0 != std::string::npos && fo.compare(fo0, 4, "True") == 0;
+        if (dims.size() == 2 && dims[0] == n_clusters && dims[1] >= 1 && dims[1] <= kPadded && !fortran &&
+            descr.find("<f4") != std::string::npos && data + (std::streamoff)(count * 4) <= size) {
+            std::vector<float> raw(count);
+            f.seekg(data);
+            f.read(reinterpret_cast<char*>(raw.data()), (std::streamsize)(count * 4));
+            if (!f) return false;
+            out.assign(n_clusters * kPadded, 0.0f);
+            for (size_t c = 0; c < n_clusters; ++c)
+                std::memcpy(&out[c * kPadded], &raw[c * dims[1]], dims[1] * 4);
+            return true;
+        }
+        // another array (the graph): skip its data when its size is known
+        pos = (item && count) ? data + (std::streamoff)(item * count) : hit + 1;
+    }
+    return false;
+}
+
 void throw_status(chm_status s, const char* what) {
     if (s == CHM_OK) return;
     if (s == CHM_ERR_INVALID) throw std::invalid_argument(std::string(what) + ": invalid argument");
@@ -636,15 +746,21 @@ void chimera_index::load(const std::string& index_dir, const SearchOptions& opti
             std::ifstream f(p, std::ios::binary);
             int64_t hdr[2] = {0, 0};
             f.read(reinterpret_cast<char*>(hdr), sizeof(hdr));
-            if (!f)
-                throw std::runtime_error("Missing " + p + " (the rotated centroids; an index written by the cuVS "
-                                         "build keeps them only inside centroids.carga)");
-            if (hdr[0] != static_cast<int64_t>(m.n_clusters) || hdr[1] != static_cast<int64_t>(kPadded))
-                throw std::runtime_error("Invalid centroid payload: " + p);
-            m.centroids_rot.resize(m.n_clusters * kPadded);
-            f.read(reinterpret_cast<char*>(m.centroids_rot.data()),
-                   static_cast<std::streamsize>(m.centroids_rot.size() * 4));
-            if (!f) throw std::runtime_error("Invalid centroid payload: " + p);
+            if (!f) {
+                // an index written by the reference: the rotated centroids are the
+                // dataset inside its cuVS CAGRA file
+                const auto pc = (dir / "centroids.carga").string();
+                if (!read_carga_centroids(pc, m.n_clusters, m.centroids_rot))
+                    throw std::runtime_error("Missing " + p + ", and " + pc +
+                                             " holds no (n_clusters, dim) fp32 dataset block");
+            } else {
+                if (hdr[0] != static_cast<int64_t>(m.n_clusters) || hdr[1] != static_cast<int64_t>(kPadded))
+                    throw std::runtime_error("Invalid centroid payload: " + p);
+                m.centroids_rot.resize(m.n_clusters * kPadded);
+                f.read(reinterpret_cast<char*>(m.centroids_rot.data()),
+                       static_cast<std::streamsize>(m.centroids_rot.size() * 4));
+                if (!f) throw std::runtime_error("Invalid centroid payload: " + p);
+            }
         }
         {
             const auto p = (dir / "doclens.bin").string();

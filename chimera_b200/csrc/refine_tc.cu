@@ -87,6 +87,7 @@ struct __align__(1024) RtSmem {
     uint32_t exact[kRtMaxDocs][32];  // exact max per (doc, query token), ordered keys
     uint32_t cand[kRtMaxCand];       // (row << 5 | t)
     int n_cand;
+    int cand_base;                   // 1-bit: this item's first slot in the query's candidate list
     float em[32];                    // margin per unit |factor|
     alignas(16) float cb1[32];
     uint64_t bar;
@@ -114,22 +115,6 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
-}
-
-// lut_ip with the LUT in global memory (L2-resident): the 32 entries are
-// loaded first, all in flight at once, then added in the reference order.
-__device__ __forceinline__ float lut_ip_ldg(const float* __restrict__ lut, uint4 code) {
-    const uint32_t w[4] = {code.x, code.y, code.z, code.w};
-    float v[32];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-#pragma unroll
-        for (int n = 0; n < 8; ++n) v[q * 8 + n] = __ldg(lut + (q * 8 + n) * 16 + ((w[q] >> (n * 4)) & 0xF));
-    }
-    float ip = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 32; ++c) ip = fadd(ip, v[c]);
-    return ip;
 }
 
 // byte offset of (row, k) in a K-major SW128 tile with 128-byte rows
@@ -539,10 +524,20 @@ __global__ void __launch_bounds__(256) rt_query_kernel(const float* __restrict__
     }
 }
 
+// 1-bit candidates handed to rt_exact1_kernel: per query, the packed code,
+// factor and (refined index, query token) of every candidate row.
+struct RtCandOut {
+    uint4* code;     // [nq][ccap]
+    uint2* meta;     // [nq][ccap]: factor bits, refined index << 5 | query token
+    int32_t* count;  // [nq] (may run past ccap: the query is then flagged)
+    int ccap;
+};
+
 // kFull: the full-bit MaxSim of fullbit_kernel (codes at width w, cb = cbex,
 // the AVX-512 lane order for the exact sums, its 16-lane document reduction);
-// else the 1-bit score of refine_1bit_kernel (cb = cb1, exact sums from the
-// query's LUTs).
+// else the 1-bit score of refine_1bit_kernel (cb = cb1): the candidates go
+// to rt_exact1_kernel, which has the query's LUTs in shared memory, and
+// rt_tree1_kernel makes the scores.
 //
 // Item k (the CTA's k-th) goes through: loads issued (iteration k-2), tile
 // expanded and multiplied (iteration k-1), accumulators reduced (iteration k).
@@ -552,7 +547,7 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
     const float* __restrict__ factors, const float* __restrict__ cb1, const float* __restrict__ rot,
     const float* __restrict__ lut, const uint8_t* __restrict__ qtile, const float* __restrict__ qem, int cap,
     const int32_t* __restrict__ n_items, float* __restrict__ scores, uint32_t* __restrict__ status,
-    unsigned long long* __restrict__ stats) {
+    unsigned long long* __restrict__ stats, RtCandOut co) {
     using Sh = RtShape<kFull, kW>;
     extern __shared__ uint8_t smem_raw[];
     RtSmem<kFull, kW>& s =
@@ -737,9 +732,26 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
             for (uint32_t mm = cmask; mm; mm &= mm - 1) s.cand[at++] = ((uint32_t)tid << 5) | (uint32_t)(__ffs(mm) - 1);
         __syncthreads();
         const int nc = s.n_cand;
-        // ---- exact sums of the candidates, spread over the four warps
+        // ---- exact sums of the candidates: full-bit here, spread over the
+        // four warps; 1-bit candidates are written out for rt_exact1_kernel
         if (nc > kRtMaxCand) {
             if (tid == 0) atomicOr(status + q, 1u);  // rescored by the SIMT kernel
+        } else if (!kFull) {
+            if (tid == 0) s.cand_base = nc > 0 ? atomicAdd(co.count + q, nc) : 0;
+            __syncthreads();
+            const int base = s.cand_base;
+            if (base + nc > co.ccap) {
+                if (tid == 0) atomicOr(status + q, 1u);  // list full: rescored by the SIMT kernel
+            } else {
+                for (int c = tid; c < nc; c += kRtThreads) {
+                    const uint32_t e = s.cand[c];
+                    const int row = (int)(e >> 5);
+                    const size_t at = (size_t)q * co.ccap + base + c;
+                    co.code[at] = s.raw[k % Sh::kRaw][row];
+                    co.meta[at] = make_uint2(__float_as_uint(s.fac[rs][row]),
+                                             ((uint32_t)(rec.r0 + s.row_doc[k & 1][row]) << 5) | (e & 31u));
+                }
+            }
         } else {
             for (int c = lane * (kRtThreads / 32) + warp; c < nc; c += kRtThreads) {
                 const uint32_t e = s.cand[c];
@@ -767,9 +779,6 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
                         }
                     }
                     ip = reduce16_avx512(acc);
-                } else {
-                    // refine_1bit_kernel's LUT sum
-                    ip = lut_ip_ldg(lut + ((size_t)q * kQ + t) * kLutPerQ, s.raw[k % Sh::kRaw][row]);
                 }
                 const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[rs][row]);
                 atomicMax(&s.exact[s.row_doc[k & 1][row]][t], float_key_asc(dist));
@@ -778,22 +787,18 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
         n_cand += (unsigned long long)(tid == 0 ? nc : 0);
         __syncthreads();
         // ---- document scores: the reference's 128-thread tree (kernels.cu:557-570)
+        // (1-bit: rt_tree1_kernel makes the scores once every candidate's exact sum is in)
         for (int j = warp; j < nd; j += kRtThreads / 32) {
-            const float m = key_to_float_asc(s.exact[j][lane]);
-            float x;
             if (kFull) {
                 // fullbit_kernel: max[0:16] + max[16:32] lane-wise, then the 16-lane tree
-                x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
+                const float m = key_to_float_asc(s.exact[j][lane]);
+                float x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
 #pragma unroll
                 for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
-            } else {
-                x = fadd(fadd(fadd(0.0f, m), 0.0f), 0.0f);
-#pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+                if (lane == 0) scores[(size_t)q * cap + rec.r0 + j] = ((rec.foreign >> j) & 1u) ? -INFINITY : x;
+                s.exact[j][lane] = float_key_asc(-INFINITY);
             }
-            if (lane == 0) scores[(size_t)q * cap + rec.r0 + j] = ((rec.foreign >> j) & 1u) ? -INFINITY : x;
             s.mx[j][lane] = 0u;
-            s.exact[j][lane] = float_key_asc(kFull ? -INFINITY : -FLT_MAX);
             if (lane == 0) s.maxf[j] = 0u;
         }
         if (tid == 0) {
@@ -818,6 +823,66 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
     __syncthreads();
     sm100::tc_fence_after();
     if (warp == 0) sm100::tmem_dealloc(tmem, kRtTmemCols);
+}
+
+// Exact 1-bit sums of the candidates the tensor-core kernel wrote out
+// (refine_1bit_kernel's LUT sum, kernels.cu:363-375): the query's 32 LUTs in
+// shared memory, rows 513 floats apart so that lanes on different query
+// tokens spread over the banks, one candidate per thread, the max per
+// (refined doc, query token) by atomicMax on ordered keys.  Flagged queries
+// are skipped: the SIMT kernel rescores them.
+constexpr int kRxThreads = 256;
+constexpr int kRxStride = kLutPerQ + 1;
+size_t rt_exact1_smem() { return sizeof(float) * (size_t)kQ * kRxStride; }
+
+__global__ void __launch_bounds__(kRxThreads) rt_exact1_kernel(RtCandOut co, const float* __restrict__ lut,
+                                                                const float* __restrict__ cb1,
+                                                                const uint32_t* __restrict__ status, int cap,
+                                                                uint32_t* __restrict__ exact) {
+    extern __shared__ float s_lut[];
+    __shared__ float s_cb[kQ];
+    const int q = blockIdx.y;
+    if (status[q]) return;
+    const int n = min(co.count[q], co.ccap);
+    if ((int)blockIdx.x * kRxThreads >= n) return;
+    const float* src = lut + (size_t)q * kQ * kLutPerQ;
+    for (int i = threadIdx.x; i < kQ * kLutPerQ; i += kRxThreads)
+        s_lut[(i / kLutPerQ) * kRxStride + (i % kLutPerQ)] = __ldg(src + i);
+    if (threadIdx.x < kQ) s_cb[threadIdx.x] = cb1[q * kQ + threadIdx.x];
+    __syncthreads();
+    const uint4* code = co.code + (size_t)q * co.ccap;
+    const uint2* meta = co.meta + (size_t)q * co.ccap;
+    for (int i = blockIdx.x * kRxThreads + threadIdx.x; i < n; i += gridDim.x * kRxThreads) {
+        const uint4 c = code[i];
+        const uint2 m = meta[i];
+        const int t = (int)(m.y & 31u);
+        const float ip = lut_ip(s_lut + t * kRxStride, c);
+        const float dist = fmul(fsub(ip, s_cb[t]), __uint_as_float(m.x));
+        atomicMax(exact + ((size_t)q * cap + (m.y >> 5)) * kQ + t, float_key_asc(dist));
+    }
+}
+
+// 1-bit document scores from the exact maxima: the reference's 128-thread
+// tree (kernels.cu:557-570: strides 64 and 32 add zeros, then 16..1), one
+// warp per refined doc.  Docs without maxima (longer than one tile: the SIMT
+// kernel scores them) are left alone; other shards' docs (-1) score -inf.
+__global__ void rt_tree1_kernel(const uint32_t* __restrict__ exact, const int32_t* __restrict__ docs,
+                                const int32_t* __restrict__ counts, int cap, float* __restrict__ scores) {
+    const int q = blockIdx.y, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= counts[q]) return;
+    const size_t at = (size_t)q * cap + r;
+    if (docs[at] < 0) {
+        if (lane == 0) scores[at] = -INFINITY;
+        return;
+    }
+    const uint32_t key = exact[at * kQ + lane];
+    if (__shfl_sync(0xffffffffu, key, 0) == 0u) return;
+    const float m = key_to_float_asc(key);
+    float x = fadd(fadd(fadd(0.0f, m), 0.0f), 0.0f);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+    if (lane == 0) scores[at] = x;
 }
 
 // Queries whose tensor-core launch gave up on a bounded wait are scored
@@ -846,7 +911,13 @@ struct RtWork {
     uint32_t* rows;
     uint8_t* qtile;  // per query: the B tile (rt_query_kernel)
     float* qem;      // per query token: the margin
+    RtCandOut cand;  // 1-bit: the candidates of each query
+    uint32_t* exact; // 1-bit: [nq][cap][32] exact max per (refined doc, query token), ordered keys
 };
+
+// 1-bit candidate slots per refined doc: every (doc, query token) has at
+// least one, and about 1.03 on average (more: the query is flagged).
+constexpr int kRtCandPerDoc = 40;
 
 template <typename A>
 static void rt_layout(A& a, int nq, int cap, RtWork* w) {
@@ -860,8 +931,15 @@ static void rt_layout(A& a, int nq, int cap, RtWork* w) {
     auto rows = a.template take<uint32_t>((size_t)nq * cap * kRtRows);
     auto qtile = a.template take<uint8_t>((size_t)nq * kRtN * 128);
     auto qem = a.template take<float>((size_t)nq * kQ);
-    if (w) *w = RtWork{(int2*)items, (int32_t*)n_items, (uint32_t*)status, (unsigned long long*)stats,
-                       (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint32_t*)rows, (uint8_t*)qtile, (float*)qem};
+    const int ccap = kRtCandPerDoc * cap;
+    auto ccode = a.template take<uint4>((size_t)nq * ccap);
+    auto cmeta = a.template take<uint2>((size_t)nq * ccap);
+    auto ccount = a.template take<int32_t>((size_t)nq);
+    auto exact = a.template take<uint32_t>((size_t)nq * cap * kQ);
+    if (w)
+        *w = RtWork{(int2*)items, (int32_t*)n_items, (uint32_t*)status, (unsigned long long*)stats,
+                    (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint32_t*)rows, (uint8_t*)qtile, (float*)qem,
+                    RtCandOut{(uint4*)ccode, (uint2*)cmeta, (int32_t*)ccount, ccap}, (uint32_t*)exact};
 }
 
 struct RtSizer {
@@ -930,7 +1008,7 @@ static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* r
     CHM_TRY(rt_grid(refine_tc_kernel<true, kW>, smem, nq, fb_cap, &grid));
     refine_tc_kernel<true, kW><<<grid, kRtThreads, smem, st>>>(w.meta, w.rows, idx->full_codes, idx->full_factors,
                                                                cbex, rot, nullptr, w.qtile, w.qem, fb_cap, w.n_items,
-                                                               scores, w.status, w.stats);
+                                                               scores, w.status, w.stats, w.cand);
     return launch_status("fullbit_tc_kernel");
 }
 
@@ -992,10 +1070,22 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
                                   (int)smem));
     dim3 grid;
     CHM_TRY(chm::rt_grid(chm::refine_tc_kernel<false, 1>, smem, nq, k_refine, &grid));
+    CHM_CUDA(cudaMemsetAsync(w.cand.count, 0, sizeof(int32_t) * nq, st));
+    CHM_CUDA(cudaMemsetAsync(w.exact, 0, sizeof(uint32_t) * (size_t)nq * k_refine * chm::kQ, st));
     chm::refine_tc_kernel<false, 1><<<grid, chm::kRtThreads, smem, st>>>(
         w.meta, w.rows, codes, factors, cb1, rot, lut, w.qtile, w.qem, k_refine, w.n_items, scores, w.status,
-        w.stats);
+        w.stats, w.cand);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
+    // exact sums: about four resident waves of 3 CTAs per SM over the batch
+    const size_t xsmem = chm::rt_exact1_smem();
+    CHM_CUDA(cudaFuncSetAttribute(chm::rt_exact1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsmem));
+    const int xg = std::max(1, std::min(64, (148 * 3 * 4 + nq - 1) / nq));
+    chm::rt_exact1_kernel<<<dim3((unsigned)xg, (unsigned)nq), chm::kRxThreads, xsmem, st>>>(w.cand, lut, cb1, w.status,
+                                                                                          k_refine, w.exact);
+    CHM_TRY(chm::launch_status("rt_exact1_kernel"));
+    chm::rt_tree1_kernel<<<dim3((unsigned)((k_refine + 7) / 8), (unsigned)nq), 256, 0, st>>>(
+        w.exact, refined_docs, num_refined, k_refine, scores);
+    CHM_TRY(chm::launch_status("rt_tree1_kernel"));
     return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, w.big, w.n_big,
                                     w.status, st);
 }

@@ -10,13 +10,23 @@
 // with fp32 rounding (any summation order for S, the 5-level tree for P)
 //     P_fp32 <= S_fp32 * (1 + eps),  eps = (32 * max_doc_len + 8) * 2^-24 * 1.25
 // because a token sits in one cluster, so a doc has at most 32 * doclen
-// positive visits.
+// positive visits.  The score pass sums upper bounds of the dists instead of
+// the dists: the 8-bit LUT entry for byte b is the sum of the reference's two
+// 4-bit entries (chunks 2b, 2b + 1), and both ip sums are sums of the same
+// <= 128 query components along trees of height <= 35 (reference) and <= 12
+// (here), so |ip' - ip| <= 47 u sum|q| (u = 2^-24); the subtraction of cb1,
+// the product with the factor and the final fma add <= 6 u (sum|q| + |cb1|)
+// per unit |factor| for both paths together.  m = |factor| * M_t with
+// M_t = 2^-24 (100 sum|q| + 16 |cb1|) covers all of it with room.
 //
 //  score   : CTA per (query token t, split, query); each warp streams whole
-//            probed lists (no per-visit search), 1-bit LUT sums in the
-//            reference order, and posts dist > 0 into S[q][doc] with a
-//            fire-and-forget float reduction (runs of one doc inside a warp
-//            are summed first: the lists are in doc order).
+//            probed lists (no per-visit search), scores each code with an
+//            8-bit LUT (16 lookups instead of the reference's 32) and posts
+//            dist' + m > 0 into S[q][doc] with a fire-and-forget float
+//            reduction (runs of one doc inside a warp are summed first: the
+//            lists are in doc order).  m bounds |dist' - dist| (below), so
+//            every term is at least the reference's dist and S stays an
+//            upper bound.
 //  hist / pivot / compact : per query, the 12-bit bucket that holds the
 //            K'-th largest S (K' = k_refine + slack) and the keys
 //            (S << 32 | ~doc) at or above it.
@@ -106,8 +116,26 @@ __device__ __forceinline__ void post_dist(float* S, int doc, float d, bool valid
     }
 }
 
+// 8-bit LUT sum of a 1-bit code: byte b of the code indexes entry b of
+// `lut8` ([16][256], shared memory); two interleaved chains of 8 adds.
+__device__ __forceinline__ float lut8_ip(const float* lut8, uint4 code) {
+    const uint32_t w[4] = {code.x, code.y, code.z, code.w};
+    float a = 0.0f, b = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float v = lut8[(q * 4 + i) * 256 + __byte_perm(w[q], 0, 0x4440 + i)];
+            if (q < 2) a = fadd(a, v); else b = fadd(b, v);
+        }
+    }
+    return fadd(a, b);
+}
+
 __global__ void __launch_bounds__(kBsWarps * 32) bound_score_kernel(BoundCtx c, int splits) {
     __shared__ float s_lut[kLutPerQ];
+    __shared__ float s_lut8[16 * 256];
+    __shared__ float s_mt;
     __shared__ int s_next;
     const int t = blockIdx.x / splits, split = blockIdx.x % splits;
     const int q = blockIdx.y;
@@ -117,6 +145,22 @@ __global__ void __launch_bounds__(kBsWarps * 32) bound_score_kernel(BoundCtx c, 
     if (threadIdx.x == 0) s_next = kBsWarps;
     __syncthreads();
     const float cb1 = c.cb1[q * kQ + t];
+    // byte b's entries: chunk 2b is its low nibble, chunk 2b + 1 its high one
+    for (int i = threadIdx.x; i < 16 * 256; i += blockDim.x) {
+        const int b = i >> 8, e = i & 255;
+        s_lut8[i] = fadd(s_lut[(2 * b) * 16 + (e & 15)], s_lut[(2 * b + 1) * 16 + (e >> 4)]);
+    }
+    if (warp == 0) {
+        // sum |q_d|: the single-bit entries are the components themselves
+        float a = 0.0f;
+#pragma unroll
+        for (int bit = 0; bit < 4; ++bit) a += fabsf(s_lut[lane * 16 + (1 << bit)]);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+        if (lane == 0) s_mt = (100.0f * a + 16.0f * fabsf(cb1)) * 0x1p-24f;
+    }
+    __syncthreads();
+    const float mt = s_mt;
     const uint32_t* labels = c.labels + ((size_t)q * kQ + t) * c.nprobe;
     float* S = c.S + (size_t)q * c.num_docs;
     // warps take this split's lists (p = split + k * splits) in turn
@@ -139,10 +183,11 @@ __global__ void __launch_bounds__(kBsWarps * 32) bound_score_kernel(BoundCtx c, 
                 int d0 = -1, d1 = -1;
                 if (v0) { k0 = __ldg(codes + e0); f0 = __ldg(fac + e0); d0 = __ldg(docs + e0); }
                 if (v1) { k1 = __ldg(codes + e1); f1 = __ldg(fac + e1); d1 = __ldg(docs + e1); }
-                const float dist0 = fmul(fsub(lut_ip_prmt(s_lut, k0), cb1), f0);
+                // dist' + |f| M_t >= the reference's dist
+                const float dist0 = __fmaf_ru(fabsf(f0), mt, fmul(fsub(lut8_ip(s_lut8, k0), cb1), f0));
                 post_dist(S, d0, dist0, v0 && d0 >= 0 && (int64_t)d0 < c.num_docs, lane);
                 if (b + 32 < len) {
-                    const float dist1 = fmul(fsub(lut_ip_prmt(s_lut, k1), cb1), f1);
+                    const float dist1 = __fmaf_ru(fabsf(f1), mt, fmul(fsub(lut8_ip(s_lut8, k1), cb1), f1));
                     post_dist(S, d1, dist1, v1 && d1 >= 0 && (int64_t)d1 < c.num_docs, lane);
                 }
             }

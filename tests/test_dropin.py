@@ -157,3 +157,44 @@ def test_saved_files_are_the_reference_layout_byte_for_byte(tmp_path):
         got = open(tmp_path / "ix" / name, "rb").read()
         assert len(got) == len(want), name
         assert got == want, name
+
+
+def _write_carga_like(path, centroids, degree=8, seed=0):
+    """A file laid out as cuVS serialises a CAGRA index with its dataset: a
+    few scalars, the graph as a .npy block (uint32, (n, degree)), a bool,
+    then the dataset as a .npy block (fp32, (n, dim))."""
+    rng = np.random.default_rng(seed)
+    n = centroids.shape[0]
+    with open(path, "wb") as f:
+        f.write(b"<f4\x00")                                   # dtype string
+        f.write(struct.pack("<iqqqi", 4, n, centroids.shape[1], degree, 0))
+        np.lib.format.write_array(f, rng.integers(0, n, (n, degree), dtype=np.uint32))
+        f.write(b"\x01")                                      # dataset included
+        np.lib.format.write_array(f, np.ascontiguousarray(centroids, np.float32))
+
+
+@pytest.mark.gpu
+def test_load_reference_index_with_carga_centroids(tmp_path):
+    """An index directory as the reference writes it (centroids.carga, no
+    centroids.f32) loads: the rotated centroids come from the CAGRA file's
+    dataset block, and the searches equal those of the original index."""
+    chimera = _chimera()
+    c = _corpus.corpus("mini")
+    cfg = c["cfg"]
+    kw = dict(nprobe=cfg.nprobe, k_refine=cfg.k_refine, k_full_bit=cfg.k_full_bit, num_chunks=cfg.num_chunks)
+    idx = chimera.ChimeraIndex.build(np.ascontiguousarray(c["emb"]), [int(x) for x in c["doclens"]],
+                                     cfg.n_clusters, cfg.ex_bits, **kw)
+    want = idx.search(np.ascontiguousarray(c["queries"]), k=cfg.k)
+    ix = tmp_path / "ix"
+    idx.save(str(ix))
+    raw = open(ix / "centroids.f32", "rb").read()
+    nc, d = struct.unpack("<qq", raw[:16])
+    cents = np.frombuffer(raw[16:], np.float32).reshape(nc, d)
+    os.remove(ix / "centroids.f32")
+    _write_carga_like(ix / "centroids.carga", cents)
+    got = chimera.ChimeraIndex.load(str(ix), **kw).search(np.ascontiguousarray(c["queries"]), k=cfg.k)
+    assert got == want
+    # no dataset block of the right shape: a clear error
+    _write_carga_like(ix / "centroids.carga", cents[:, :64][: nc - 1])
+    with pytest.raises(RuntimeError):
+        chimera.ChimeraIndex.load(str(ix), **kw)
