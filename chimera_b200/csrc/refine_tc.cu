@@ -82,9 +82,9 @@ struct __align__(1024) RtSmem {
     float fac[3][kRtRows];
     int row_doc[2][kRtRows];         // item-local doc of each row (-1: past the item's tokens)
     alignas(16) int rec[3][kRtRecWords];
+    uint32_t ridx[3][kRtRows];       // each row's code index (record slot), for the candidate hand-off
     alignas(16) uint32_t mx[kRtMaxDocs][32];  // max estimate per (doc, query token) as an ordered key, then the threshold
     uint32_t maxf[kRtMaxDocs];       // max |factor| per doc (float bits, >= 0)
-    uint32_t exact[kRtMaxDocs][32];  // exact max per (doc, query token), ordered keys
     uint32_t cand[kRtMaxCand];       // (row << 5 | t)
     int n_cand;
     int cand_base;                   // 1-bit: this item's first slot in the query's candidate list
@@ -378,6 +378,7 @@ __device__ __forceinline__ void rt_issue(RtSmem<kFull, kW>& s, int rs, int cs, c
     constexpr int kC = RtShape<kFull, kW>::kRowChunks;
     const int tid = threadIdx.x;
     if (tid < kRtRecWords / 4) cp_async16(&s.rec[rs][4 * tid], reinterpret_cast<const uint4*>(rec) + tid);
+    s.ridx[rs][tid] = idx;
     if (idx != kRtNoRow) {
         const uint4* src = reinterpret_cast<const uint4*>(codes) + (size_t)idx * kC;
 #pragma unroll
@@ -524,20 +525,19 @@ __global__ void __launch_bounds__(256) rt_query_kernel(const float* __restrict__
     }
 }
 
-// 1-bit candidates handed to rt_exact1_kernel: per query, the packed code,
-// factor and (refined index, query token) of every candidate row.
+// Candidates handed to the exact pass (rt_exact_kernel): per query, every
+// candidate row's code index and (refined index, query token).
 struct RtCandOut {
-    uint4* code;     // [nq][ccap]
-    uint2* meta;     // [nq][ccap]: factor bits, refined index << 5 | query token
+    uint2* ent;      // [nq][ccap]: code index, refined index << 5 | query token
     int32_t* count;  // [nq] (may run past ccap: the query is then flagged)
     int ccap;
 };
 
 // kFull: the full-bit MaxSim of fullbit_kernel (codes at width w, cb = cbex,
 // the AVX-512 lane order for the exact sums, its 16-lane document reduction);
-// else the 1-bit score of refine_1bit_kernel (cb = cb1): the candidates go
-// to rt_exact1_kernel, which has the query's LUTs in shared memory, and
-// rt_tree1_kernel makes the scores.
+// else the 1-bit score of refine_1bit_kernel (cb = cb1).  The candidates go
+// to rt_exact_kernel, which holds the query's LUTs (1-bit) or rotated query
+// (full-bit) in shared memory, and rt_tree_kernel makes the scores.
 //
 // Item k (the CTA's k-th) goes through: loads issued (iteration k-2), tile
 // expanded and multiplied (iteration k-1), accumulators reduced (iteration k).
@@ -565,10 +565,7 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
             s.cb1[tid] = cb1[q * kQ + tid];
             s.em[tid] = qem[q * kQ + tid];
         }
-        for (int i = tid; i < kRtMaxDocs * 32; i += kRtThreads) {
-            (&s.mx[0][0])[i] = 0u;
-            (&s.exact[0][0])[i] = float_key_asc(kFull ? -INFINITY : -FLT_MAX);
-        }
+        for (int i = tid; i < kRtMaxDocs * 32; i += kRtThreads) (&s.mx[0][0])[i] = 0u;
         if (tid < kRtMaxDocs) s.maxf[tid] = 0u;
         if (tid == 0) {
             s.n_cand = 0;
@@ -732,11 +729,10 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
             for (uint32_t mm = cmask; mm; mm &= mm - 1) s.cand[at++] = ((uint32_t)tid << 5) | (uint32_t)(__ffs(mm) - 1);
         __syncthreads();
         const int nc = s.n_cand;
-        // ---- exact sums of the candidates: full-bit here, spread over the
-        // four warps; 1-bit candidates are written out for rt_exact1_kernel
+        // ---- the candidates go to the exact pass
         if (nc > kRtMaxCand) {
             if (tid == 0) atomicOr(status + q, 1u);  // rescored by the SIMT kernel
-        } else if (!kFull) {
+        } else {
             if (tid == 0) s.cand_base = nc > 0 ? atomicAdd(co.count + q, nc) : 0;
             __syncthreads();
             const int base = s.cand_base;
@@ -746,58 +742,16 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
                 for (int c = tid; c < nc; c += kRtThreads) {
                     const uint32_t e = s.cand[c];
                     const int row = (int)(e >> 5);
-                    const size_t at = (size_t)q * co.ccap + base + c;
-                    co.code[at] = s.raw[k % Sh::kRaw][row];
-                    co.meta[at] = make_uint2(__float_as_uint(s.fac[rs][row]),
-                                             ((uint32_t)(rec.r0 + s.row_doc[k & 1][row]) << 5) | (e & 31u));
+                    co.ent[(size_t)q * co.ccap + base + c] =
+                        make_uint2(s.ridx[rs][row], ((uint32_t)(rec.r0 + s.row_doc[k & 1][row]) << 5) | (e & 31u));
                 }
-            }
-        } else {
-            for (int c = lane * (kRtThreads / 32) + warp; c < nc; c += kRtThreads) {
-                const uint32_t e = s.cand[c];
-                const int row = (int)(e >> 5), t = (int)(e & 31);
-                float ip;
-                if (kFull) {
-                    // fullbit_kernel's arithmetic: 16 lane chains over b = 0..7, reduce16
-                    // (the query row: L1-resident, one query's 16 KB; 16-byte aligned)
-                    const float4* qt = reinterpret_cast<const float4*>(rot + ((size_t)q * kQ + t) * kDim);
-                    const uint8_t* a = s.a[k % Sh::kA];
-                    float acc[16];
-#pragma unroll
-                    for (int l = 0; l < 16; ++l) acc[l] = 0.0f;
-#pragma unroll
-                    for (int b = 0; b < 8; ++b) {
-                        const uint4 raw = *reinterpret_cast<const uint4*>(a + sw128_off(row, b));
-                        const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-                        for (int l4 = 0; l4 < 4; ++l4) {
-                            const float4 qv = __ldg(qt + 4 * b + l4);
-                            const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                acc[4 * l4 + e] = __fmaf_rn((float)((rw[l4] >> (8 * e)) & 0xFFu), qq[e], acc[4 * l4 + e]);
-                        }
-                    }
-                    ip = reduce16_avx512(acc);
-                }
-                const float dist = fmul(fsub(ip, s.cb1[t]), s.fac[rs][row]);
-                atomicMax(&s.exact[s.row_doc[k & 1][row]][t], float_key_asc(dist));
             }
         }
         n_cand += (unsigned long long)(tid == 0 ? nc : 0);
         __syncthreads();
         // ---- document scores: the reference's 128-thread tree (kernels.cu:557-570)
-        // (1-bit: rt_tree1_kernel makes the scores once every candidate's exact sum is in)
+        // (rt_tree_kernel makes the scores once every candidate's exact sum is in)
         for (int j = warp; j < nd; j += kRtThreads / 32) {
-            if (kFull) {
-                // fullbit_kernel: max[0:16] + max[16:32] lane-wise, then the 16-lane tree
-                const float m = key_to_float_asc(s.exact[j][lane]);
-                float x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
-#pragma unroll
-                for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
-                if (lane == 0) scores[(size_t)q * cap + rec.r0 + j] = ((rec.foreign >> j) & 1u) ? -INFINITY : x;
-                s.exact[j][lane] = float_key_asc(-INFINITY);
-            }
             s.mx[j][lane] = 0u;
             if (lane == 0) s.maxf[j] = 0u;
         }
@@ -825,49 +779,100 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
     if (warp == 0) sm100::tmem_dealloc(tmem, kRtTmemCols);
 }
 
-// Exact 1-bit sums of the candidates the tensor-core kernel wrote out
-// (refine_1bit_kernel's LUT sum, kernels.cu:363-375): the query's 32 LUTs in
-// shared memory, rows 513 floats apart so that lanes on different query
-// tokens spread over the banks, one candidate per thread, the max per
-// (refined doc, query token) by atomicMax on ordered keys.  Flagged queries
-// are skipped: the SIMT kernel rescores them.
+// Exact sums of the candidates the tensor-core kernel handed off, one per
+// thread, the max per (refined doc, query token) by atomicMax on ordered
+// keys.  kFull: fullbit_kernel's arithmetic (16 lane chains over the 8
+// chunks of 16 levels, reduce16 in the AVX-512 order, search_impl.cu:
+// 510-574) against the rotated query; else refine_1bit_kernel's LUT sum
+// (kernels.cu:363-375).  The query's 32 LUTs (or 32 rotated tokens) sit in
+// shared memory with padded rows, so that lanes on different query tokens
+// spread over the banks.  Flagged queries are skipped: the SIMT kernels
+// rescore them.
 constexpr int kRxThreads = 256;
-constexpr int kRxStride = kLutPerQ + 1;
-size_t rt_exact1_smem() { return sizeof(float) * (size_t)kQ * kRxStride; }
+template <bool kFull>
+constexpr int rx_stride() { return kFull ? kDim + 4 : kLutPerQ + 1; }
+template <bool kFull>
+size_t rt_exact_smem() { return sizeof(float) * (size_t)kQ * rx_stride<kFull>(); }
 
-__global__ void __launch_bounds__(kRxThreads) rt_exact1_kernel(RtCandOut co, const float* __restrict__ lut,
-                                                                const float* __restrict__ cb1,
-                                                                const uint32_t* __restrict__ status, int cap,
-                                                                uint32_t* __restrict__ exact) {
-    extern __shared__ float s_lut[];
+template <bool kFull, int kW>
+__global__ void __launch_bounds__(kRxThreads) rt_exact_kernel(RtCandOut co, const uint8_t* __restrict__ codes,
+                                                               const float* __restrict__ factors,
+                                                               const float* __restrict__ table,
+                                                               const float* __restrict__ cb,
+                                                               const uint32_t* __restrict__ status, int cap,
+                                                               uint32_t* __restrict__ exact) {
+    constexpr int kS = rx_stride<kFull>();
+    constexpr int kRow = kFull ? kDim : kLutPerQ;  // floats per query token in `table`
+    extern __shared__ float s_tab[];
     __shared__ float s_cb[kQ];
     const int q = blockIdx.y;
     if (status[q]) return;
     const int n = min(co.count[q], co.ccap);
     if ((int)blockIdx.x * kRxThreads >= n) return;
-    const float* src = lut + (size_t)q * kQ * kLutPerQ;
-    for (int i = threadIdx.x; i < kQ * kLutPerQ; i += kRxThreads)
-        s_lut[(i / kLutPerQ) * kRxStride + (i % kLutPerQ)] = __ldg(src + i);
-    if (threadIdx.x < kQ) s_cb[threadIdx.x] = cb1[q * kQ + threadIdx.x];
+    const float* src = table + (size_t)q * kQ * kRow;
+    for (int i = threadIdx.x; i < kQ * kRow; i += kRxThreads) s_tab[(i / kRow) * kS + (i % kRow)] = __ldg(src + i);
+    if (threadIdx.x < kQ) s_cb[threadIdx.x] = cb[q * kQ + threadIdx.x];
     __syncthreads();
-    const uint4* code = co.code + (size_t)q * co.ccap;
-    const uint2* meta = co.meta + (size_t)q * co.ccap;
+    const uint2* ent = co.ent + (size_t)q * co.ccap;
     for (int i = blockIdx.x * kRxThreads + threadIdx.x; i < n; i += gridDim.x * kRxThreads) {
-        const uint4 c = code[i];
-        const uint2 m = meta[i];
+        const uint2 m = ent[i];
         const int t = (int)(m.y & 31u);
-        const float ip = lut_ip(s_lut + t * kRxStride, c);
-        const float dist = fmul(fsub(ip, s_cb[t]), __uint_as_float(m.x));
+        const float* tab = s_tab + t * kS;
+        float ip;
+        if (kFull) {
+            uint32_t pw[kW * 4];
+            const uint4* cp = reinterpret_cast<const uint4*>(codes) + (size_t)m.x * kW;
+#pragma unroll
+            for (int v = 0; v < kW; ++v) {
+                const uint4 x = __ldg(cp + v);
+                pw[4 * v] = x.x;
+                pw[4 * v + 1] = x.y;
+                pw[4 * v + 2] = x.z;
+                pw[4 * v + 3] = x.w;
+            }
+            float acc[16];
+#pragma unroll
+            for (int l = 0; l < 16; ++l) acc[l] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t wd[4];
+                if (!expand_chunk_fast<kW>(pw, c, wd)) {
+                    const uint8_t* pk = reinterpret_cast<const uint8_t*>(pw);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t x = 0;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) x |= (uint32_t)code_at(pk, c * 16 + j * 4 + b, kW) << (8 * b);
+                        wd[j] = x;
+                    }
+                }
+#pragma unroll
+                for (int l4 = 0; l4 < 4; ++l4) {
+                    const float4 qv = *reinterpret_cast<const float4*>(tab + 16 * c + 4 * l4);
+                    const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        acc[4 * l4 + e] = __fmaf_rn((float)((wd[l4] >> (8 * e)) & 0xFFu), qq[e], acc[4 * l4 + e]);
+                }
+            }
+            ip = reduce16_avx512(acc);
+        } else {
+            ip = lut_ip(tab, __ldg(reinterpret_cast<const uint4*>(codes) + m.x));
+        }
+        const float dist = fmul(fsub(ip, s_cb[t]), __ldg(factors + m.x));
         atomicMax(exact + ((size_t)q * cap + (m.y >> 5)) * kQ + t, float_key_asc(dist));
     }
 }
 
-// 1-bit document scores from the exact maxima: the reference's 128-thread
-// tree (kernels.cu:557-570: strides 64 and 32 add zeros, then 16..1), one
-// warp per refined doc.  Docs without maxima (longer than one tile: the SIMT
-// kernel scores them) are left alone; other shards' docs (-1) score -inf.
-__global__ void rt_tree1_kernel(const uint32_t* __restrict__ exact, const int32_t* __restrict__ docs,
-                                const int32_t* __restrict__ counts, int cap, float* __restrict__ scores) {
+// Document scores from the exact maxima, one warp per refined doc.  kFull:
+// fullbit_kernel's reduction (max[0:16] + max[16:32] lane-wise, then the
+// 16-lane tree); else the reference's 128-thread tree (kernels.cu:557-570:
+// strides 64 and 32 add zeros, then 16..1).  Docs without maxima (longer
+// than one tile: the SIMT kernels score them) are left alone; other shards'
+// docs (-1) score -inf.
+template <bool kFull>
+__global__ void rt_tree_kernel(const uint32_t* __restrict__ exact, const int32_t* __restrict__ docs,
+                               const int32_t* __restrict__ counts, int cap, float* __restrict__ scores) {
     const int q = blockIdx.y, lane = threadIdx.x & 31;
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= counts[q]) return;
@@ -879,10 +884,37 @@ __global__ void rt_tree1_kernel(const uint32_t* __restrict__ exact, const int32_
     const uint32_t key = exact[at * kQ + lane];
     if (__shfl_sync(0xffffffffu, key, 0) == 0u) return;
     const float m = key_to_float_asc(key);
-    float x = fadd(fadd(fadd(0.0f, m), 0.0f), 0.0f);
+    float x;
+    if (kFull) {
+        x = fadd(m, __shfl_down_sync(0xffffffffu, m, 16));
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+        for (int off = 8; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off, 16));
+    } else {
+        x = fadd(fadd(fadd(0.0f, m), 0.0f), 0.0f);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
+    }
     if (lane == 0) scores[at] = x;
+}
+
+// The exact pass and the scores after a tensor-core launch.  table: the
+// LUTs (1-bit) or the rotated queries (full-bit); cb: cb1 or cbex.
+template <bool kFull, int kW>
+static chm_status rt_finish(const RtCandOut& co, const uint8_t* codes, const float* factors, const float* table,
+                            const float* cb, const uint32_t* status, int nq, int cap, uint32_t* exact,
+                            const int32_t* docs, const int32_t* counts, float* scores, cudaStream_t st) {
+    const size_t smem = rt_exact_smem<kFull>();
+    CHM_CUDA(cudaFuncSetAttribute(rt_exact_kernel<kFull, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    // about four resident waves over the batch
+    const int per_sm = kFull ? 8 : 3;
+    const int gx = std::max(1, std::min(64, (148 * per_sm * 4 + nq - 1) / nq));
+    rt_exact_kernel<kFull, kW><<<dim3((unsigned)gx, (unsigned)nq), kRxThreads, smem, st>>>(co, codes, factors, table,
+                                                                                           cb, status, cap, exact);
+    CHM_TRY(launch_status("rt_exact_kernel"));
+    rt_tree_kernel<kFull><<<dim3((unsigned)((cap + 7) / 8), (unsigned)nq), 256, 0, st>>>(exact, docs, counts, cap,
+                                                                                         scores);
+    return launch_status("rt_tree_kernel");
 }
 
 // Queries whose tensor-core launch gave up on a bounded wait are scored
@@ -932,14 +964,13 @@ static void rt_layout(A& a, int nq, int cap, RtWork* w) {
     auto qtile = a.template take<uint8_t>((size_t)nq * kRtN * 128);
     auto qem = a.template take<float>((size_t)nq * kQ);
     const int ccap = kRtCandPerDoc * cap;
-    auto ccode = a.template take<uint4>((size_t)nq * ccap);
-    auto cmeta = a.template take<uint2>((size_t)nq * ccap);
+    auto cent = a.template take<uint2>((size_t)nq * ccap);
     auto ccount = a.template take<int32_t>((size_t)nq);
     auto exact = a.template take<uint32_t>((size_t)nq * cap * kQ);
     if (w)
         *w = RtWork{(int2*)items, (int32_t*)n_items, (uint32_t*)status, (unsigned long long*)stats,
                     (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint32_t*)rows, (uint8_t*)qtile, (float*)qem,
-                    RtCandOut{(uint4*)ccode, (uint2*)cmeta, (int32_t*)ccount, ccap}, (uint32_t*)exact};
+                    RtCandOut{(uint2*)cent, (int32_t*)ccount, ccap}, (uint32_t*)exact};
 }
 
 struct RtSizer {
@@ -998,18 +1029,23 @@ static chm_status rt_grid(Kernel kernel, size_t smem, int nq, int cap, dim3* gri
 }
 
 template <int kW>
-static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex, int fb_cap,
-                                   const RtWork& w, float* scores, cudaStream_t st) {
+static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* rot, const float* cbex,
+                                   const int32_t* fb_docs, const int32_t* num_fb, int fb_cap, const RtWork& w,
+                                   float* scores, cudaStream_t st) {
     rt_query_kernel<true, kW><<<nq, 256, 0, st>>>(rot, cbex, w.qtile, w.qem);
     CHM_TRY(launch_status("rt_query_kernel"));
     const size_t smem = refine_tc_smem_bytes<true, kW>();
     CHM_CUDA(cudaFuncSetAttribute(refine_tc_kernel<true, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid;
     CHM_TRY(rt_grid(refine_tc_kernel<true, kW>, smem, nq, fb_cap, &grid));
+    CHM_CUDA(cudaMemsetAsync(w.cand.count, 0, sizeof(int32_t) * nq, st));
+    CHM_CUDA(cudaMemsetAsync(w.exact, 0, sizeof(uint32_t) * (size_t)nq * fb_cap * kQ, st));
     refine_tc_kernel<true, kW><<<grid, kRtThreads, smem, st>>>(w.meta, w.rows, idx->full_codes, idx->full_factors,
                                                                cbex, rot, nullptr, w.qtile, w.qem, fb_cap, w.n_items,
                                                                scores, w.status, w.stats, w.cand);
-    return launch_status("fullbit_tc_kernel");
+    CHM_TRY(launch_status("fullbit_tc_kernel"));
+    return rt_finish<true, kW>(w.cand, idx->full_codes, idx->full_factors, rot, cbex, w.status, nq, fb_cap, w.exact,
+                               fb_docs, num_fb, scores, st);
 }
 
 // full-bit rescoring of the queries flagged in `status` by the plain kernel
@@ -1076,16 +1112,9 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
         w.meta, w.rows, codes, factors, cb1, rot, lut, w.qtile, w.qem, k_refine, w.n_items, scores, w.status,
         w.stats, w.cand);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
-    // exact sums: about four resident waves of 3 CTAs per SM over the batch
-    const size_t xsmem = chm::rt_exact1_smem();
-    CHM_CUDA(cudaFuncSetAttribute(chm::rt_exact1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsmem));
-    const int xg = std::max(1, std::min(64, (148 * 3 * 4 + nq - 1) / nq));
-    chm::rt_exact1_kernel<<<dim3((unsigned)xg, (unsigned)nq), chm::kRxThreads, xsmem, st>>>(w.cand, lut, cb1, w.status,
-                                                                                          k_refine, w.exact);
-    CHM_TRY(chm::launch_status("rt_exact1_kernel"));
-    chm::rt_tree1_kernel<<<dim3((unsigned)((k_refine + 7) / 8), (unsigned)nq), 256, 0, st>>>(
-        w.exact, refined_docs, num_refined, k_refine, scores);
-    CHM_TRY(chm::launch_status("rt_tree1_kernel"));
+    const chm_status fin = chm::rt_finish<false, 1>(w.cand, codes, factors, lut, cb1, w.status, nq, k_refine, w.exact,
+                                                    refined_docs, num_refined, scores, st);
+    if (fin != CHM_OK) return fin;
     return chm_refine_1bit_complete(idx, nq, lut, cb1, refined_docs, num_refined, k_refine, scores, w.big, w.n_big,
                                     w.status, st);
 }
@@ -1113,12 +1142,12 @@ extern "C" chm_status chm_fullbit_score_tc(const chm_index* idx, int32_t nq, con
     if (a.overflow) return CHM_ERR_CAPACITY;
     CHM_TRY(chm::rt_plan<true>(idx, nullptr, nq, fb_docs, num_fb, fb_cap, w, st));
     switch (w_bits) {
-        case 2: CHM_TRY(chm::launch_fullbit_tc<2>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
-        case 3: CHM_TRY(chm::launch_fullbit_tc<3>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
-        case 4: CHM_TRY(chm::launch_fullbit_tc<4>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
-        case 5: CHM_TRY(chm::launch_fullbit_tc<5>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
-        case 6: CHM_TRY(chm::launch_fullbit_tc<6>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
-        case 7: CHM_TRY(chm::launch_fullbit_tc<7>(idx, nq, rot, cbex, fb_cap, w, scores, st)); break;
+        case 2: CHM_TRY(chm::launch_fullbit_tc<2>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;
+        case 3: CHM_TRY(chm::launch_fullbit_tc<3>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;
+        case 4: CHM_TRY(chm::launch_fullbit_tc<4>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;
+        case 5: CHM_TRY(chm::launch_fullbit_tc<5>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;
+        case 6: CHM_TRY(chm::launch_fullbit_tc<6>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;
+        case 7: CHM_TRY(chm::launch_fullbit_tc<7>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;
         default: return CHM_ERR_INVALID;
     }
     // long docs; then every doc of a query whose tensor-core launch failed

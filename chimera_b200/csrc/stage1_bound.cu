@@ -524,32 +524,51 @@ __global__ void __launch_bounds__(kBxWarps * 32, 1) bound_exact_kernel(ExactCtx 
     __syncthreads();
     const uint4* codes = reinterpret_cast<const uint4*>(c.codes_tok);
     uint32_t* m = s_m + warp * 32;
-    for (int i = blockIdx.x * kBxWarps + warp; i < n; i += gridDim.x * kBxWarps) {
-        const int32_t doc = c.cand[(size_t)q * c.kc + i];
+    auto map_mask = [&](uint32_t cl) {
+        uint32_t h = map_hash(cl);
+        for (int probe = 0; probe < kMapSlots; ++probe, h = (h + 1) & (kMapSlots - 1)) {
+            const uint64_t e = s_map[h];
+            if (e == kMapEmpty) return 0u;
+            if ((uint32_t)(e >> 32) == cl) return (uint32_t)e;
+        }
+        return 0u;
+    };
+    auto post = [&](uint32_t mask, uint4 code, float f) {
+        for (; mask; mask &= mask - 1) {
+            const int t = __ffs(mask) - 1;
+            const float dist = fmul(fsub(lut_ip_prmt(s_lut + t * kLutPerQ, code), s_cb1[t]), f);
+            if (dist > 0.0f) atomicMax(m + t, __float_as_uint(dist));
+        }
+    };
+    // the next doc's token range is loaded while the current one is scored
+    int i = blockIdx.x * kBxWarps + warp;
+    int32_t doc = i < n ? c.cand[(size_t)q * c.kc + i] : 0;
+    int64_t t0 = i < n ? c.doc_ptrs[doc] : 0, t1 = i < n ? c.doc_ptrs[doc + 1] : 0;
+    for (; i < n; i += gridDim.x * kBxWarps) {
+        const int inext = i + gridDim.x * kBxWarps;
+        int32_t dnext = 0;
+        int64_t n0 = 0, n1 = 0;
+        if (inext < n) {
+            dnext = c.cand[(size_t)q * c.kc + inext];
+            n0 = c.doc_ptrs[dnext];
+            n1 = c.doc_ptrs[dnext + 1];
+        }
         m[lane] = 0u;
         __syncwarp();
-        const int64_t t0 = c.doc_ptrs[doc], t1 = c.doc_ptrs[doc + 1];
-        for (int64_t tok = t0 + lane; tok < t1; tok += 32) {
-            const uint32_t cl = __ldg(c.tok_cluster + tok);
-            uint32_t mask = 0;
-            uint32_t h = map_hash(cl);
-            for (int probe = 0; probe < kMapSlots; ++probe, h = (h + 1) & (kMapSlots - 1)) {
-                const uint64_t e = s_map[h];
-                if (e == kMapEmpty) break;
-                if ((uint32_t)(e >> 32) == cl) {
-                    mask = (uint32_t)e;
-                    break;
-                }
-            }
-            if (mask) {
-                const uint4 code = __ldg(codes + tok);
-                const float f = __ldg(c.factor_tok + tok);
-                for (; mask; mask &= mask - 1) {
-                    const int t = __ffs(mask) - 1;
-                    const float dist = fmul(fsub(lut_ip_prmt(s_lut + t * kLutPerQ, code), s_cb1[t]), f);
-                    if (dist > 0.0f) atomicMax(m + t, __float_as_uint(dist));
-                }
-            }
+        // 64 tokens per step, two per lane: clusters, codes and factors all in
+        // flight before the map lookups
+        for (int64_t base = t0; base < t1; base += 64) {
+            const int64_t ta = base + lane, tb = base + 32 + lane;
+            const bool va = ta < t1, vb = tb < t1;
+            uint32_t ca = 0xFFFFFFFFu, cb = 0xFFFFFFFFu;
+            uint4 ka = make_uint4(0, 0, 0, 0), kb = make_uint4(0, 0, 0, 0);
+            float fa = 0.0f, fb = 0.0f;
+            if (va) { ca = __ldg(c.tok_cluster + ta); ka = __ldg(codes + ta); fa = __ldg(c.factor_tok + ta); }
+            if (vb) { cb = __ldg(c.tok_cluster + tb); kb = __ldg(codes + tb); fb = __ldg(c.factor_tok + tb); }
+            const uint32_t ma = va && (int64_t)ca < c.n_clusters ? map_mask(ca) : 0u;
+            const uint32_t mb = vb && (int64_t)cb < c.n_clusters ? map_mask(cb) : 0u;
+            post(ma, ka, fa);
+            post(mb, kb, fb);
         }
         __syncwarp();
         // sum_partial_scores_kernel's tree over the 32 per-token maxima (kernels.cu:192-198)
@@ -558,6 +577,9 @@ __global__ void __launch_bounds__(kBxWarps * 32, 1) bound_exact_kernel(ExactCtx 
         for (int off = 16; off >= 1; off >>= 1) x = fadd(x, __shfl_down_sync(0xffffffffu, x, off));
         if (lane == 0) c.keys[(size_t)q * c.kc + i] = ((uint64_t)__float_as_uint(x) << 32) | (uint32_t)(~(uint32_t)doc);
         __syncwarp();
+        doc = dnext;
+        t0 = n0;
+        t1 = n1;
     }
 }
 

@@ -5,8 +5,9 @@
 // with <q, c> a sequential fp32 fma chain; top-k by (dist, id).  The bf16
 // tensor-core pass only proposes candidates:
 //   1. threshold : tensor-core dists to a prefix of the centroids, exact
-//                  radix select of the K'-th smallest per row -> tau_row, so at
-//                  least K' centroids pass the filter below;
+//                  radix select of a small order statistic per row -> tau_row,
+//                  chosen so that about 4 K' centroids pass the filter below
+//                  (fewer than K' + 1: the row takes the exact path);
 //   2. filter    : tensor-core dists to every centroid, rows keep the
 //                  (dist, id) pairs with dist <= tau_row (per-split buffers);
 //   3. re-rank   : the K' best survivors get exact fp32 dists; the row is
@@ -584,7 +585,7 @@ namespace chm {
 
 struct ProbePlan {
     int64_t rows, nc;
-    int nprobe, kc, prefix, splits, store_splits, cap;
+    int nprobe, kc, kthr, prefix, splits, store_splits, cap;
 };
 
 // SMs of the current device (148 on B200; also the answer when no device is
@@ -628,18 +629,24 @@ static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
     p.nc = nc;
     p.nprobe = nprobe;
     p.kc = std::min<int64_t>(nc, std::min(512, nprobe + 64));
-    // prefix sample such that ~16x kc centroids survive on average (about
-    // 3,100 of the 4,096 a re-rank row holds); a larger sample costs more in
-    // the threshold pass than it saves in the re-rank
+    // a prefix sample of nc / 16 centroids (at least 4 kc); a larger sample
+    // costs more in the threshold pass than it saves in the re-rank
     p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, nc / 16));
     p.prefix = (int)std::min<int64_t>(nc, ((p.prefix + kTN - 1) / kTN) * kTN);
+    // the threshold is the kthr-th smallest prefix dist, kthr chosen so that
+    // about 4 kc centroids pass the filter: enough for the re-rank's kc + 1
+    // (fewer: the row takes the exact path), a quarter of the survivors
+    // (and of the re-rank's select work) of kthr = kc
+    p.kthr = p.kc;
+    if (p.prefix < nc)
+        p.kthr = (int)std::max<int64_t>(1, std::min<int64_t>(p.kc, (4LL * p.kc * p.prefix + nc - 1) / nc));
     const int64_t row_tiles = (rows + kTM - 1) / kTM;
     const int sms = device_sms();
     // small batches split the centroid range across many CTAs, so that a
     // single query still uses the whole GPU
     p.splits = choose_splits(row_tiles, (int)((nc + kTN - 1) / kTN), sms);
     p.store_splits = choose_splits(row_tiles, (p.prefix + kTN - 1) / kTN, sms);
-    const double expect = (double)p.kc * nc / std::max(1, p.prefix);
+    const double expect = (double)p.kthr * nc / std::max(1, p.prefix);
     p.cap = (int)std::min<double>(kSurvMax, std::max(64.0, 4.0 * expect / p.splits + 64));
     return p;
 }
@@ -725,7 +732,7 @@ chm_status chm_tc_probe(const float* rot, int64_t rows, const float* centroids, 
     t1.ld = p.prefix;
     t1.err = cnt + 1;
     CHM_TRY(launch_tc<kStore>(qb, rows, cent_bf16, p.prefix, p.store_splits, t1, st));
-    CHM_TRY(chm_row_kth(pdist, rows, p.prefix, p.kc, tau, tlab, st));
+    CHM_TRY(chm_row_kth(pdist, rows, p.prefix, p.kthr, tau, tlab, st));
     // 2) filter over all centroids
     TcArgs t2{};
     t2.rows = rows;
