@@ -188,21 +188,42 @@ extern "C" chm_status chm_build_assign(const float* x, int64_t n, int32_t dim, c
 // array is fully written by dist_gemm_kernel before row_select_kernel reads
 // it, so nothing in it has to start at zero.  One array per device: calls
 // that overlap on one device (two streams, two host threads) race on it.
+#include <atomic>
 #include <cstdio>
+#include <mutex>
 
 namespace chm {
 
 void set_last_message(const char* msg);
 
+constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) float g_noalloc_probe_dist[CHM_PROBE_NOALLOC_MAX_ELEMENTS];
+static std::atomic<float*> g_noalloc_probe_ptr[kNoAllocMaxDevices];
+static std::mutex g_noalloc_probe_mu;
 
-// Device address of the static scratch in the current context, looked up on
-// every call: a cached address would dangle once cudaDeviceReset (or a
-// primary-context teardown) reloads the module.
+// Device address of the static scratch for the current device, looked up once
+// per device with that device current (the first call on the device), then
+// cached.  cudaDeviceReset unloads the module, which leaves the cached
+// address stale.
 static chm_status noalloc_probe_scratch(float** out) {
-    void* addr = nullptr;
-    CHM_CUDA(cudaGetSymbolAddress(&addr, g_noalloc_probe_dist));
-    *out = static_cast<float*>(addr);
+    int dev = 0;
+    CHM_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        set_last_message("chm_probe_noalloc: device ordinal beyond 63");
+        return CHM_ERR_UNSUPPORTED;
+    }
+    float* p = g_noalloc_probe_ptr[dev].load(std::memory_order_acquire);
+    if (!p) {
+        std::lock_guard<std::mutex> lock(g_noalloc_probe_mu);
+        p = g_noalloc_probe_ptr[dev].load(std::memory_order_acquire);
+        if (!p) {
+            void* addr = nullptr;
+            CHM_CUDA(cudaGetSymbolAddress(&addr, g_noalloc_probe_dist));
+            p = static_cast<float*>(addr);
+            g_noalloc_probe_ptr[dev].store(p, std::memory_order_release);
+        }
+    }
+    *out = p;
     return CHM_OK;
 }
 

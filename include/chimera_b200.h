@@ -134,7 +134,9 @@ chm_status chm_probe(const float* rot_queries, int64_t nrows, const float* centr
  * 131,072 centroids.  Larger nrows * n_clusters returns CHM_ERR_CAPACITY
  * (message in chm_last_error) and launches nothing.  The first call on each
  * device performs a one-time setup (cudaGetSymbolAddress with that device
- * current); make it before any stream capture begins.  The scratch needs no
+ * current); make it before any stream capture begins.  The address it caches
+ * does not survive cudaDeviceReset of that device, so do not call this entry
+ * point on a device after resetting it in the same process.  The scratch needs no
  * zeroing (it is fully written before it is read).  There is one scratch per
  * device: calls that overlap on one device (two streams or two host threads)
  * race, so serialise them. */
