@@ -582,7 +582,7 @@ def profile_stages(torch, capi, index, searcher, q, cfg):
     res = torch.empty(B, p.k, dtype=torch.int64, device=dev)
     nres = torch.empty(B, dtype=torch.int32, device=dev)
     v = C.byref(index.view)
-    fbb = L.chm_fullbit_score_tc_workspace_bytes(B, p.k_refine)
+    fbb = L.chm_refine_tc_workspace_bytes(v, B, p.k_refine)  # room for long docs' parts, as chm_search
     fbws = torch.empty(max(fbb, 1), dtype=torch.uint8, device=dev)
     stages = [
         ("prepare", 1, lambda: L.chm_prepare_queries(P(index.flips), index.dim, index.ex_bits, P(q), ntok, P(rot),

@@ -82,6 +82,7 @@ EXPORTS = {
     "chm_fullbit_score_tc_workspace_bytes": ([I32, I32], SZ),
     "chm_fullbit_score_tc": ([V, I32, V, V, V, V, I32, V, V, SZ, V], C.c_int),
     "chm_refine_1bit_tc_workspace_bytes": ([I32, I32], SZ),
+    "chm_refine_tc_workspace_bytes": ([V, I32, I32], SZ),
     "chm_refine_1bit_tc": ([V, I32, V, V, V, V, V, I32, V, V, SZ, V], C.c_int),
     "chm_select_fullbit": ([I32, V, V, V, I32, I32, I32, V, V, I32, V], C.c_int),
     "chm_fullbit_score": ([V, I32, V, V, V, V, I32, V, V], C.c_int),

@@ -70,7 +70,7 @@ static void layout(A& a, const chm_index* idx, const chm_search_params* p, Searc
                                    ? chm_probe_tc_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe)
                                    : chm_probe_workspace_bytes((int64_t)ntok, idx->n_clusters, p->nprobe);
     const size_t s1_bytes = stage1_bytes(idx, p->batch, p->nprobe, p->table_log2_extra, p->k_refine);
-    const size_t rt_bytes = chm_fullbit_score_tc_workspace_bytes(p->batch, p->k_refine);
+    const size_t rt_bytes = chm_refine_tc_workspace_bytes(idx, p->batch, p->k_refine);
     auto rot = a.template take<float>(ntok * kDim);
     auto cb1 = a.template take<float>(ntok);
     auto cbex = a.template take<float>(ntok);

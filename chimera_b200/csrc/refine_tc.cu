@@ -51,22 +51,27 @@ constexpr uint32_t kRtIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(k
 constexpr int kRtMaxCand = 512;      // candidates per tile (more: the query is rescored by the SIMT kernel)
 constexpr uint32_t kRtNoRow = 0xFFFFFFFFu;  // code index of a row past the item's tokens
 
-// Per-item record, filled in parallel after planning: row offsets of the
-// item's docs, and which docs belong to another shard (-1 ids).
+// Per-item record, filled in parallel after planning: the first token and
+// the row offset of each of the item's docs, and which docs belong to
+// another shard (-1 ids).  Row i of doc j is token tstart[j] + i - tok0[j]
+// (token order).  A part item holds 128-token part p of one longer doc:
+// nd = 1 and tstart[0] is the part's first token.
 struct RtItem {
+    int64_t tstart[kRtMaxDocs];  // first token of doc j's rows
     int r0, nd, ntok;
     uint32_t foreign;            // bit j: doc j of the item is not this shard's
     int tok0[kRtMaxDocs + 1];    // first row of doc j; entries past nd hold ntok
     int pad[3];
 };
-static_assert(sizeof(RtItem) == 96, "RtItem is six 16-byte chunks");
+static_assert(sizeof(RtItem) == 224, "RtItem is fourteen 16-byte chunks");
+// Long docs of at most this many 128-token parts become part items.
+constexpr int kRtMaxParts = 16;
 constexpr int kRtRecWords = (int)sizeof(RtItem) / 4;
 
-// Pipeline slots.  While item k is reduced, item k+1 is multiplied and item
-// k+2's loads land, so records and factors rotate through three slots (item
-// k in slot k % 3).  The 1-bit exact sums read item k's packed codes: three
-// code slots and one expanded tile.  The full-bit exact sums read item k's
-// expanded tile: two tiles and two code slots.
+// Pipeline slots.  While item k is reduced, item k+1 is multiplied, item
+// k+2's codes and factors land and item k+3's record lands (item k+2's row
+// code indices come from its record), so records rotate through four slots
+// and factors and code indices through three (item k in slot k % 4, k % 3).
 template <bool kFull, int kW>
 struct RtShape {
     static constexpr int kA = kFull ? 2 : 1;
@@ -81,8 +86,8 @@ struct __align__(1024) RtSmem {
     uint4 raw[RtShape<kFull, kW>::kRaw][kRtRows * RtShape<kFull, kW>::kRowChunks];  // packed codes as loaded
     float fac[3][kRtRows];
     int row_doc[2][kRtRows];         // item-local doc of each row (-1: past the item's tokens)
-    alignas(16) int rec[3][kRtRecWords];
-    uint32_t ridx[3][kRtRows];       // each row's code index (record slot), for the candidate hand-off
+    alignas(16) int rec[4][kRtRecWords];  // item k's record in slot k % 4
+    uint32_t ridx[3][kRtRows];       // each row's code index (factor slot), for the candidate hand-off
     alignas(16) uint32_t mx[kRtMaxDocs][32];  // max estimate per (doc, query token) as an ordered key, then the threshold
     uint32_t maxf[kRtMaxDocs];       // max |factor| per doc (float bits, >= 0)
     uint32_t cand[kRtMaxCand];       // (row << 5 | t)
@@ -211,7 +216,7 @@ __device__ __forceinline__ bool expand_chunk_fast(const uint32_t* pw, int c, uin
 __global__ void __launch_bounds__(1024) refine_plan_kernel(const int64_t* __restrict__ doc_ptrs,
                                                            const int32_t* __restrict__ refined_docs,
                                                            const int32_t* __restrict__ num_refined, int k_refine,
-                                                           int levels, int2* __restrict__ items,
+                                                           int icap, int levels, int2* __restrict__ items,
                                                            int32_t* __restrict__ n_items, int32_t* __restrict__ big,
                                                            int32_t* __restrict__ n_big) {
     extern __shared__ uint16_t s_j[];
@@ -272,12 +277,52 @@ __global__ void __launch_bounds__(1024) refine_plan_kernel(const int64_t* __rest
         const int c = walk(i);
         if (c < R) {
             if ((s_big[c >> 5] >> (c & 31)) & 1u) big[(size_t)q * k_refine + at_bg++] = c;
-            else items[(size_t)q * k_refine + at_it++] = make_int2(c, (int)s_j[c]);
+            else items[(size_t)q * icap + at_it++] = make_int2(c, (int)s_j[c]);
+        }
+    }
+    // Long docs of at most kRtMaxParts parts become part items (r, -(p + 1))
+    // after the others, when the item array has room for all of them; the
+    // rest stay in the big list for the SIMT kernels.
+    __syncthreads();
+    constexpr int kPer = 8;  // big docs per thread: k_refine <= 8192 over 1024 threads
+    const int nb = (int)tot_bg;
+    const int b0 = min(nb, tid * kPer), b1 = min(nb, b0 + kPer);
+    int br[kPer], bp[kPer];
+    uint32_t cnt_parts = 0, cnt_keep = 0;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        br[u] = -1;
+        bp[u] = 0;
+        if (b0 + u < b1) {
+            const int r = big[(size_t)q * k_refine + b0 + u];
+            const int64_t d = refined_docs[(size_t)q * k_refine + r];
+            const int64_t l = doc_ptrs[d + 1] - doc_ptrs[d];
+            const int np = (int)((l + kRtRows - 1) / kRtRows);
+            br[u] = r;
+            bp[u] = np <= kRtMaxParts ? np : 0;
+            if (bp[u]) cnt_parts += np; else ++cnt_keep;
+        }
+    }
+    uint32_t tot_parts, tot_keep;
+    uint32_t at_p = blk_scan_excl(cnt_parts, s_warp, &tot_parts);
+    uint32_t at_k = blk_scan_excl(cnt_keep, s_warp, &tot_keep);
+    const bool room = tot_it + tot_parts <= (uint32_t)icap;
+    if (room) {
+        // every thread has read its big entries (the scans synchronise)
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            if (br[u] < 0) continue;
+            if (bp[u]) {
+                for (int pp = 0; pp < bp[u]; ++pp)
+                    items[(size_t)q * icap + tot_it + at_p++] = make_int2(br[u], -(pp + 1));
+            } else {
+                big[(size_t)q * k_refine + at_k++] = br[u];
+            }
         }
     }
     if (tid == 0) {
-        n_items[q] = (int32_t)tot_it;
-        n_big[q] = (int32_t)tot_bg;
+        n_items[q] = (int32_t)(tot_it + (room ? tot_parts : 0));
+        n_big[q] = (int32_t)(room ? tot_keep : tot_bg);
     }
 }
 
@@ -294,21 +339,36 @@ static size_t rt_plan_smem(int cap) {
     return 2 * ((size_t)levels * w + ((levels * w) & 1)) + 4 * (size_t)((cap + 31) / 32);
 }
 
-// One warp per item: its record and, per row, the code index (the cluster
-// position through tok2pos when it is given, else the token id: full codes
-// and the token-order 1-bit codes; kRtNoRow past the item's tokens).
-template <bool kFull>
-__global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint32_t* __restrict__ tok2pos,
-                               const int32_t* __restrict__ docs, int cap, const int2* __restrict__ items,
-                               const int32_t* __restrict__ n_items, RtItem* __restrict__ meta,
-                               uint32_t* __restrict__ rows) {
+// One warp per item: its record.  A normal item (x, y) holds refined docs
+// x..y-1; a part item (r, -(p + 1)) holds tokens 128 p .. 128 p + 127 of doc r.
+__global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const int32_t* __restrict__ docs, int cap,
+                               int icap, const int2* __restrict__ items, const int32_t* __restrict__ n_items,
+                               RtItem* __restrict__ meta) {
     const int q = blockIdx.y;
     const int lane = threadIdx.x & 31;
     const int NI = n_items[q];
     // warps stride over the query's items
     for (int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < NI;
          item += gridDim.x * (blockDim.x >> 5)) {
-        const int2 rr = items[(size_t)q * cap + item];
+        const int2 rr = items[(size_t)q * icap + item];
+        RtItem* m = meta + (size_t)q * icap + item;
+        if (rr.y < 0) {
+            const int part = -rr.y - 1;
+            const int64_t d = docs[(size_t)q * cap + rr.x];
+            const int64_t t0 = doc_ptrs[d], len = doc_ptrs[d + 1] - t0;
+            const int64_t rem = len - (int64_t)part * kRtRows;
+            const int ntok = (int)(rem < kRtRows ? rem : kRtRows);
+            if (lane == 0) {
+                m->tstart[0] = t0 + (int64_t)part * kRtRows;
+                m->r0 = rr.x;
+                m->nd = 1;
+                m->ntok = ntok;
+                m->foreign = 0u;
+                m->tok0[0] = 0;
+            }
+            if (lane < kRtMaxDocs) m->tok0[lane + 1] = ntok;
+            continue;
+        }
         const int nd = rr.y - rr.x;
         int64_t first = 0;
         int len = 0;
@@ -329,7 +389,6 @@ __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint3
         }
         const int ntok = __shfl_sync(0xffffffffu, incl, 31);
         const uint32_t fmask = __ballot_sync(0xffffffffu, foreign);
-        RtItem* m = meta + (size_t)q * cap + item;
         if (lane == 0) {
             m->r0 = rr.x;
             m->nd = nd;
@@ -337,55 +396,46 @@ __global__ void rt_fill_kernel(const int64_t* __restrict__ doc_ptrs, const uint3
             m->foreign = fmask;
             m->tok0[0] = 0;
         }
-        if (lane < kRtMaxDocs) m->tok0[lane + 1] = incl;  // docs past nd repeat the total
-        uint32_t* rw = rows + ((size_t)q * cap + item) * kRtRows;
-        // this lane's four rows: their tokens first (shuffles need every lane),
-        // then the four cluster-position loads together
-        int64_t token[kRtRows / 32];
-#pragma unroll
-        for (int g = 0; g < kRtRows / 32; ++g) {
-            const int row = 32 * g + lane;
-            // the row's doc: the first doc whose inclusive end exceeds row
-            int lo = 0, hi = nd;
-#pragma unroll
-            for (int step = 0; step < 6; ++step) {
-                const int mid = (lo + hi) >> 1;
-                const int end = __shfl_sync(0xffffffffu, incl, mid & 31);
-                if (lo < hi) {
-                    if (end <= row) lo = mid + 1; else hi = mid;
-                }
-            }
-            const int ld = min(lo, 31);
-            const int64_t f0 = __shfl_sync(0xffffffffu, first, ld);
-            const int prev_end = __shfl_sync(0xffffffffu, incl, (ld + 31) & 31);  // every lane shuffles
-            token[g] = row < ntok ? f0 + (row - (ld > 0 ? prev_end : 0)) : -1;
+        if (lane < kRtMaxDocs) {
+            m->tok0[lane + 1] = incl;  // docs past nd repeat the total
+            m->tstart[lane] = first;
         }
-        uint32_t v[kRtRows / 32];
-#pragma unroll
-        for (int g = 0; g < kRtRows / 32; ++g)
-            v[g] = token[g] < 0 ? kRtNoRow : tok2pos == nullptr ? (uint32_t)token[g] : __ldg(tok2pos + token[g]);
-#pragma unroll
-        for (int g = 0; g < kRtRows / 32; ++g) rw[32 * g + lane] = v[g];
     }
 }
 
-// Starts the asynchronous loads of one item: its record into record slot rs,
-// and this thread's row (packed code, factor) into code slot cs and factor
-// slot rs.  idx: the row's code index, kRtNoRow for none.
+// Starts the asynchronous load of one item's record into record slot rs.
 template <bool kFull, int kW>
-__device__ __forceinline__ void rt_issue(RtSmem<kFull, kW>& s, int rs, int cs, const RtItem* rec, uint32_t idx,
-                                         const uint8_t* __restrict__ codes, const float* __restrict__ factors) {
+__device__ __forceinline__ void rt_issue_rec(RtSmem<kFull, kW>& s, int rs, const RtItem* rec) {
+    if (threadIdx.x < kRtRecWords / 4)
+        cp_async16(&s.rec[rs][4 * threadIdx.x], reinterpret_cast<const uint4*>(rec) + threadIdx.x);
+}
+
+// Starts the asynchronous loads of this thread's row of the item whose
+// record is in slot rs (landed): the packed code into code slot cs and the
+// factor into factor slot fs; the row's code index (the token, or its
+// cluster position through tok2pos; kRtNoRow past the item's tokens) goes to
+// ridx[fs].
+template <bool kFull, int kW>
+__device__ __forceinline__ void rt_issue_rows(RtSmem<kFull, kW>& s, int rs, int fs, int cs,
+                                              const uint8_t* __restrict__ codes, const float* __restrict__ factors,
+                                              const uint32_t* __restrict__ tok2pos) {
     constexpr int kC = RtShape<kFull, kW>::kRowChunks;
     const int tid = threadIdx.x;
-    if (tid < kRtRecWords / 4) cp_async16(&s.rec[rs][4 * tid], reinterpret_cast<const uint4*>(rec) + tid);
-    s.ridx[rs][tid] = idx;
+    const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[rs]);
+    uint32_t idx = kRtNoRow;
+    if (tid < rec.ntok) {
+        int j = 0;
+        while (rec.tok0[j + 1] <= tid) ++j;
+        const int64_t tok = rec.tstart[j] + (tid - rec.tok0[j]);
+        idx = tok2pos != nullptr ? __ldg(tok2pos + tok) : (uint32_t)tok;
+    }
+    s.ridx[fs][tid] = idx;
     if (idx != kRtNoRow) {
         const uint4* src = reinterpret_cast<const uint4*>(codes) + (size_t)idx * kC;
 #pragma unroll
         for (int v = 0; v < kC; ++v) cp_async16(&s.raw[cs][tid * kC + v], src + v);
-        cp_async4(&s.fac[rs][tid], factors + idx);
+        cp_async4(&s.fac[fs][tid], factors + idx);
     }
-    cp_async_commit();
 }
 
 // Expands this thread's row of the item in record slot rs / code slot cs
@@ -539,14 +589,14 @@ struct RtCandOut {
 // to rt_exact_kernel, which holds the query's LUTs (1-bit) or rotated query
 // (full-bit) in shared memory, and rt_tree_kernel makes the scores.
 //
-// Item k (the CTA's k-th) goes through: loads issued (iteration k-2), tile
-// expanded and multiplied (iteration k-1), accumulators reduced (iteration k).
+// Item k (the CTA's k-th) goes through: record loaded (iteration k-3),
+// codes and factors loaded (iteration k-2), tile expanded and multiplied
+// (iteration k-1), accumulators reduced (iteration k).
 template <bool kFull, int kW>
 __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
-    const RtItem* __restrict__ meta, const uint32_t* __restrict__ rows, const uint8_t* __restrict__ codes,
-    const float* __restrict__ factors, const float* __restrict__ cb1, const float* __restrict__ rot,
-    const float* __restrict__ lut, const uint8_t* __restrict__ qtile, const float* __restrict__ qem, int cap,
-    const int32_t* __restrict__ n_items, float* __restrict__ scores, uint32_t* __restrict__ status,
+    const RtItem* __restrict__ meta, const uint32_t* __restrict__ tok2pos, const uint8_t* __restrict__ codes,
+    const float* __restrict__ factors, const float* __restrict__ cb1, const uint8_t* __restrict__ qtile,
+    const float* __restrict__ qem, int icap, const int32_t* __restrict__ n_items, uint32_t* __restrict__ status,
     unsigned long long* __restrict__ stats, RtCandOut co) {
     using Sh = RtShape<kFull, kW>;
     extern __shared__ uint8_t smem_raw[];
@@ -583,13 +633,19 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
     }
     const uint32_t tmem = s.tmem_base;
     const float inv_fix = 1.0f / kFix;
-    const size_t qb = (size_t)q * cap;
+    const size_t qb = (size_t)q * icap;
     const int G = gridDim.x;
     int it = blockIdx.x;
-    // item 0 loaded, expanded and multiplied; item 1 loaded; item 2's code indices in registers
-    uint32_t idx = __ldg(rows + (qb + it) * kRtRows + tid);
-    rt_issue(s, 0, 0, meta + qb + it, idx, codes, factors);
-    if (it + G < NI) idx = __ldg(rows + (qb + it + G) * kRtRows + tid);
+    // records of items 0..2 loaded; item 0's rows loaded, expanded and
+    // multiplied; item 1's rows loaded
+    rt_issue_rec(s, 0, meta + qb + it);
+    if (it + G < NI) rt_issue_rec(s, 1, meta + qb + it + G);
+    if (it + 2 * G < NI) rt_issue_rec(s, 2, meta + qb + it + 2 * G);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    rt_issue_rows(s, 0, 0, 0, codes, factors, tok2pos);
+    cp_async_commit();
     cp_async_wait_all();
     __syncthreads();
     rt_expand(s, 0, 0, 0, 0);
@@ -600,8 +656,8 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
         sm100::tc_fence_after();
         rt_mma(s, 0, tmem);
     }
-    if (it + G < NI) rt_issue(s, 1, 1 % Sh::kRaw, meta + qb + it + G, idx, codes, factors);
-    if (it + 2 * G < NI) idx = __ldg(rows + (qb + it + 2 * G) * kRtRows + tid);
+    if (it + G < NI) rt_issue_rows(s, 1, 1, 1 % Sh::kRaw, codes, factors, tok2pos);
+    cp_async_commit();
     cp_async_wait_all();
     __syncthreads();
 
@@ -610,7 +666,7 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
     int k = 0;
     for (; it < NI; it += G, ++k) {
         const bool has1 = it + G < NI, has2 = it + 2 * G < NI, has3 = it + 3 * G < NI;
-        const int rs = k % 3;
+        const int rs = k % 4, fs = k % 3;  // record slot; factor and code-index slot
         // ---- item k's accumulators, one row per thread.  Every thread waits
         // for the MMA itself; a wait that ran out is acted on at the barrier
         // below (what was read or expanded meanwhile is then discarded).
@@ -622,7 +678,7 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
         sm100::tmem_ld32_async(taddr + 32, lo);
         sm100::tmem_wait_ld();
         // ---- item k+1: expanded and multiplied while item k is reduced
-        if (has1) rt_expand(s, (k + 1) % 3, (k + 1) % Sh::kRaw, (k + 1) % Sh::kA, (k + 1) & 1);
+        if (has1) rt_expand(s, (k + 1) % 4, (k + 1) % Sh::kRaw, (k + 1) % Sh::kA, (k + 1) & 1);
         fence_proxy_async_smem();
         sm100::tc_fence_before();
         if (__syncthreads_or(!ok)) {
@@ -633,14 +689,15 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
             sm100::tc_fence_after();
             rt_mma(s, (k + 1) % Sh::kA, tmem);
         }
-        // ---- item k+2's loads and item k+3's code indices, in flight during the reduction
-        if (has2) rt_issue(s, (k + 2) % 3, (k + 2) % Sh::kRaw, meta + qb + it + 2 * G, idx, codes, factors);
-        if (has3) idx = __ldg(rows + (qb + it + 3 * G) * kRtRows + tid);
+        // ---- item k+2's rows and item k+3's record, in flight during the reduction
+        if (has2) rt_issue_rows(s, (k + 2) % 4, (k + 2) % 3, (k + 2) % Sh::kRaw, codes, factors, tok2pos);
+        if (has3) rt_issue_rec(s, (k + 3) % 4, meta + qb + it + 3 * G);
+        cp_async_commit();
         // ---- estimated dists, kept in registers
         const RtItem& rec = *reinterpret_cast<const RtItem*>(s.rec[rs]);
         const int T = rec.ntok;
         const int ld = tid < T ? s.row_doc[k & 1][tid] : -1;
-        const float f = tid < T ? s.fac[rs][tid] : 0.0f;
+        const float f = tid < T ? s.fac[fs][tid] : 0.0f;
         // (x * 2^-14 is exact, so the fma rounds exactly as the subtraction
         // of the product would)
         float da[32];
@@ -743,7 +800,7 @@ __global__ void __launch_bounds__(kRtThreads, kFull ? 3 : 5) refine_tc_kernel(
                     const uint32_t e = s.cand[c];
                     const int row = (int)(e >> 5);
                     co.ent[(size_t)q * co.ccap + base + c] =
-                        make_uint2(s.ridx[rs][row], ((uint32_t)(rec.r0 + s.row_doc[k & 1][row]) << 5) | (e & 31u));
+                        make_uint2(s.ridx[fs][row], ((uint32_t)(rec.r0 + s.row_doc[k & 1][row]) << 5) | (e & 31u));
                 }
             }
         }
@@ -933,6 +990,7 @@ size_t refine_tc_smem_bytes() { return sizeof(RtSmem<kFull, kW>) + 1024; }
 
 // Workspace of one tensor-core refinement call.
 struct RtWork {
+    int icap;        // items per query (parts of long docs included)
     int2* items;
     int32_t* n_items;
     uint32_t* status;
@@ -940,36 +998,34 @@ struct RtWork {
     int32_t* big;
     int32_t* n_big;
     RtItem* meta;
-    uint32_t* rows;
     uint8_t* qtile;  // per query: the B tile (rt_query_kernel)
     float* qem;      // per query token: the margin
-    RtCandOut cand;  // 1-bit: the candidates of each query
-    uint32_t* exact; // 1-bit: [nq][cap][32] exact max per (refined doc, query token), ordered keys
+    RtCandOut cand;  // the candidates of each query
+    uint32_t* exact; // [nq][cap][32] exact max per (refined doc, query token), ordered keys
 };
 
-// 1-bit candidate slots per refined doc: every (doc, query token) has at
-// least one, and about 1.03 on average (more: the query is flagged).
-constexpr int kRtCandPerDoc = 40;
+// Candidate slots per item: every (doc or part, query token) has at least
+// one, about 1.03 on average (more: the query is flagged).
+constexpr int kRtCandPerItem = 36;
 
 template <typename A>
-static void rt_layout(A& a, int nq, int cap, RtWork* w) {
-    auto items = a.template take<int2>((size_t)nq * cap);
+static void rt_layout(A& a, int nq, int cap, int icap, RtWork* w) {
+    auto items = a.template take<int2>((size_t)nq * icap);
     auto n_items = a.template take<int32_t>((size_t)nq);
     auto status = a.template take<uint32_t>((size_t)nq);
     auto stats = a.template take<unsigned long long>(2);  // rows scored, exact candidates (last call)
     auto big = a.template take<int32_t>((size_t)nq * cap);
     auto n_big = a.template take<int32_t>((size_t)nq);
-    auto meta = a.template take<RtItem>((size_t)nq * cap);
-    auto rows = a.template take<uint32_t>((size_t)nq * cap * kRtRows);
+    auto meta = a.template take<RtItem>((size_t)nq * icap);
     auto qtile = a.template take<uint8_t>((size_t)nq * kRtN * 128);
     auto qem = a.template take<float>((size_t)nq * kQ);
-    const int ccap = kRtCandPerDoc * cap;
+    const int ccap = kRtCandPerItem * icap;
     auto cent = a.template take<uint2>((size_t)nq * ccap);
     auto ccount = a.template take<int32_t>((size_t)nq);
     auto exact = a.template take<uint32_t>((size_t)nq * cap * kQ);
     if (w)
-        *w = RtWork{(int2*)items, (int32_t*)n_items, (uint32_t*)status, (unsigned long long*)stats,
-                    (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint32_t*)rows, (uint8_t*)qtile, (float*)qem,
+        *w = RtWork{icap, (int2*)items, (int32_t*)n_items, (uint32_t*)status, (unsigned long long*)stats,
+                    (int32_t*)big, (int32_t*)n_big, (RtItem*)meta, (uint8_t*)qtile, (float*)qem,
                     RtCandOut{(uint2*)cent, (int32_t*)ccount, ccap}, (uint32_t*)exact};
 }
 
@@ -982,20 +1038,41 @@ struct RtSizer {
     }
 };
 
-// tok2pos: NULL when the rows' codes are in token order.
-template <bool kFull>
-static chm_status rt_plan(const chm_index* idx, const uint32_t* tok2pos, int nq, const int32_t* docs,
-                          const int32_t* counts, int cap, const RtWork& w, cudaStream_t st) {
+static size_t rt_bytes(int nq, int cap, int icap) {
+    RtSizer s;
+    rt_layout(s, nq, cap, icap, nullptr);
+    return s.s.off;
+}
+
+// Items per query with room for the parts of long docs: per refined doc one
+// item, plus twice the mean doc length in parts (refined docs run longer
+// than the mean), at most kRtMaxParts - 1 more.
+static int rt_icap(const chm_index* idx, int cap) {
+    if (idx == nullptr || idx->max_doc_len <= kRtRows || idx->num_docs <= 0) return cap;
+    const double mean = (double)idx->n_tokens / (double)idx->num_docs;
+    const int extra = (int)std::min<double>(kRtMaxParts - 1, std::ceil(2.0 * mean / kRtRows));
+    return (int)std::min<int64_t>((int64_t)cap * (1 + extra), (int64_t)1 << 30);
+}
+
+// The item capacity a call's workspace affords: the room for long docs'
+// parts when it is large enough, else one item per refined doc.
+static int rt_call_icap(const chm_index* idx, int nq, int cap, size_t ws_bytes) {
+    const int full = rt_icap(idx, cap);
+    return ws_bytes >= rt_bytes(nq, cap, full) ? full : cap;
+}
+
+static chm_status rt_plan(const chm_index* idx, int nq, const int32_t* docs, const int32_t* counts, int cap,
+                          const RtWork& w, cudaStream_t st) {
     refine_status_clear_kernel<<<(nq + 255) / 256, 256, 0, st>>>(w.status, nq, w.stats);
     CHM_TRY(launch_status("refine_status_clear_kernel"));
     const size_t plan_smem = rt_plan_smem(cap);
     CHM_CUDA(cudaFuncSetAttribute(refine_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem));
-    refine_plan_kernel<<<nq, 1024, plan_smem, st>>>(idx->doc_ptrs, docs, counts, cap, rt_plan_levels(cap), w.items,
-                                                    w.n_items, w.big, w.n_big);
+    refine_plan_kernel<<<nq, 1024, plan_smem, st>>>(idx->doc_ptrs, docs, counts, cap, w.icap, rt_plan_levels(cap),
+                                                    w.items, w.n_items, w.big, w.n_big);
     CHM_TRY(launch_status("refine_plan_kernel"));
     // one warp per item, 4 warps per block, 128 blocks per query striding over its items
-    rt_fill_kernel<kFull><<<dim3(128u, (unsigned)nq), 128, 0, st>>>(
-        idx->doc_ptrs, tok2pos, docs, cap, w.items, w.n_items, w.meta, w.rows);
+    rt_fill_kernel<<<dim3(128u, (unsigned)nq), 128, 0, st>>>(idx->doc_ptrs, docs, cap, w.icap, w.items, w.n_items,
+                                                            w.meta);
     return launch_status("rt_fill_kernel");
 }
 
@@ -1037,12 +1114,12 @@ static chm_status launch_fullbit_tc(const chm_index* idx, int nq, const float* r
     const size_t smem = refine_tc_smem_bytes<true, kW>();
     CHM_CUDA(cudaFuncSetAttribute(refine_tc_kernel<true, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid;
-    CHM_TRY(rt_grid(refine_tc_kernel<true, kW>, smem, nq, fb_cap, &grid));
+    CHM_TRY(rt_grid(refine_tc_kernel<true, kW>, smem, nq, w.icap, &grid));
     CHM_CUDA(cudaMemsetAsync(w.cand.count, 0, sizeof(int32_t) * nq, st));
     CHM_CUDA(cudaMemsetAsync(w.exact, 0, sizeof(uint32_t) * (size_t)nq * fb_cap * kQ, st));
-    refine_tc_kernel<true, kW><<<grid, kRtThreads, smem, st>>>(w.meta, w.rows, idx->full_codes, idx->full_factors,
-                                                               cbex, rot, nullptr, w.qtile, w.qem, fb_cap, w.n_items,
-                                                               scores, w.status, w.stats, w.cand);
+    refine_tc_kernel<true, kW><<<grid, kRtThreads, smem, st>>>(w.meta, nullptr, idx->full_codes, idx->full_factors,
+                                                               cbex, w.qtile, w.qem, w.icap, w.n_items, w.status,
+                                                               w.stats, w.cand);
     CHM_TRY(launch_status("fullbit_tc_kernel"));
     return rt_finish<true, kW>(w.cand, idx->full_codes, idx->full_factors, rot, cbex, w.status, nq, fb_cap, w.exact,
                                fb_docs, num_fb, scores, st);
@@ -1073,9 +1150,13 @@ static chm_status rescore_flagged_fullbit(const chm_index* idx, int nq, const fl
 }  // namespace chm
 
 extern "C" size_t chm_refine_1bit_tc_workspace_bytes(int32_t nq, int32_t k_refine) {
-    chm::RtSizer s;
-    chm::rt_layout(s, nq, k_refine, nullptr);
-    return s.s.off;
+    if (nq <= 0 || k_refine <= 0) return 0;
+    return chm::rt_bytes(nq, k_refine, k_refine);
+}
+
+extern "C" size_t chm_refine_tc_workspace_bytes(const chm_index* idx, int32_t nq, int32_t cap) {
+    if (nq <= 0 || cap <= 0) return 0;
+    return chm::rt_bytes(nq, cap, chm::rt_icap(idx, cap));
 }
 
 chm_status chm_refine_1bit_complete(const chm_index* idx, int32_t nq, const float* lut, const float* cb1,
@@ -1091,25 +1172,24 @@ extern "C" chm_status chm_refine_1bit_tc(const chm_index* idx, int32_t nq, const
     cudaStream_t st = (cudaStream_t)stream;
     chm::Arena a(ws, ws_bytes);
     chm::RtWork w;
-    chm::rt_layout(a, nq, k_refine, &w);
+    chm::rt_layout(a, nq, k_refine, chm::rt_call_icap(idx, nq, k_refine, ws_bytes), &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
     // the token-order copies make each refined doc one contiguous span of codes
     const bool tok_order = idx->codes1_tok != nullptr && idx->factor1_tok != nullptr;
     const uint8_t* codes = tok_order ? idx->codes1_tok : idx->codes1;
     const float* factors = tok_order ? idx->factor1_tok : idx->factor1;
-    CHM_TRY(chm::rt_plan<false>(idx, tok_order ? nullptr : idx->tok2pos, nq, refined_docs, num_refined, k_refine, w,
-                                st));
+    CHM_TRY(chm::rt_plan(idx, nq, refined_docs, num_refined, k_refine, w, st));
     chm::rt_query_kernel<false, 1><<<nq, 256, 0, st>>>(rot, cb1, w.qtile, w.qem);
     CHM_TRY(chm::launch_status("rt_query_kernel"));
     const size_t smem = chm::refine_tc_smem_bytes<false, 1>();
     CHM_CUDA(cudaFuncSetAttribute(chm::refine_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
     dim3 grid;
-    CHM_TRY(chm::rt_grid(chm::refine_tc_kernel<false, 1>, smem, nq, k_refine, &grid));
+    CHM_TRY(chm::rt_grid(chm::refine_tc_kernel<false, 1>, smem, nq, w.icap, &grid));
     CHM_CUDA(cudaMemsetAsync(w.cand.count, 0, sizeof(int32_t) * nq, st));
     CHM_CUDA(cudaMemsetAsync(w.exact, 0, sizeof(uint32_t) * (size_t)nq * k_refine * chm::kQ, st));
     chm::refine_tc_kernel<false, 1><<<grid, chm::kRtThreads, smem, st>>>(
-        w.meta, w.rows, codes, factors, cb1, rot, lut, w.qtile, w.qem, k_refine, w.n_items, scores, w.status,
+        w.meta, tok_order ? nullptr : idx->tok2pos, codes, factors, cb1, w.qtile, w.qem, w.icap, w.n_items, w.status,
         w.stats, w.cand);
     CHM_TRY(chm::launch_status("refine_tc_kernel"));
     const chm_status fin = chm::rt_finish<false, 1>(w.cand, codes, factors, lut, cb1, w.status, nq, k_refine, w.exact,
@@ -1138,9 +1218,9 @@ extern "C" chm_status chm_fullbit_score_tc(const chm_index* idx, int32_t nq, con
         return chm_fullbit_score(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, scores, stream);
     chm::Arena a(ws, ws_bytes);
     chm::RtWork w;
-    chm::rt_layout(a, nq, fb_cap, &w);
+    chm::rt_layout(a, nq, fb_cap, chm::rt_call_icap(idx, nq, fb_cap, ws_bytes), &w);
     if (a.overflow) return CHM_ERR_CAPACITY;
-    CHM_TRY(chm::rt_plan<true>(idx, nullptr, nq, fb_docs, num_fb, fb_cap, w, st));
+    CHM_TRY(chm::rt_plan(idx, nq, fb_docs, num_fb, fb_cap, w, st));
     switch (w_bits) {
         case 2: CHM_TRY(chm::launch_fullbit_tc<2>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;
         case 3: CHM_TRY(chm::launch_fullbit_tc<3>(idx, nq, rot, cbex, fb_docs, num_fb, fb_cap, w, scores, st)); break;

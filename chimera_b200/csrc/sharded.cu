@@ -79,7 +79,7 @@ void shard_layout(A& a, const chm_index* idx, const chm_search_params* p, int wo
                                    ? chm_probe_tc_workspace_bytes((int64_t)per, idx->n_clusters, p->nprobe)
                                    : chm_probe_workspace_bytes((int64_t)per, idx->n_clusters, p->nprobe);
     const size_t s1_bytes = chm_stage1_ex_workspace_bytes(idx, p->batch, p->nprobe, p->table_log2_extra);
-    const size_t rt_bytes = chm_fullbit_score_tc_workspace_bytes(p->batch, p->k_refine);
+    const size_t rt_bytes = chm_refine_tc_workspace_bytes(idx, p->batch, p->k_refine);
     ShardBuffers s;
     s.rot = (float*)a.template take<float>(rows * kDim);
     s.cb1 = (float*)a.template take<float>(rows);

@@ -267,7 +267,7 @@ class CudaShardBackend:
         self.onebit = e(B, self.kr)
         self.fd, self.nf, self.fs = e(B, self.kr, dt=torch.int32), e(B, dt=torch.int32), e(B, self.kr)
         self.res, self.nres = e(B, self.k, dt=torch.int64), e(B, dt=torch.int32)
-        self.fb_bytes = self.L.chm_fullbit_score_tc_workspace_bytes(B, self.kr)
+        self.fb_bytes = self.L.chm_refine_tc_workspace_bytes(self.v, B, self.kr)
         self.fb_ws = e(max(self.fb_bytes, 1), dt=torch.uint8)
         self._probe_ws = {}
         self._s1_extra = None

@@ -242,6 +242,14 @@ chm_status chm_fullbit_score(const chm_index* index, int32_t nq, const float* ro
  * to 7 (w = 8 runs chm_fullbit_score).  Workspace from
  * chm_fullbit_score_tc_workspace_bytes. */
 size_t chm_fullbit_score_tc_workspace_bytes(int32_t nq, int32_t fb_cap);
+
+/* Workspace for chm_refine_1bit_tc or chm_fullbit_score_tc on `index` with
+ * room to score its documents longer than one 128-token tile on the tensor
+ * cores as 128-token parts (up to 16 parts; their maxima merge across parts).
+ * The two sizes above give long documents that room only when the batch's
+ * other items leave it, and otherwise the SIMT kernels.  Any of the three
+ * sizes works with either call. */
+size_t chm_refine_tc_workspace_bytes(const chm_index* index, int32_t nq, int32_t cap);
 chm_status chm_fullbit_score_tc(const chm_index* index, int32_t nq, const float* rot,
                                 const float* cbex, const int32_t* fb_docs, const int32_t* num_fb,
                                 int32_t fb_cap, float* scores, void* workspace,

@@ -3,7 +3,9 @@ lane order for the candidates) against chm_fullbit_score (exact sums of every
 token): identical scores bit for bit, at every code width the filter handles
 (w = 1 + ex_bits = 2..7; w = 8 takes the plain kernel), on the oracle's
 selected docs, on random doc lists with shard-foreign slots (-1) and short
-counts, and on documents longer than one 128-token tile."""
+counts, and on documents longer than one 128-token tile (tensor-core parts
+with chm_refine_tc_workspace_bytes' room, else the SIMT long-document
+kernel)."""
 import ctypes as C
 
 import numpy as np
@@ -16,7 +18,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def _both(c, d, lists, counts, cap):
+def _both(c, d, lists, counts, cap, parts=True):
     L = capi.lib()
     st = capi._stream(torch)
     P = capi._ptr
@@ -29,7 +31,7 @@ def _both(c, d, lists, counts, cap):
     b = torch.full((nq, cap), 7.0, device="cuda")
     v = C.byref(d.view)
     capi.check(L.chm_fullbit_score(v, nq, P(rot), P(cbex), P(fd), P(nf), cap, P(a), st), "simt")
-    wb = L.chm_fullbit_score_tc_workspace_bytes(nq, cap)
+    wb = L.chm_refine_tc_workspace_bytes(v, nq, cap) if parts else L.chm_fullbit_score_tc_workspace_bytes(nq, cap)
     ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
     capi.check(L.chm_fullbit_score_tc(v, nq, P(rot), P(cbex), P(fd), P(nf), cap, P(b), P(ws), wb, st), "tc")
     torch.cuda.synchronize()
@@ -62,8 +64,9 @@ def test_fullbit_tc_matches_simt_on_oracle_lists(name, ex_bits):
     np.testing.assert_array_equal(a[0, :counts[0]].view(np.uint32), np.asarray(want, np.float32).view(np.uint32))
 
 
+@pytest.mark.parametrize("parts", [True, False])
 @pytest.mark.parametrize("name", ["small", "long"])
-def test_fullbit_tc_random_lists(name):
+def test_fullbit_tc_random_lists(name, parts):
     c = _corpus.corpus(name)
     cfg = c["cfg"]
     d = _corpus.device_index(c, torch)
@@ -74,4 +77,4 @@ def test_fullbit_tc_random_lists(name):
     lists[rng.random(lists.shape) < 0.25] = -1
     counts = rng.integers(0, cap + 1, nq).astype(np.int32)
     counts[0] = cap
-    _both(c, d, lists, counts, cap)
+    _both(c, d, lists, counts, cap, parts)

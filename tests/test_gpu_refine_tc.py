@@ -2,8 +2,9 @@
 candidates) against chm_refine_1bit (exact LUT sums of every token): the
 1-bit document scores must be identical bit for bit.  Covers the realistic
 refined lists of the oracle, random lists, documents longer than one
-128-token tile (scored by the SIMT long-document kernel), shard-foreign slots
-(-1) and short per-query counts."""
+128-token tile (tensor-core parts whose maxima merge across parts when the
+workspace has room -- chm_refine_tc_workspace_bytes -- else the SIMT
+long-document kernel), shard-foreign slots (-1) and short per-query counts."""
 import numpy as np
 import pytest
 
@@ -15,7 +16,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def _run_both(c, d, lists, counts, k_refine):
+def _run_both(c, d, lists, counts, k_refine, parts=True):
     L = capi.lib()
     st = capi._stream(torch)
     P = capi._ptr
@@ -29,7 +30,8 @@ def _run_both(c, d, lists, counts, k_refine):
     a = torch.full((nq, k_refine), 7.0, device="cuda")
     b = torch.full((nq, k_refine), 7.0, device="cuda")
     capi.check(L.chm_refine_1bit(C_view(d), nq, P(lut), P(cb1), P(rd), P(nr), k_refine, P(a), st), "simt")
-    wb = L.chm_refine_1bit_tc_workspace_bytes(nq, k_refine)
+    wb = (L.chm_refine_tc_workspace_bytes(C_view(d), nq, k_refine) if parts else
+          L.chm_refine_1bit_tc_workspace_bytes(nq, k_refine))
     ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
     capi.check(L.chm_refine_1bit_tc(C_view(d), nq, P(lut), P(cb1), P(rot), P(rd), P(nr), k_refine, P(b), P(ws), wb,
                                     st), "tc")
@@ -46,9 +48,10 @@ def C_view(d):
     return C.byref(d.view)
 
 
+@pytest.mark.parametrize("parts", [True, False])
 @pytest.mark.parametrize("layout", ["token", "cluster"])
 @pytest.mark.parametrize("name", ["mini", "small", "long"])
-def test_refine_tc_matches_simt_on_oracle_lists(name, layout):
+def test_refine_tc_matches_simt_on_oracle_lists(name, layout, parts):
     """Both kernels on both 1-bit layouts: the token-order copies (one span
     per doc) and the cluster-ordered arrays gathered through tok2pos."""
     c = _corpus.corpus(name)
@@ -66,7 +69,7 @@ def test_refine_tc_matches_simt_on_oracle_lists(name, layout):
         # the oracle's own 1-bit scores are the reference for the first query's list
         if q == 0:
             want0 = tr["onebit_scores"]
-    a = _run_both(c, d, lists, counts, kr)
+    a = _run_both(c, d, lists, counts, kr, parts)
     np.testing.assert_array_equal(a[0, :counts[0]].view(np.uint32), want0.view(np.uint32))
 
 
