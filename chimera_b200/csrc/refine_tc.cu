@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(1024) refine_plan_kernel(const int64_t* __rest
         }
     }
     // Long docs of at most kRtMaxParts parts become part items (r, -(p + 1))
-    // after the others, when the item array has room for all of them; the
+    // after the others, in refined order while the item array has room; the
     // rest stay in the big list for the SIMT kernels.
     __syncthreads();
     constexpr int kPer = 8;  // big docs per thread: k_refine <= 8192 over 1024 threads
@@ -303,26 +303,41 @@ __global__ void __launch_bounds__(1024) refine_plan_kernel(const int64_t* __rest
             if (bp[u]) cnt_parts += np; else ++cnt_keep;
         }
     }
-    uint32_t tot_parts, tot_keep;
-    uint32_t at_p = blk_scan_excl(cnt_parts, s_warp, &tot_parts);
-    uint32_t at_k = blk_scan_excl(cnt_keep, s_warp, &tot_keep);
-    const bool room = tot_it + tot_parts <= (uint32_t)icap;
-    if (room) {
-        // every thread has read its big entries (the scans synchronise)
+    // a doc's parts fit when they end within the room the other items leave
+    const uint32_t room = (uint32_t)icap - tot_it;
+    uint32_t tot_parts;
+    const uint32_t start_p = blk_scan_excl(cnt_parts, s_warp, &tot_parts);
+    uint32_t at = start_p, fit_parts = 0;
+    cnt_keep = 0;
 #pragma unroll
-        for (int u = 0; u < kPer; ++u) {
-            if (br[u] < 0) continue;
-            if (bp[u]) {
-                for (int pp = 0; pp < bp[u]; ++pp)
-                    items[(size_t)q * icap + tot_it + at_p++] = make_int2(br[u], -(pp + 1));
-            } else {
-                big[(size_t)q * k_refine + at_k++] = br[u];
-            }
+    for (int u = 0; u < kPer; ++u) {
+        if (br[u] < 0) continue;
+        if (bp[u] && at + bp[u] <= room) fit_parts += bp[u];
+        else {
+            if (bp[u]) bp[u] = -bp[u];  // does not fit: stays in the big list
+            ++cnt_keep;
+        }
+        at += bp[u] > 0 ? bp[u] : -bp[u];  // eligible docs advance the running part offset
+    }
+    // fitting docs are a prefix in refined order (their parts start earlier),
+    // so their items are contiguous from tot_it
+    uint32_t tot_fit, tot_keep;
+    uint32_t at_p = blk_scan_excl(fit_parts, s_warp, &tot_fit);
+    uint32_t at_k = blk_scan_excl(cnt_keep, s_warp, &tot_keep);
+    // every thread has read its big entries (the scans synchronise)
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        if (br[u] < 0) continue;
+        if (bp[u] > 0) {
+            for (int pp = 0; pp < bp[u]; ++pp)
+                items[(size_t)q * icap + tot_it + at_p++] = make_int2(br[u], -(pp + 1));
+        } else {
+            big[(size_t)q * k_refine + at_k++] = br[u];
         }
     }
     if (tid == 0) {
-        n_items[q] = (int32_t)(tot_it + (room ? tot_parts : 0));
-        n_big[q] = (int32_t)(room ? tot_keep : tot_bg);
+        n_items[q] = (int32_t)(tot_it + tot_fit);
+        n_big[q] = (int32_t)tot_keep;
     }
 }
 
@@ -1045,12 +1060,13 @@ static size_t rt_bytes(int nq, int cap, int icap) {
 }
 
 // Items per query with room for the parts of long docs: per refined doc one
-// item, plus twice the mean doc length in parts (refined docs run longer
-// than the mean), at most kRtMaxParts - 1 more.
+// item, plus three times the mean doc length in parts (refined docs run
+// longer than the mean), at most kRtMaxParts - 1 more.  Parts that do not
+// fit go to the SIMT kernels.
 static int rt_icap(const chm_index* idx, int cap) {
     if (idx == nullptr || idx->max_doc_len <= kRtRows || idx->num_docs <= 0) return cap;
     const double mean = (double)idx->n_tokens / (double)idx->num_docs;
-    const int extra = (int)std::min<double>(kRtMaxParts - 1, std::ceil(2.0 * mean / kRtRows));
+    const int extra = (int)std::min<double>(kRtMaxParts - 1, std::ceil(3.0 * mean / kRtRows));
     return (int)std::min<int64_t>((int64_t)cap * (1 + extra), (int64_t)1 << 30);
 }
 
