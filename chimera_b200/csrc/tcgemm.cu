@@ -73,7 +73,7 @@ struct TcSmem {
     alignas(1024) uint8_t b[kStages][kTileBytes];
     uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, mma_done;
     uint32_t tmem_base;
-    float cn[2][2][kTN];        // per-tile ||c||^2: [epilogue group][double buffer]
+    alignas(16) float cn[2][2][kTN];  // per-tile ||c||^2: [epilogue group][double buffer]
     float pass[2][4][32][33];   // per-lane copy of 32 values whose mask has set bits
     int rowcnt[kTM];            // filter: survivors appended per row (both groups)
 };
@@ -245,17 +245,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
                                     out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j]), cnb[c * 32 + j]);
                         }
                     } else {
-                        // Branch-free pass over the 32 values: bit j set when column
-                        // j can enter (d <= tau for the filter, d <= the current
-                        // 16th best for the top-16).  d = cn - 2 v is exact in one
-                        // fma because 2 v is exact.  Out-of-range columns carry +inf
-                        // norms and never pass.
+                        // Column j can enter when d <= tau (filter) or d <= the
+                        // current 16th best (top-16).  d = cn - 2 v is exact in
+                        // one fma because 2 v is exact.  Out-of-range columns
+                        // carry +inf norms and never pass.  Most groups of 32
+                        // have no such column: the fast pass takes their minimum
+                        // in four independent chains (norms four at a time), and
+                        // only a passing group builds its mask.
                         const float lim = (MODE == kFilter) ? tau : thr;
-                        uint32_t mask = 0;
+                        const float4* cn4 = reinterpret_cast<const float4*>(cnb + c * 32);
+                        float m0 = INFINITY, m1 = INFINITY, m2 = INFINITY, m3 = INFINITY;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float d = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j]), cnb[c * 32 + j]);
-                            mask |= (d <= lim ? 1u : 0u) << j;
+                        for (int j4 = 0; j4 < 8; ++j4) {
+                            const float4 n4 = cn4[j4];
+                            m0 = fminf(m0, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 0]), n4.x));
+                            m1 = fminf(m1, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 1]), n4.y));
+                            m2 = fminf(m2, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 2]), n4.z));
+                            m3 = fminf(m3, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 3]), n4.w));
+                        }
+                        uint32_t mask = 0;
+                        if (fminf(fminf(m0, m1), fminf(m2, m3)) <= lim) {
+                            uint32_t mk[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const float d = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j]), cnb[c * 32 + j]);
+                                mk[j & 3] |= (d <= lim ? 1u : 0u) << j;
+                            }
+                            mask = (mk[0] | mk[1]) | (mk[2] | mk[3]);
                         }
                         if (mask) {
                             // rare: copy the 32 values to this lane's shared row and
@@ -458,11 +474,37 @@ __global__ void __launch_bounds__(kRerankThreads) probe_rerank_kernel(
     bitonic_asc(s_ex, ne);
     const float kth = key_to_float_asc((uint32_t)(s_ex[nprobe - 1] >> 32));
     const bool certified = kth < a_star - e;
-    if (!certified) {
-        if (threadIdx.x == 0) fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
+    if (certified) {
+        for (int i = threadIdx.x; i < nprobe; i += blockDim.x) labels[row * nprobe + i] = (uint32_t)s_ex[i];
         return;
     }
-    for (int i = threadIdx.x; i < nprobe; i += blockDim.x) labels[row * nprobe + i] = (uint32_t)s_ex[i];
+    // Second try before the exact fallback: every survivor gets its exact
+    // dist.  Every centroid left out then has an approximate dist above tau,
+    // so the row is proven when its k-th exact dist is below tau - E.  (With
+    // many centroids per mixture component the gap after the k-th candidate is
+    // often narrower than E, while tau sits well beyond it.)
+    if (total > m) {
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            int lo = 0, hi = splits;
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (s_off[mid + 1] <= i) lo = mid + 1; else hi = mid;
+            }
+            const uint32_t col = (uint32_t)surv[((size_t)row * splits + lo) * cap + (i - s_off[lo])];
+            s_keys[i] = dist_key(exact_dist(s_q, centroids + (size_t)col * kDim, cn[col]), col);
+        }
+        int nt = 1;
+        while (nt < total) nt <<= 1;
+        for (int i = total + threadIdx.x; i < nt; i += blockDim.x) s_keys[i] = ~0ull;
+        __syncthreads();
+        bitonic_asc(s_keys, nt);
+        const float kth2 = key_to_float_asc((uint32_t)(s_keys[nprobe - 1] >> 32));
+        if (kth2 < tau[row] - e) {
+            for (int i = threadIdx.x; i < nprobe; i += blockDim.x) labels[row * nprobe + i] = (uint32_t)s_keys[i];
+            return;
+        }
+    }
+    if (threadIdx.x == 0) fallback_list[atomicAdd(fallback_cnt, 1u)] = (int32_t)row;
 }
 
 // Assignment re-rank: one warp per row over its 16 x splits candidates.
@@ -629,9 +671,10 @@ static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
     p.nc = nc;
     p.nprobe = nprobe;
     p.kc = std::min<int64_t>(nc, std::min(512, nprobe + 64));
-    // a prefix sample of nc / 16 centroids (at least 4 kc); a larger sample
-    // costs more in the threshold pass than it saves in the re-rank
-    p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, nc / 16));
+    // a prefix sample of nc / 16 centroids, at most 65,536 (at least 4 kc); a
+    // larger sample costs more in the threshold pass (its dists are written
+    // out and selected per row) than it saves in the re-rank
+    p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, std::min<int64_t>(nc / 16, 65536)));
     p.prefix = (int)std::min<int64_t>(nc, ((p.prefix + kTN - 1) / kTN) * kTN);
     // the threshold is the kthr-th smallest prefix dist, kthr chosen so that
     // about 4 kc centroids pass the filter: enough for the re-rank's kc + 1

@@ -65,6 +65,9 @@ CONFIGS = {
     # C3's per-query shape (mean list length 244, nprobe 128, k_refine 3000) on 1/8 of its corpus:
     # the small case for full ncu captures (about 1 GB on the device)
     "c3s": Config("c3s", 125_000, ("normal", 64, 20, 8, 180), 2048, 128, 32768, 4, 128, 3000, 300),
+    # C5's density of centroids per mixture component (64) and its query and
+    # search shape on 1/64 of its documents: the probe's near-ties as at C5
+    "c5s": Config("c5s", 137_500, ("normal", 68, 22, 8, 180), 1024, 1024, 65_536, 4, 128, 3000, 300),
     # test-sized corpora with the same recipe
     "mini": Config("mini", 300, ("normal", 64, 20, 8, 180), 64, 6, 128, 4, 16, 60, 20, 5, 10),
     "small": Config("small", 2000, ("normal", 64, 20, 8, 180), 256, 16, 512, 4, 24, 300, 60,
