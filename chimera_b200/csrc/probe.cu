@@ -22,13 +22,20 @@ constexpr int kGemmThreads = 256;  // 16 x 16 threads, 4 x 8 outputs each
 
 // Loads a BK-wide k-slab of A (rows) and B (cols) into shared memory,
 // transposed so the inner loop reads contiguous rows/cols.
+// rows_dev (optional): a device count that caps `rows` (row tiles past it
+// return at once).
 __global__ void __launch_bounds__(kGemmThreads) dist_gemm_kernel(
     const float* __restrict__ A, int64_t rows, const float* __restrict__ B,
-    const float* __restrict__ bnorm, int64_t cols, int lda, int kdim, float* __restrict__ dist) {
+    const float* __restrict__ bnorm, int64_t cols, int lda, int kdim, float* __restrict__ dist,
+    const uint32_t* __restrict__ rows_dev = nullptr) {
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[BK][BN + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int64_t row0 = (int64_t)blockIdx.y * BM;
+    if (rows_dev != nullptr) {
+        rows = min(rows, (int64_t)*rows_dev);
+        if (row0 >= rows) return;
+    }
     const int64_t col0 = (int64_t)blockIdx.x * BN;
     float acc[4][8];
 #pragma unroll
@@ -82,6 +89,45 @@ __global__ void __launch_bounds__(kSelThreads) row_select_kernel(
     const int64_t row = blockIdx.x;
     block_select_smallest(dist + row * cols, cols, k, labels + row * k);
 }
+
+// Exact top-k of listed rows in batches (the tensor-core probe's and the
+// assignment's fallback): the first min(count, max_rows) listed rows are
+// gathered, one SIMT GEMM pass computes their exact dists to every centroid
+// (each centroid read once for the whole batch), and a CTA per row selects.
+__global__ void fallback_gather_kernel(const float* __restrict__ x, const int32_t* __restrict__ list,
+                                       const uint32_t* __restrict__ count, int max_rows, float* __restrict__ q) {
+    const int i = blockIdx.x;
+    const int n = min((int)*count, max_rows);
+    const float v = i < n ? x[(int64_t)list[i] * kDim + threadIdx.x] : 0.0f;
+    q[(int64_t)i * kDim + threadIdx.x] = v;
+}
+
+__global__ void __launch_bounds__(kSelThreads) fallback_select_kernel(const float* __restrict__ dist, int64_t cols,
+                                                                      int k, const int32_t* __restrict__ list,
+                                                                      const uint32_t* __restrict__ count, int max_rows,
+                                                                      uint32_t* __restrict__ labels) {
+    const int i = blockIdx.x;
+    if (i >= min((int)*count, max_rows)) return;
+    block_select_smallest(dist + (int64_t)i * cols, cols, k, labels + (int64_t)list[i] * k);
+}
+
+}  // namespace chm
+
+chm_status chm_probe_fallback_batch(const float* x, const int32_t* list, const uint32_t* count, int max_rows,
+                                    const float* centroids, const float* cn, int64_t nc, int k, float* q_scratch,
+                                    float* dist_scratch, uint32_t* labels, cudaStream_t st) {
+    chm::fallback_gather_kernel<<<max_rows, chm::kDim, 0, st>>>(x, list, count, max_rows, q_scratch);
+    CHM_TRY(chm::launch_status("fallback_gather_kernel"));
+    dim3 g((unsigned)((nc + chm::BN - 1) / chm::BN), (unsigned)((max_rows + chm::BM - 1) / chm::BM));
+    chm::dist_gemm_kernel<<<g, chm::kGemmThreads, 0, st>>>(q_scratch, max_rows, centroids, cn, nc, chm::kDim,
+                                                           chm::kDim, dist_scratch, count);
+    CHM_TRY(chm::launch_status("dist_gemm_kernel"));
+    chm::fallback_select_kernel<<<max_rows, chm::kSelThreads, 0, st>>>(dist_scratch, nc, k, list, count, max_rows,
+                                                                        labels);
+    return chm::launch_status("fallback_select_kernel");
+}
+
+namespace chm {
 
 // k-th smallest value per row (the tensor-core probe's filter threshold).
 __global__ void __launch_bounds__(kSelThreads) row_kth_kernel(const float* __restrict__ dist, int64_t cols, int k,

@@ -47,7 +47,8 @@ constexpr int kTcThreads = 384;
 constexpr int kBoxBytes = 128 * 64 * 2;             // one 128 x 64 bf16 TMA box
 constexpr int kTileBytes = 2 * kBoxBytes;           // 128 x 128 bf16
 constexpr int kTopA = 16;                           // assignment candidates per row
-constexpr int kFallbackRows = 16;                   // rows recomputed exactly at a time
+constexpr int kFallbackRows = 16;                   // rows recomputed exactly at a time, past the batch
+constexpr int kFallbackBatch = 64;                  // probe rows recomputed exactly in one GEMM pass
 constexpr int kMaxSplits = 296;                     // centroid-range splits per row tile
 constexpr uint32_t kIdesc = sm100::idesc_bf16_f32(kTM, kTN);
 
@@ -560,11 +561,11 @@ __global__ void __launch_bounds__(1024) exact_rows_kernel(const float* __restric
                                                           const float* __restrict__ cn, int64_t cols, int k,
                                                           const int32_t* __restrict__ list,
                                                           const uint32_t* __restrict__ count, float* __restrict__ scratch,
-                                                          uint32_t* __restrict__ out_labels) {
+                                                          uint32_t* __restrict__ out_labels, uint32_t first = 0) {
     __shared__ float s_q[kDim];
     const uint32_t n = *count;
     float* d = scratch + (size_t)blockIdx.x * cols;
-    for (uint32_t r = blockIdx.x; r < n; r += gridDim.x) {
+    for (uint32_t r = first + blockIdx.x; r < n; r += gridDim.x) {
         const int64_t row = list[r];
         __syncthreads();
         if (threadIdx.x < kDim) s_q[threadIdx.x] = x[row * kDim + threadIdx.x];
@@ -622,6 +623,10 @@ static chm_status launch_tc(const __nv_bfloat16* a, int64_t rows, const __nv_bfl
 
 }  // namespace chm
 
+
+chm_status chm_probe_fallback_batch(const float* x, const int32_t* list, const uint32_t* count, int max_rows,
+                                    const float* centroids, const float* cn, int64_t nc, int k, float* q_scratch,
+                                    float* dist_scratch, uint32_t* labels, cudaStream_t st);
 
 namespace chm {
 
@@ -739,6 +744,8 @@ size_t chm_tc_probe_workspace_bytes(int64_t rows, int64_t nc, int nprobe) {
     s.take<int32_t>((size_t)rows);                           // fallback list
     s.take<uint32_t>(4);                                     // counters
     s.take<float>((size_t)chm::kFallbackRows * nc);        // fallback scratch rows
+    s.take<float>((size_t)chm::kFallbackBatch * chm::kDim);  // batched fallback: rows
+    s.take<float>((size_t)chm::kFallbackBatch * nc);         // batched fallback: dists
     return s.off;
 }
 
@@ -761,6 +768,8 @@ chm_status chm_tc_probe(const float* rot, int64_t rows, const float* centroids, 
     auto* fl = a.take<int32_t>((size_t)rows);
     auto* cnt = a.take<uint32_t>(4);
     auto* scratch = a.take<float>((size_t)kFallbackRows * nc);
+    auto* fbq = a.take<float>((size_t)kFallbackBatch * kDim);
+    auto* fbd = a.take<float>((size_t)kFallbackBatch * nc);
     if (a.overflow) return CHM_ERR_CAPACITY;
     CHM_CUDA(cudaMemsetAsync(cnt, 0, 16, st));
     const int64_t nel = rows * kK;
@@ -791,7 +800,10 @@ chm_status chm_tc_probe(const float* rot, int64_t rows, const float* centroids, 
     probe_rerank_kernel<<<(unsigned)rows, kRerankThreads, 0, st>>>(rot, centroids, cn, surv, scnt, p.splits, p.cap,
                                                                    tau, p.kc, nprobe, cnmax, labels, fl, cnt);
     CHM_TRY(launch_status("probe_rerank_kernel"));
-    exact_rows_kernel<<<kFallbackRows, 1024, 0, st>>>(rot, centroids, cn, nc, nprobe, fl, cnt, scratch, labels);
+    // the first kFallbackBatch flagged rows in one exact GEMM pass, the rest row by row
+    CHM_TRY(chm_probe_fallback_batch(rot, fl, cnt, kFallbackBatch, centroids, cn, nc, nprobe, fbq, fbd, labels, st));
+    exact_rows_kernel<<<kFallbackRows, 1024, 0, st>>>(rot, centroids, cn, nc, nprobe, fl, cnt, scratch, labels,
+                                                      (uint32_t)kFallbackBatch);
     return launch_status("exact_rows_kernel");
 }
 
@@ -802,6 +814,8 @@ size_t chm_tc_assign_workspace_bytes(int64_t rows, int64_t nc) {
     s.take<int32_t>((size_t)rows);
     s.take<uint32_t>(4);
     s.take<float>((size_t)chm::kFallbackRows * nc);
+    s.take<float>((size_t)chm::kFallbackBatch * chm::kDim);
+    s.take<float>((size_t)chm::kFallbackBatch * nc);
     return s.off;
 }
 
@@ -815,6 +829,8 @@ chm_status chm_tc_assign(const float* x128, int64_t rows, const float* centroids
     auto* fl = a.take<int32_t>((size_t)rows);
     auto* cnt = a.take<uint32_t>(4);
     auto* scratch = a.take<float>((size_t)kFallbackRows * nc);
+    auto* fbq = a.take<float>((size_t)kFallbackBatch * kDim);
+    auto* fbd = a.take<float>((size_t)kFallbackBatch * nc);
     if (a.overflow) return CHM_ERR_CAPACITY;
     CHM_CUDA(cudaMemsetAsync(cnt, 0, 16, st));
     const int64_t nel = rows * kK;
@@ -830,7 +846,9 @@ chm_status chm_tc_assign(const float* x128, int64_t rows, const float* centroids
     assign_rerank_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x128, rows, centroids, cn, top, 2,
                                                                              cnmax, assign, fl, cnt);
     CHM_TRY(launch_status("assign_rerank_kernel"));
-    exact_rows_kernel<<<kFallbackRows, 1024, 0, st>>>(x128, centroids, cn, nc, 1, fl, cnt, scratch, assign);
+    CHM_TRY(chm_probe_fallback_batch(x128, fl, cnt, kFallbackBatch, centroids, cn, nc, 1, fbq, fbd, assign, st));
+    exact_rows_kernel<<<kFallbackRows, 1024, 0, st>>>(x128, centroids, cn, nc, 1, fl, cnt, scratch, assign,
+                                                      (uint32_t)kFallbackBatch);
     return launch_status("exact_rows_kernel");
 }
 

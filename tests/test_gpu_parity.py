@@ -321,6 +321,38 @@ def test_probe_tensor_core_fallback_on_ties():
     assert (tc[:, 0] < 300).all()
 
 
+def test_probe_tensor_core_fallback_every_row():
+    """One centroid repeated: every dist ties, no row can be certified, and
+    all 300 rows take the exact fallback -- the first 64 in the batched GEMM
+    pass, the rest row by row."""
+    rng = np.random.default_rng(9)
+    one = rng.standard_normal((1, 128)).astype(np.float32)
+    one /= np.linalg.norm(one)
+    cents = np.repeat(one, 2048, axis=0)
+    rows = rng.standard_normal((300, 128)).astype(np.float32)
+    tc, simt = _probe_pair(rows, cents, 24)
+    np.testing.assert_array_equal(tc, simt)
+    np.testing.assert_array_equal(tc, np.tile(np.arange(24, dtype=np.uint32), (300, 1)))
+
+
+def test_build_assign_tensor_core_fallback_every_row():
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((700, 128)).astype(np.float32)
+    cents = np.repeat(x[:1], 500, axis=0)          # every row ties on all centroids
+    L = capi.lib()
+    xd, cd = T(x), T(cents)
+    cn = torch.empty(cents.shape[0], device="cuda")
+    capi.check(L.chm_row_norms(P(cd), cents.shape[0], P(cn), S()), "norms")
+    nb = L.chm_build_assign_workspace_bytes(x.shape[0], cents.shape[0])
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    out = torch.full((x.shape[0],), -1, dtype=torch.int32, device="cuda")
+    capi.check(L.chm_build_assign(P(xd), x.shape[0], 128, P(cd), P(cn), cents.shape[0], P(out), P(ws), nb, S()),
+               "assign")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), np.zeros(x.shape[0], np.int32))
+    np.testing.assert_array_equal(O.assign(x[:50], cents), np.zeros(50, np.uint32))
+
+
 def test_build_assign_tensor_core_with_duplicate_centroids():
     rng = np.random.default_rng(11)
     x = rng.standard_normal((5000, 128)).astype(np.float32)
