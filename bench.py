@@ -43,7 +43,9 @@ def log(*a):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event reasons sampled during the timed region:
+    through NVML every 10 ms (read-only queries), else through nvidia-smi
+    (about one sample per 200 ms)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -54,17 +56,45 @@ class ClockSampler:
         self.rows = []
         self._stop = threading.Event()
         self._t = None
+        self._nv = None
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(gpu_index).uuid)
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            self._nv = pynvml
+        except Exception:
+            self._nv = None
+
+    def _sample_nvml(self):
+        nv, h = self._nv, self._h
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        why = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        flags = ["Active" if why & b else "Not Active" for b in bits]
+        return [str(self.gpu), str(sm), str(mx), "", hex(why)] + flags
 
     def _run(self):
         while not self._stop.is_set():
             try:
+                if self._nv is not None:
+                    self.rows.append(self._sample_nvml())
+                    self._stop.wait(0.01)
+                    continue
                 out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q,
                                       "--format=csv,noheader,nounits"], capture_output=True, text=True,
                                      timeout=5).stdout.strip()
                 if out:
                     self.rows.append([x.strip() for x in out.split(",")])
             except Exception:
-                pass
+                self._nv = None
             self._stop.wait(0.2)
 
     def __enter__(self):
@@ -85,7 +115,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in self.rows for i in range(4)
                           if len(r) > 5 + i and r[5 + i].lower().startswith("active")})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml" if self._nv else "nvidia-smi"}
 
 
 # DRAM bytes per unit of work of the dominant kernel, from the ncu capture in

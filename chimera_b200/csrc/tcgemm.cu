@@ -21,11 +21,12 @@
 // certificate over the 32 candidates.
 //
 // GEMM kernel: one CTA = 128 query rows x a range of 128-centroid tiles.
-// Warp 0 issues TMA loads (A once, B through a 4-stage ring), warp 1 owns
-// TMEM and issues tcgen05.mma (M=128, N=128, K=16 x 8) into two TMEM
-// accumulators, warps 4-7 and 8-11 drain alternate accumulators with
-// tcgen05.ld.  Every TMA load goes to the issuing CTA alone (no cluster-wide
-// delivery).
+// One warp issues TMA loads (A once, B through a 3- or 4-stage ring), one
+// owns TMEM and issues tcgen05.mma (M=128, N=128, K=16 x 8) into one TMEM
+// accumulator per epilogue group, and the epilogue groups (four warps each,
+// warps 0 .. 4 G - 1, so that warp % 4 is the TMEM lane quarter) drain the
+// accumulators in turn with tcgen05.ld.  Every TMA load goes to the issuing
+// CTA alone (no cluster-wide delivery).
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
@@ -40,10 +41,6 @@
 namespace chm {
 
 constexpr int kTM = 128, kTN = 128, kK = 128;
-constexpr int kStages = 4;
-// warp 0 TMA, warp 1 MMA, warps 4-7 and 8-11 two epilogue groups that drain
-// alternate accumulators
-constexpr int kTcThreads = 384;
 constexpr int kBoxBytes = 128 * 64 * 2;             // one 128 x 64 bf16 TMA box
 constexpr int kTileBytes = 2 * kBoxBytes;           // 128 x 128 bf16
 constexpr int kTopA = 16;                           // assignment candidates per row
@@ -69,26 +66,60 @@ struct TcArgs {
     uint32_t* err;
 };
 
+// Epilogue groups per mode: the filter and store passes drain with three
+// groups (12 epilogue warps, three TMEM accumulators of 128 columns), so that
+// three warps per scheduler hide the TMEM-load and shared-load latency; the
+// top-16 pass keeps two (its 16 running keys per row need the registers).
+// Warps are spread over the four schedulers round-robin, and each scheduler
+// holds a quarter of the register file (16,384 registers): with 14 warps
+// (at most 4 per scheduler) a thread may use 128.
+template <int MODE>
+struct TcCfg {
+    static constexpr int kGroups = MODE == kTop16 ? 2 : 3;
+    static constexpr int kEpiWarps = 4 * kGroups;
+    static constexpr int kTmaWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
+    static constexpr int kThreads = (kEpiWarps + 2) * 32;
+    static constexpr int kStages = 4;
+    static constexpr uint32_t kTmemCols = kGroups <= 2 ? 256u : 512u;  // a power of two >= kGroups * 128
+    static constexpr int kMaxRegs = (16384 / ((kEpiWarps + 2 + 3) / 4 * 32)) / 8 * 8;
+};
+
+template <int MODE>
 struct TcSmem {
+    using C = TcCfg<MODE>;
     alignas(1024) uint8_t a[kTileBytes];
-    alignas(1024) uint8_t b[kStages][kTileBytes];
-    uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, mma_done;
+    alignas(1024) uint8_t b[C::kStages][kTileBytes];
+    uint64_t full[C::kStages], empty[C::kStages], acc_full[C::kGroups], acc_empty[C::kGroups], a_full, mma_done;
     uint32_t tmem_base;
-    alignas(16) float cn[2][2][kTN];  // per-tile ||c||^2: [epilogue group][double buffer]
-    float pass[2][4][32][33];   // per-lane copy of 32 values whose mask has set bits
-    int rowcnt[kTM];            // filter: survivors appended per row (both groups)
+    alignas(16) float cn[C::kEpiWarps][kTN];  // per epilogue warp: ||c||^2 of its current tile
+    float pass[C::kEpiWarps][32][33];         // per lane: 32 values of a group with set mask bits
+    int rowcnt[kTM];                          // filter: survivors appended per row (all groups)
 };
 
 __device__ __forceinline__ uint64_t dist_key(float d, uint32_t col) {
     return ((uint64_t)float_key_asc(d) << 32) | col;
 }
 
+// this lane's 4 norms of tile `tile` (columns 4 lane .. 4 lane + 3); +inf past the end
+__device__ __forceinline__ float4 tile_norms4(const float* __restrict__ cn, int64_t cols, int tile, int lane) {
+    const int64_t c = (int64_t)tile * kTN + 4 * lane;
+    float4 v;
+    v.x = c + 0 < cols ? __ldg(cn + c + 0) : INFINITY;
+    v.y = c + 1 < cols ? __ldg(cn + c + 1) : INFINITY;
+    v.z = c + 2 < cols ? __ldg(cn + c + 2) : INFINITY;
+    v.w = c + 3 < cols ? __ldg(cn + c + 3) : INFINITY;
+    return v;
+}
+
 template <int MODE>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                               const __grid_constant__ CUtensorMap tmB,
-                                                               TcArgs p) {
+__global__ void __maxnreg__(TcCfg<MODE>::kMaxRegs) tc_dist_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                         const __grid_constant__ CUtensorMap tmB,
+                                                                         TcArgs p) {
+    using C = TcCfg<MODE>;
+    constexpr int NG = C::kGroups, NS = C::kStages;
     extern __shared__ uint8_t smem_raw[];
-    TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    TcSmem<MODE>& s =
+        *reinterpret_cast<TcSmem<MODE>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row0 = (int64_t)blockIdx.y * kTM;
     const int n_tiles_total = (int)((p.cols + kTN - 1) / kTN);
@@ -97,11 +128,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
     const int n_tiles = max(0, t_end - t_begin);
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStages; ++i) {
+        for (int i = 0; i < NS; ++i) {
             sm100::mbar_init(&s.full[i], 1);
             sm100::mbar_init(&s.empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NG; ++i) {
             sm100::mbar_init(&s.acc_full[i], 1);
             sm100::mbar_init(&s.acc_empty[i], 128);
         }
@@ -109,8 +140,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
         sm100::mbar_init(&s.mma_done, 1);
         sm100::fence_mbar_init();
     }
-    if (warp == 1) {
-        sm100::tmem_alloc(&s.tmem_base, 256);
+    if (warp == C::kMmaWarp) {
+        sm100::tmem_alloc(&s.tmem_base, C::kTmemCols);
         sm100::tmem_relinquish();
     }
     if (threadIdx.x < kTM) s.rowcnt[threadIdx.x] = 0;
@@ -120,60 +151,62 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
     const uint32_t tmem = s.tmem_base;
     bool failed = false;
 
-    if (warp == 0 && lane == 0) {
-        // ---- TMA producer ----
-        sm100::prefetch_tmap(&tmA);
-        sm100::prefetch_tmap(&tmB);
-        sm100::mbar_expect_tx(&s.a_full, kTileBytes);
-        sm100::tma_load_2d(s.a, &tmA, 0, (int)row0, &s.a_full);
-        sm100::tma_load_2d(s.a + kBoxBytes, &tmA, 64, (int)row0, &s.a_full);
-        for (int it = 0; it < n_tiles; ++it) {
-            const int st = it % kStages;
-            const uint32_t round = it / kStages;
-            if (!sm100::mbar_wait(&s.empty[st], (round & 1) ^ 1)) { failed = true; break; }
-            const int n0 = (t_begin + it) * kTN;
-            sm100::mbar_expect_tx(&s.full[st], kTileBytes);
-            sm100::tma_load_2d(s.b[st], &tmB, 0, n0, &s.full[st]);
-            sm100::tma_load_2d(s.b[st] + kBoxBytes, &tmB, 64, n0, &s.full[st]);
-        }
-        // drain: every issued load has landed before the CTA may exit
-        const int issued = failed ? 0 : n_tiles;
-        for (int it = max(0, issued - kStages); it < issued; ++it)
-            if (!sm100::mbar_wait(&s.full[it % kStages], (it / kStages) & 1)) failed = true;
-        if (!sm100::mbar_wait(&s.a_full, 0)) failed = true;
-    } else if (warp == 1 && lane == 0) {
-        // ---- MMA issuer ----
-        bool ok = sm100::mbar_wait(&s.a_full, 0);
-        const uint32_t a_base = sm100::smem_addr(s.a);
-        int it = 0;
-        for (; ok && it < n_tiles; ++it) {
-            const int st = it % kStages;
-            const int buf = it & 1;
-            if (!sm100::mbar_wait(&s.acc_empty[buf], ((it >> 1) & 1) ^ 1)) { ok = false; break; }
-            if (!sm100::mbar_wait(&s.full[st], (it / kStages) & 1)) { ok = false; break; }
-            sm100::tc_fence_after();
-            const uint32_t b_base = sm100::smem_addr(s.b[st]);
-            const uint32_t d_tmem = tmem + buf * kTN;
-#pragma unroll
-            for (int kk = 0; kk < kK / 16; ++kk) {
-                const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-                sm100::mma_bf16(d_tmem, sm100::smem_desc_sw128(a_base + off), sm100::smem_desc_sw128(b_base + off),
-                                kIdesc, kk > 0 ? 1u : 0u);
+    if (warp == C::kTmaWarp) {
+        if (lane == 0) {
+            // ---- TMA producer ----
+            sm100::prefetch_tmap(&tmA);
+            sm100::prefetch_tmap(&tmB);
+            sm100::mbar_expect_tx(&s.a_full, kTileBytes);
+            sm100::tma_load_2d(s.a, &tmA, 0, (int)row0, &s.a_full);
+            sm100::tma_load_2d(s.a + kBoxBytes, &tmA, 64, (int)row0, &s.a_full);
+            for (int it = 0; it < n_tiles; ++it) {
+                const int st = it % NS;
+                const uint32_t round = it / NS;
+                if (!sm100::mbar_wait(&s.empty[st], (round & 1) ^ 1)) { failed = true; break; }
+                const int n0 = (t_begin + it) * kTN;
+                sm100::mbar_expect_tx(&s.full[st], kTileBytes);
+                sm100::tma_load_2d(s.b[st], &tmB, 0, n0, &s.full[st]);
+                sm100::tma_load_2d(s.b[st] + kBoxBytes, &tmB, 64, n0, &s.full[st]);
             }
-            sm100::mma_commit(&s.empty[st]);
-            sm100::mma_commit(&s.acc_full[buf]);
+            // drain: every issued load has landed before the CTA may exit
+            const int issued = failed ? 0 : n_tiles;
+            for (int it = max(0, issued - NS); it < issued; ++it)
+                if (!sm100::mbar_wait(&s.full[it % NS], (it / NS) & 1)) failed = true;
+            if (!sm100::mbar_wait(&s.a_full, 0)) failed = true;
         }
-        failed = !ok;
-        // all issued MMAs complete before TMEM is released
-        sm100::mma_commit(&s.mma_done);
-        if (!sm100::mbar_wait(&s.mma_done, 0)) failed = true;
-    } else if (warp >= 4) {
+    } else if (warp == C::kMmaWarp) {
+        if (lane == 0) {
+            // ---- MMA issuer: tile `it` into accumulator it % NG ----
+            bool ok = sm100::mbar_wait(&s.a_full, 0);
+            const uint32_t a_base = sm100::smem_addr(s.a);
+            for (int it = 0; ok && it < n_tiles; ++it) {
+                const int st = it % NS;
+                const int buf = it % NG;
+                if (!sm100::mbar_wait(&s.acc_empty[buf], ((it / NG) & 1) ^ 1)) { ok = false; break; }
+                if (!sm100::mbar_wait(&s.full[st], (it / NS) & 1)) { ok = false; break; }
+                sm100::tc_fence_after();
+                const uint32_t b_base = sm100::smem_addr(s.b[st]);
+                const uint32_t d_tmem = tmem + buf * kTN;
+#pragma unroll
+                for (int kk = 0; kk < kK / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+                    sm100::mma_bf16(d_tmem, sm100::smem_desc_sw128(a_base + off),
+                                    sm100::smem_desc_sw128(b_base + off), kIdesc, kk > 0 ? 1u : 0u);
+                }
+                sm100::mma_commit(&s.empty[st]);
+                sm100::mma_commit(&s.acc_full[buf]);
+            }
+            failed = !ok;
+            // all issued MMAs complete before TMEM is released
+            sm100::mma_commit(&s.mma_done);
+            if (!sm100::mbar_wait(&s.mma_done, 0)) failed = true;
+        }
+    } else {
         // ---- epilogue: TMEM -> registers -> filter / store / top-16 ----
-        // group g drains the tiles it = g, g + 2, ...: accumulator buffer g,
-        // so the two run side by side (top-16: each group keeps its own 16)
-        constexpr int ngroups = 2;
-        const int g = (warp - 4) >> 2;
-        const int q4 = (warp - 4) & 3;  // TMEM lane quarter: warp % 4
+        // group g drains the tiles it = g, g + NG, ... from accumulator g, so
+        // the groups run side by side (top-16: each group keeps its own 16)
+        const int g = warp >> 2;
+        const int q4 = warp & 3;        // TMEM lane quarter: warp % 4
         const int rl = q4 * 32 + lane;  // row within the tile
         const int64_t row = row0 + rl;
         const bool vrow = row < p.rows;
@@ -184,126 +217,113 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
 #pragma unroll
             for (int j = 0; j < kTopA; ++j) best[j] = ~0ull;
         }
-        const int et = q4 * 32 + lane;                          // 0..127 within the group
-        float thr = INFINITY;                                   // kTop16: float of best[15]
-        float* row_vals = s.pass[g][q4][lane];
-        float cn_next = INFINITY;  // this thread's norm of the group's next tile, loaded one tile ahead
-        if (g < n_tiles) {
-            const int64_t c0 = (int64_t)(t_begin + g) * kTN + et;
-            cn_next = c0 < p.cols ? __ldg(p.cn + c0) : INFINITY;
-        }
-        for (int it = g; it < n_tiles; it += ngroups) {
-            const int buf = it & 1;
-            const int nb = (it / ngroups) & 1;                  // this group's norms buffer
+        float thr = INFINITY;  // kTop16: float of best[15]
+        float* row_vals = s.pass[warp][lane];
+        float* cnw = s.cn[warp];
+        // this lane's share of the warp's next tile norms, loaded one tile ahead
+        float4 cn_next = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+        if (g < n_tiles) cn_next = tile_norms4(p.cn, p.cols, t_begin + g, lane);
+        for (int it = g; it < n_tiles; it += NG) {
+            const int buf = it % NG;
             const int64_t n0 = (int64_t)(t_begin + it) * kTN;
-            // stage this tile's norms (the group's other buffer may still be read)
-            s.cn[g][nb][et] = cn_next;
-            if (it + ngroups < n_tiles) {
-                const int64_t c1 = (int64_t)(t_begin + it + ngroups) * kTN + et;
-                cn_next = c1 < p.cols ? __ldg(p.cn + c1) : INFINITY;
-            }
-            // every warp of the group passes this barrier once per tile, also
-            // after a failed wait, so the barrier count stays equal across warps
-            sm100::named_bar(1 + g, 128);
+            // stage this tile's norms in the warp's own buffer (warp-synchronous)
+            __syncwarp();
+            *reinterpret_cast<float4*>(cnw + 4 * lane) = cn_next;
+            __syncwarp();
+            if (it + NG < n_tiles) cn_next = tile_norms4(p.cn, p.cols, t_begin + it + NG, lane);
             if (failed) continue;
             // warp-uniform wait: the tcgen05.ld below needs every lane
-            const bool ok = __all_sync(0xffffffffu, sm100::mbar_wait(&s.acc_full[buf], (it >> 1) & 1));
+            const bool ok = __all_sync(0xffffffffu, sm100::mbar_wait(&s.acc_full[buf], (it / NG) & 1));
             if (!ok) { failed = true; continue; }
             sm100::tc_fence_after();
-            const float* cnb = s.cn[g][nb];
             const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + buf * kTN;
-            // two halves of 64 columns keep 64 accumulators in registers at a time
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t r[2][32];
-                sm100::tmem_ld32_async(tbase + h * 64, r[0]);
-                sm100::tmem_ld32_async(tbase + h * 64 + 32, r[1]);
+            // 32 columns at a time: 32 accumulators in registers
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld32_async(tbase + c * 32, r);
                 sm100::tmem_wait_ld();
-                if (h == 1) {
+                if (c == 3) {
                     // the accumulator is in registers: hand TMEM back to the MMA warp
                     sm100::tc_fence_before();
                     sm100::mbar_arrive(&s.acc_empty[buf]);
                 }
                 if (!vrow) continue;
+                const float* cnb = cnw + c * 32;
+                if (MODE == kStore) {
+                    float* out = p.dist + row * p.ld + n0 + c * 32;
+                    if (n0 + c * 32 + 32 <= p.cols && (p.ld & 3) == 0) {
 #pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const int c = 2 * h + cc;
-                    if (MODE == kStore) {
-                        float* out = p.dist + row * p.ld + n0 + c * 32;
-                        if (n0 + c * 32 + 32 <= p.cols && (p.ld & 3) == 0) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4) {
-                                float4 o;
-                                o.x = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 0]), cnb[c * 32 + j + 0]);
-                                o.y = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 1]), cnb[c * 32 + j + 1]);
-                                o.z = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 2]), cnb[c * 32 + j + 2]);
-                                o.w = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j + 3]), cnb[c * 32 + j + 3]);
-                                *reinterpret_cast<float4*>(out + j) = o;
-                            }
-                        } else {
-                            for (int j = 0; j < 32; ++j)
-                                if (n0 + c * 32 + j < p.cols)
-                                    out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j]), cnb[c * 32 + j]);
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 o;
+                            o.x = __fmaf_rn(-2.0f, __uint_as_float(r[j + 0]), cnb[j + 0]);
+                            o.y = __fmaf_rn(-2.0f, __uint_as_float(r[j + 1]), cnb[j + 1]);
+                            o.z = __fmaf_rn(-2.0f, __uint_as_float(r[j + 2]), cnb[j + 2]);
+                            o.w = __fmaf_rn(-2.0f, __uint_as_float(r[j + 3]), cnb[j + 3]);
+                            *reinterpret_cast<float4*>(out + j) = o;
                         }
                     } else {
-                        // Column j can enter when d <= tau (filter) or d <= the
-                        // current 16th best (top-16).  d = cn - 2 v is exact in
-                        // one fma because 2 v is exact.  Out-of-range columns
-                        // carry +inf norms and never pass.  Most groups of 32
-                        // have no such column: the fast pass takes their minimum
-                        // in four independent chains (norms four at a time), and
-                        // only a passing group builds its mask.
-                        const float lim = (MODE == kFilter) ? tau : thr;
-                        const float4* cn4 = reinterpret_cast<const float4*>(cnb + c * 32);
-                        float m0 = INFINITY, m1 = INFINITY, m2 = INFINITY, m3 = INFINITY;
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + c * 32 + j < p.cols) out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[j]), cnb[j]);
+                    }
+                } else {
+                    // Column j can enter when d <= tau (filter) or d <= the
+                    // current 16th best (top-16).  d = cn - 2 v is exact in
+                    // one fma because 2 v is exact.  Out-of-range columns
+                    // carry +inf norms and never pass.  Most groups of 32
+                    // have no such column: the fast pass takes their minimum
+                    // in four independent chains (norms four at a time), and
+                    // only a passing group builds its mask.
+                    const float lim = (MODE == kFilter) ? tau : thr;
+                    const float4* cn4 = reinterpret_cast<const float4*>(cnb);
+                    float m0 = INFINITY, m1 = INFINITY, m2 = INFINITY, m3 = INFINITY;
 #pragma unroll
-                        for (int j4 = 0; j4 < 8; ++j4) {
-                            const float4 n4 = cn4[j4];
-                            m0 = fminf(m0, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 0]), n4.x));
-                            m1 = fminf(m1, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 1]), n4.y));
-                            m2 = fminf(m2, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 2]), n4.z));
-                            m3 = fminf(m3, __fmaf_rn(-2.0f, __uint_as_float(r[cc][4 * j4 + 3]), n4.w));
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 n4 = cn4[j4];
+                        m0 = fminf(m0, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 0]), n4.x));
+                        m1 = fminf(m1, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 1]), n4.y));
+                        m2 = fminf(m2, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 2]), n4.z));
+                        m3 = fminf(m3, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 3]), n4.w));
+                    }
+                    uint32_t mask = 0;
+                    if (fminf(fminf(m0, m1), fminf(m2, m3)) <= lim) {
+                        uint32_t mk[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float d = __fmaf_rn(-2.0f, __uint_as_float(r[j]), cnb[j]);
+                            mk[j & 3] |= (d <= lim ? 1u : 0u) << j;
                         }
-                        uint32_t mask = 0;
-                        if (fminf(fminf(m0, m1), fminf(m2, m3)) <= lim) {
-                            uint32_t mk[4] = {0u, 0u, 0u, 0u};
+                        mask = (mk[0] | mk[1]) | (mk[2] | mk[3]);
+                    }
+                    if (mask) {
+                        // rare: copy the 32 values to this lane's shared row and
+                        // walk the set bits with a runtime index (keeps the hot
+                        // loop small and r[] in registers)
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                const float d = __fmaf_rn(-2.0f, __uint_as_float(r[cc][j]), cnb[c * 32 + j]);
-                                mk[j & 3] |= (d <= lim ? 1u : 0u) << j;
-                            }
-                            mask = (mk[0] | mk[1]) | (mk[2] | mk[3]);
-                        }
-                        if (mask) {
-                            // rare: copy the 32 values to this lane's shared row and
-                            // walk the set bits with a runtime index (keeps the hot
-                            // loop small and r[][] in registers)
+                        for (int j = 0; j < 32; ++j) row_vals[j] = __uint_as_float(r[j]);
+                        while (mask) {
+                            const int j = __ffs(mask) - 1;
+                            mask &= mask - 1;
+                            const float d = __fmaf_rn(-2.0f, row_vals[j], cnb[j]);
+                            const uint32_t col = (uint32_t)(n0 + c * 32 + j);
+                            if (MODE == kFilter) {
+                                const int at = atomicAdd(&s.rowcnt[rl], 1);  // shared by all groups
+                                if (at < p.cap)
+                                    p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + at] = dist_key(d, col);
+                            } else {
+                                const uint64_t key = dist_key(d, col);
+                                if (key < best[kTopA - 1]) {
+                                    best[kTopA - 1] = key;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) row_vals[j] = __uint_as_float(r[cc][j]);
-                            while (mask) {
-                                const int j = __ffs(mask) - 1;
-                                mask &= mask - 1;
-                                const float d = __fmaf_rn(-2.0f, row_vals[j], cnb[c * 32 + j]);
-                                const uint32_t col = (uint32_t)(n0 + c * 32 + j);
-                                if (MODE == kFilter) {
-                                    const int at = atomicAdd(&s.rowcnt[rl], 1);  // shared by both groups
-                                    if (at < p.cap)
-                                        p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + at] = dist_key(d, col);
-                                } else {
-                                    const uint64_t key = dist_key(d, col);
-                                    if (key < best[kTopA - 1]) {
-                                        best[kTopA - 1] = key;
-#pragma unroll
-                                        for (int q = kTopA - 1; q > 0; --q) {
-                                            if (best[q] < best[q - 1]) {
-                                                const uint64_t t = best[q];
-                                                best[q] = best[q - 1];
-                                                best[q - 1] = t;
-                                            }
+                                    for (int q = kTopA - 1; q > 0; --q) {
+                                        if (best[q] < best[q - 1]) {
+                                            const uint64_t t = best[q];
+                                            best[q] = best[q - 1];
+                                            best[q - 1] = t;
                                         }
-                                        if (best[kTopA - 1] != ~0ull)
-                                            thr = key_to_float_asc((uint32_t)(best[kTopA - 1] >> 32));
                                     }
+                                    if (best[kTopA - 1] != ~0ull)
+                                        thr = key_to_float_asc((uint32_t)(best[kTopA - 1] >> 32));
                                 }
                             }
                         }
@@ -321,12 +341,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dist_kernel(const __grid_con
     sm100::tc_fence_before();
     __syncthreads();
     sm100::tc_fence_after();
-    // filter: both groups have appended; the first group's threads publish the counts
-    if (MODE == kFilter && warp >= 4 && warp < 8) {
-        const int rl = (warp - 4) * 32 + lane;
+    // filter: every group has appended; the first group's threads publish the counts
+    if (MODE == kFilter && warp < 4) {
+        const int rl = warp * 32 + lane;
         if (row0 + rl < p.rows) p.surv_cnt[(size_t)(row0 + rl) * p.splits + blockIdx.x] = s.rowcnt[rl];
     }
-    if (warp == 1) sm100::tmem_dealloc(tmem, 256);
+    if (warp == C::kMmaWarp) sm100::tmem_dealloc(tmem, C::kTmemCols);
 }
 
 // ---- helpers ---------------------------------------------------------------
@@ -603,7 +623,8 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t rows) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static size_t tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
+template <int MODE>
+static size_t tc_smem_bytes() { return sizeof(TcSmem<MODE>) + 1024; }
 
 template <int MODE>
 static chm_status launch_tc(const __nv_bfloat16* a, int64_t rows, const __nv_bfloat16* b, int64_t cols,
@@ -614,10 +635,11 @@ static chm_status launch_tc(const __nv_bfloat16* a, int64_t rows, const __nv_bfl
     splits = std::max(1, std::min(splits, n_tiles));
     args.tiles_per_split = (n_tiles + splits - 1) / splits;
     args.splits = splits;
-    const size_t smem = tc_smem_bytes();
+    const size_t smem = tc_smem_bytes<MODE>();
+    static_assert(sizeof(TcSmem<MODE>) + 1024 <= 227 * 1024, "tc_dist_kernel shared memory");
     CHM_CUDA(cudaFuncSetAttribute(tc_dist_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(splits, (unsigned)((rows + kTM - 1) / kTM));
-    tc_dist_kernel<MODE><<<grid, kTcThreads, smem, st>>>(ma, mb, args);
+    tc_dist_kernel<MODE><<<grid, TcCfg<MODE>::kThreads, smem, st>>>(ma, mb, args);
     return launch_status("tc_dist_kernel");
 }
 
