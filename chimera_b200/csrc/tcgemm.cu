@@ -365,11 +365,26 @@ __device__ __forceinline__ float err_bound(float qnorm, float cnmax) {
            4e-6f * (cnmax + 2.0f * cmax * qnorm) + 1e-6f;
 }
 
-// Exact (sequential fma) dist of row q to centroid c.
+// Exact (sequential fma) dist of row q to centroid c.  Both rows are read
+// 16 bytes at a time when both are 16-byte aligned (the fma order is the same).
 __device__ __forceinline__ float exact_dist(const float* q, const float* c, float cn) {
     float acc = 0.0f;
+    if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(c)) & 15u) == 0) {
+        const float4* q4 = reinterpret_cast<const float4*>(q);
+        const float4* c4 = reinterpret_cast<const float4*>(c);
 #pragma unroll 8
-    for (int k = 0; k < kDim; ++k) acc = __fmaf_rn(q[k], c[k], acc);
+        for (int k4 = 0; k4 < kDim / 4; ++k4) {
+            const float4 qv = q4[k4];
+            const float4 cv = __ldg(c4 + k4);
+            acc = __fmaf_rn(qv.x, cv.x, acc);
+            acc = __fmaf_rn(qv.y, cv.y, acc);
+            acc = __fmaf_rn(qv.z, cv.z, acc);
+            acc = __fmaf_rn(qv.w, cv.w, acc);
+        }
+    } else {
+#pragma unroll 8
+        for (int k = 0; k < kDim; ++k) acc = __fmaf_rn(q[k], c[k], acc);
+    }
     return fsub(cn, fmul(2.0f, acc));
 }
 
@@ -399,7 +414,7 @@ __global__ void __launch_bounds__(kRerankThreads) probe_rerank_kernel(
     uint32_t* __restrict__ labels, int32_t* __restrict__ fallback_list, uint32_t* __restrict__ fallback_cnt) {
     __shared__ uint64_t s_keys[kSurvMax];
     __shared__ uint64_t s_ex[512];
-    __shared__ float s_q[kDim];
+    __shared__ alignas(16) float s_q[kDim];
     __shared__ int s_total, s_bad;
     const int64_t row = blockIdx.x;
     // fallback_cnt[1] is the tensor-core kernels' error flag: a launch that
@@ -582,7 +597,7 @@ __global__ void __launch_bounds__(1024) exact_rows_kernel(const float* __restric
                                                           const int32_t* __restrict__ list,
                                                           const uint32_t* __restrict__ count, float* __restrict__ scratch,
                                                           uint32_t* __restrict__ out_labels, uint32_t first = 0) {
-    __shared__ float s_q[kDim];
+    __shared__ alignas(16) float s_q[kDim];
     const uint32_t n = *count;
     float* d = scratch + (size_t)blockIdx.x * cols;
     for (uint32_t r = first + blockIdx.x; r < n; r += gridDim.x) {
