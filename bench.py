@@ -164,6 +164,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c3")
     ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--inflight", type=int, default=1,
+                    help="batches in flight at once (one GPU): each on its own stream with its own workspace")
     ap.add_argument("--recall-queries", type=int, default=256)
     ap.add_argument("--cpu-sample", type=int, default=32,
                     help="queries whose full-bit stage the CPU baseline times")
@@ -254,16 +256,22 @@ def main():
     B = args.batch
     params = dict(nprobe=cfg.nprobe, k_refine=cfg.k_refine, k_full_bit=cfg.k_full_bit, num_chunks=cfg.num_chunks,
                   k=cfg.k)
+    inflight = max(1, args.inflight) if world == 1 else 1
+    main_stream = torch.cuda.current_stream()
+    lanes = [main_stream] + [torch.cuda.Stream() for _ in range(inflight - 1)]
     if world == 1:
-        searcher = capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs())
+        searchers = [capi.Searcher(index, k=cfg.k, batch=B, **cfg.search_kwargs()) for _ in range(inflight)]
+        searcher = searchers[0]
         # one result buffer per step, so that every timed step's counts can be
         # checked after the timed region
         nbuf = args.warmup + args.steps
         res_bufs = [torch.empty(B, cfg.k, dtype=torch.int64, device="cuda") for _ in range(nbuf)]
         nres_bufs = [torch.empty(B, dtype=torch.int32, device="cuda") for _ in range(nbuf)]
-        search_device = lambda qb, i: searcher.search_device(qb, res_bufs[i], nres_bufs[i])
+        # step i runs on lane i % inflight (its own stream and workspace)
+        search_device = lambda qb, i: searchers[i % inflight].search_device(qb, res_bufs[i], nres_bufs[i],
+                                                                            stream=lanes[i % inflight])
         search_full = searcher.search
-        parallelism = "single GPU"
+        parallelism = "single GPU" if inflight == 1 else f"single GPU, {inflight} batches in flight"
     else:
         # the sharded protocol in native code: stage kernels and NCCL
         # collectives on one stream, one host call per batch
@@ -282,7 +290,7 @@ def main():
     stream = torch.cuda.current_stream()
     batches = [batch_at(i) for i in range(args.warmup + args.steps)]
     for i in range(args.warmup):
-        _, nres = search_device(batches[i], 0)
+        _, nres = search_device(batches[i], i)
     torch.cuda.synchronize()
     if nres.min().item() < 0:
         raise RuntimeError("stage-1 table overflow during warmup")
@@ -305,9 +313,13 @@ def main():
         barrier()
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
+        for ln in lanes[1:]:
+            ln.wait_stream(stream)
         timed_counts = []
         for i in range(args.steps):
             timed_counts.append(search_device(batches[args.warmup + i], args.warmup + i)[1])
+        for ln in lanes[1:]:
+            stream.wait_stream(ln)
         ev1.record(stream)
         torch.cuda.nvtx.range_pop()
         barrier()
@@ -322,17 +334,23 @@ def main():
 
     # ---- end-to-end through the public entry point, host buffers -----------
     hq = [batches[args.warmup + i].cpu().pin_memory() for i in range(args.steps)]
-    hres = torch.empty(B, cfg.k, dtype=torch.int64).pin_memory()
-    dq = torch.empty_like(batches[0])
+    hres = [torch.empty(B, cfg.k, dtype=torch.int64).pin_memory() for _ in lanes]
+    dq = [torch.empty_like(batches[0]) for _ in lanes]
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    for ln in lanes[1:]:
+        ln.wait_stream(stream)
     e2e_counts = []
     for i in range(args.steps):
-        dq.copy_(hq[i], non_blocking=True)
-        r, c = search_device(dq, args.warmup + i)
-        hres.copy_(r, non_blocking=True)
+        j = (args.warmup + i) % len(lanes)
+        with torch.cuda.stream(lanes[j]):
+            dq[j].copy_(hq[i], non_blocking=True)
+            r, c = search_device(dq[j], args.warmup + i)
+            hres[j].copy_(r, non_blocking=True)
         e2e_counts.append(c)
+    for ln in lanes[1:]:
+        stream.wait_stream(ln)
     e1.record(stream)
     barrier()
     ems = max_over_ranks(e0.elapsed_time(e1))
@@ -395,7 +413,8 @@ def main():
         "config": {"workload": f"{cfg.name}: {cfg.num_docs} docs, {int(ptr_full[-1])} tokens, "
                                f"{cfg.n_clusters} clusters, ex_bits {cfg.ex_bits}, nprobe {cfg.nprobe}, "
                                f"k_refine {cfg.k_refine}, k_full_bit {cfg.k_full_bit}, k {cfg.k}",
-                   "batch_queries": B, "l2": "inputs larger than L2 (index >> 126 MB)",
+                   "batch_queries": B, "batches_in_flight": inflight,
+                   "l2": "inputs larger than L2 (index >> 126 MB)",
                    "recall@100": recall, "recall_queries": nrec,
                    "latency_ms_single_query": lat, "parallelism": parallelism,
                    "stages_scope": "rank 0 index" + (" shard, exchange excluded" if world > 1 else "")},

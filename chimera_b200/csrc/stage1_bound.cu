@@ -308,6 +308,12 @@ __global__ void __launch_bounds__(kBPreThreads) bound_compact_kernel(const float
                                                                      uint64_t* __restrict__ ckeys,
                                                                      uint32_t* __restrict__ ccnt,
                                                                      const uint32_t* __restrict__ active) {
+    // Kept keys gather in shared memory (warp-aggregated shared atomics) and
+    // go out in coalesced runs, one global atomic per run: a global atomic
+    // per warp step, whose result the warp waits for, serialised the scan.
+    constexpr int kStage = 2 * 4 * kBPreThreads;  // one step adds at most 4 * kBPreThreads keys
+    __shared__ uint64_t s_buf[kStage];
+    __shared__ uint32_t s_n, s_base;
     const int q = blockIdx.y;
     if (b_inactive(active, q)) return;
     const uint32_t d = pivot[q] == kBNoPivot ? 0u : pivot[q];
@@ -316,6 +322,19 @@ __global__ void __launch_bounds__(kBPreThreads) bound_compact_kernel(const float
     const float* qs = S + (size_t)q * M;
     uint64_t* out = ckeys + (size_t)q * kBPreCap;
     const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    auto flush = [&]() {
+        const uint32_t n = s_n;
+        if (threadIdx.x == 0) s_base = n ? atomicAdd(ccnt + q, n) : 0u;
+        __syncthreads();
+        const uint32_t base = s_base;
+        for (uint32_t j = threadIdx.x; j < n; j += blockDim.x)
+            if (base + j < (uint32_t)kBPreCap) out[base + j] = s_buf[j];
+        __syncthreads();
+        if (threadIdx.x == 0) s_n = 0;
+        __syncthreads();
+    };
     for (int64_t b = i0; b < i1; b += 4 * (int64_t)blockDim.x) {
         float v[4];
 #pragma unroll
@@ -331,13 +350,15 @@ __global__ void __launch_bounds__(kBPreThreads) bound_compact_kernel(const float
             const uint32_t m = __ballot_sync(0xffffffffu, keep);
             if (m) {
                 uint32_t base = 0;
-                if (lane == 0) base = atomicAdd(ccnt + q, (uint32_t)__popc(m));
+                if (lane == 0) base = atomicAdd(&s_n, (uint32_t)__popc(m));
                 base = __shfl_sync(0xffffffffu, base, 0);
-                const uint32_t at = base + __popc(m & ((1u << lane) - 1));
-                if (keep && at < (uint32_t)kBPreCap) out[at] = ((uint64_t)bits << 32) | (uint32_t)(~(uint32_t)i);
+                if (keep) s_buf[base + __popc(m & ((1u << lane) - 1))] = ((uint64_t)bits << 32) | (uint32_t)(~(uint32_t)i);
             }
         }
+        __syncthreads();
+        if (s_n > (uint32_t)(kStage - 4 * kBPreThreads)) flush();  // room for the next step
     }
+    flush();
 }
 
 // Bitonic sort, descending, of n (power of two) 64-bit keys in shared memory.
