@@ -51,6 +51,7 @@ constexpr int kBxWarps = 32;           // exact CTA
 constexpr int kMapSlots = 8192;        // probed-cluster map per query (>= 2 x 32 x max nprobe / 8)
 constexpr uint64_t kMapEmpty = ~0ull;
 constexpr int kBPreThreads = 256;
+constexpr int kBUnroll = 8;             // loads in flight per thread in the scans over S
 constexpr int64_t kBPreCap = 65536;    // compacted keys per query (more: fallback)
 constexpr uint32_t kBNoPivot = 0xFFFFFFFFu;
 constexpr int kBMaxCand = 12288;       // K' bound (sort buffer 16384 keys)
@@ -213,15 +214,15 @@ __global__ void __launch_bounds__(kBPreThreads) bound_hist_kernel(const float* _
     const int64_t i0 = blockIdx.x * per, i1 = min(M, i0 + per);
     const float* qs = S + (size_t)q * M;
     uint32_t cnt = 0;
-    for (int64_t i = i0 + threadIdx.x; i < i1; i += 4 * (int64_t)blockDim.x) {
-        float v[4];
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += kBUnroll * (int64_t)blockDim.x) {
+        float v[kBUnroll];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kBUnroll; ++u) {
             const int64_t j = i + u * (int64_t)blockDim.x;
             v[u] = j < i1 ? qs[j] : 0.0f;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < kBUnroll; ++u)
             if (v[u] > 0.0f) {
                 atomicAdd(&h[__float_as_uint(v[u]) >> 20], 1u);
                 ++cnt;
@@ -311,7 +312,7 @@ __global__ void __launch_bounds__(kBPreThreads) bound_compact_kernel(const float
     // Kept keys gather in shared memory (warp-aggregated shared atomics) and
     // go out in coalesced runs, one global atomic per run: a global atomic
     // per warp step, whose result the warp waits for, serialised the scan.
-    constexpr int kStage = 2 * 4 * kBPreThreads;  // one step adds at most 4 * kBPreThreads keys
+    constexpr int kStage = 2 * kBUnroll * kBPreThreads;  // one step adds at most kBUnroll * kBPreThreads keys
     __shared__ uint64_t s_buf[kStage];
     __shared__ uint32_t s_n, s_base;
     const int q = blockIdx.y;
@@ -335,15 +336,15 @@ __global__ void __launch_bounds__(kBPreThreads) bound_compact_kernel(const float
         if (threadIdx.x == 0) s_n = 0;
         __syncthreads();
     };
-    for (int64_t b = i0; b < i1; b += 4 * (int64_t)blockDim.x) {
-        float v[4];
+    for (int64_t b = i0; b < i1; b += kBUnroll * (int64_t)blockDim.x) {
+        float v[kBUnroll];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kBUnroll; ++u) {
             const int64_t i = b + u * (int64_t)blockDim.x + threadIdx.x;
             v[u] = i < i1 ? qs[i] : 0.0f;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kBUnroll; ++u) {
             const int64_t i = b + u * (int64_t)blockDim.x + threadIdx.x;
             const uint32_t bits = __float_as_uint(v[u]);
             const bool keep = v[u] > 0.0f && (bits >> 20) >= d;
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(kBPreThreads) bound_compact_kernel(const float
             }
         }
         __syncthreads();
-        if (s_n > (uint32_t)(kStage - 4 * kBPreThreads)) flush();  // room for the next step
+        if (s_n > (uint32_t)(kStage - kBUnroll * kBPreThreads)) flush();  // room for the next step
     }
     flush();
 }
