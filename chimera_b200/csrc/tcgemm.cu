@@ -237,93 +237,100 @@ __global__ void __maxnreg__(TcCfg<MODE>::kMaxRegs) tc_dist_kernel(const __grid_c
             if (!ok) { failed = true; continue; }
             sm100::tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(q4 * 32) << 16) + buf * kTN;
-            // 32 columns at a time: 32 accumulators in registers
+            // two halves of 64 columns (one TMEM-load wait each) keep 64
+            // accumulators in registers at a time
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[32];
-                sm100::tmem_ld32_async(tbase + c * 32, r);
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r2[2][32];
+                sm100::tmem_ld32_async(tbase + h * 64, r2[0]);
+                sm100::tmem_ld32_async(tbase + h * 64 + 32, r2[1]);
                 sm100::tmem_wait_ld();
-                if (c == 3) {
+                if (h == 1) {
                     // the accumulator is in registers: hand TMEM back to the MMA warp
                     sm100::tc_fence_before();
                     sm100::mbar_arrive(&s.acc_empty[buf]);
                 }
                 if (!vrow) continue;
-                const float* cnb = cnw + c * 32;
-                if (MODE == kStore) {
-                    float* out = p.dist + row * p.ld + n0 + c * 32;
-                    if (n0 + c * 32 + 32 <= p.cols && (p.ld & 3) == 0) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 o;
-                            o.x = __fmaf_rn(-2.0f, __uint_as_float(r[j + 0]), cnb[j + 0]);
-                            o.y = __fmaf_rn(-2.0f, __uint_as_float(r[j + 1]), cnb[j + 1]);
-                            o.z = __fmaf_rn(-2.0f, __uint_as_float(r[j + 2]), cnb[j + 2]);
-                            o.w = __fmaf_rn(-2.0f, __uint_as_float(r[j + 3]), cnb[j + 3]);
-                            *reinterpret_cast<float4*>(out + j) = o;
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int c = 2 * h + cc;
+                    const uint32_t* r = r2[cc];
+                    const float* cnb = cnw + c * 32;
+                    if (MODE == kStore) {
+                        float* out = p.dist + row * p.ld + n0 + c * 32;
+                        if (n0 + c * 32 + 32 <= p.cols && (p.ld & 3) == 0) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                float4 o;
+                                o.x = __fmaf_rn(-2.0f, __uint_as_float(r[j + 0]), cnb[j + 0]);
+                                o.y = __fmaf_rn(-2.0f, __uint_as_float(r[j + 1]), cnb[j + 1]);
+                                o.z = __fmaf_rn(-2.0f, __uint_as_float(r[j + 2]), cnb[j + 2]);
+                                o.w = __fmaf_rn(-2.0f, __uint_as_float(r[j + 3]), cnb[j + 3]);
+                                *reinterpret_cast<float4*>(out + j) = o;
+                            }
+                        } else {
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + c * 32 + j < p.cols) out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[j]), cnb[j]);
                         }
                     } else {
-                        for (int j = 0; j < 32; ++j)
-                            if (n0 + c * 32 + j < p.cols) out[j] = __fmaf_rn(-2.0f, __uint_as_float(r[j]), cnb[j]);
-                    }
-                } else {
-                    // Column j can enter when d <= tau (filter) or d <= the
-                    // current 16th best (top-16).  d = cn - 2 v is exact in
-                    // one fma because 2 v is exact.  Out-of-range columns
-                    // carry +inf norms and never pass.  Most groups of 32
-                    // have no such column: the fast pass takes their minimum
-                    // in four independent chains (norms four at a time), and
-                    // only a passing group builds its mask.
-                    const float lim = (MODE == kFilter) ? tau : thr;
-                    const float4* cn4 = reinterpret_cast<const float4*>(cnb);
-                    float m0 = INFINITY, m1 = INFINITY, m2 = INFINITY, m3 = INFINITY;
+                        // Column j can enter when d <= tau (filter) or d <= the
+                        // current 16th best (top-16).  d = cn - 2 v is exact in
+                        // one fma because 2 v is exact.  Out-of-range columns
+                        // carry +inf norms and never pass.  Most groups of 32
+                        // have no such column: the fast pass takes their minimum
+                        // in four independent chains (norms four at a time), and
+                        // only a passing group builds its mask.
+                        const float lim = (MODE == kFilter) ? tau : thr;
+                        const float4* cn4 = reinterpret_cast<const float4*>(cnb);
+                        float m0 = INFINITY, m1 = INFINITY, m2 = INFINITY, m3 = INFINITY;
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 n4 = cn4[j4];
-                        m0 = fminf(m0, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 0]), n4.x));
-                        m1 = fminf(m1, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 1]), n4.y));
-                        m2 = fminf(m2, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 2]), n4.z));
-                        m3 = fminf(m3, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 3]), n4.w));
-                    }
-                    uint32_t mask = 0;
-                    if (fminf(fminf(m0, m1), fminf(m2, m3)) <= lim) {
-                        uint32_t mk[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float d = __fmaf_rn(-2.0f, __uint_as_float(r[j]), cnb[j]);
-                            mk[j & 3] |= (d <= lim ? 1u : 0u) << j;
+                        for (int j4 = 0; j4 < 8; ++j4) {
+                            const float4 n4 = cn4[j4];
+                            m0 = fminf(m0, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 0]), n4.x));
+                            m1 = fminf(m1, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 1]), n4.y));
+                            m2 = fminf(m2, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 2]), n4.z));
+                            m3 = fminf(m3, __fmaf_rn(-2.0f, __uint_as_float(r[4 * j4 + 3]), n4.w));
                         }
-                        mask = (mk[0] | mk[1]) | (mk[2] | mk[3]);
-                    }
-                    if (mask) {
-                        // rare: copy the 32 values to this lane's shared row and
-                        // walk the set bits with a runtime index (keeps the hot
-                        // loop small and r[] in registers)
+                        uint32_t mask = 0;
+                        if (fminf(fminf(m0, m1), fminf(m2, m3)) <= lim) {
+                            uint32_t mk[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) row_vals[j] = __uint_as_float(r[j]);
-                        while (mask) {
-                            const int j = __ffs(mask) - 1;
-                            mask &= mask - 1;
-                            const float d = __fmaf_rn(-2.0f, row_vals[j], cnb[j]);
-                            const uint32_t col = (uint32_t)(n0 + c * 32 + j);
-                            if (MODE == kFilter) {
-                                const int at = atomicAdd(&s.rowcnt[rl], 1);  // shared by all groups
-                                if (at < p.cap)
-                                    p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + at] = dist_key(d, col);
-                            } else {
-                                const uint64_t key = dist_key(d, col);
-                                if (key < best[kTopA - 1]) {
-                                    best[kTopA - 1] = key;
+                            for (int j = 0; j < 32; ++j) {
+                                const float d = __fmaf_rn(-2.0f, __uint_as_float(r[j]), cnb[j]);
+                                mk[j & 3] |= (d <= lim ? 1u : 0u) << j;
+                            }
+                            mask = (mk[0] | mk[1]) | (mk[2] | mk[3]);
+                        }
+                        if (mask) {
+                            // rare: copy the 32 values to this lane's shared row and
+                            // walk the set bits with a runtime index (keeps the hot
+                            // loop small and r[] in registers)
 #pragma unroll
-                                    for (int q = kTopA - 1; q > 0; --q) {
-                                        if (best[q] < best[q - 1]) {
-                                            const uint64_t t = best[q];
-                                            best[q] = best[q - 1];
-                                            best[q - 1] = t;
+                            for (int j = 0; j < 32; ++j) row_vals[j] = __uint_as_float(r[j]);
+                            while (mask) {
+                                const int j = __ffs(mask) - 1;
+                                mask &= mask - 1;
+                                const float d = __fmaf_rn(-2.0f, row_vals[j], cnb[j]);
+                                const uint32_t col = (uint32_t)(n0 + c * 32 + j);
+                                if (MODE == kFilter) {
+                                    const int at = atomicAdd(&s.rowcnt[rl], 1);  // shared by all groups
+                                    if (at < p.cap)
+                                        p.surv[((size_t)row * p.splits + blockIdx.x) * p.cap + at] = dist_key(d, col);
+                                } else {
+                                    const uint64_t key = dist_key(d, col);
+                                    if (key < best[kTopA - 1]) {
+                                        best[kTopA - 1] = key;
+#pragma unroll
+                                        for (int q = kTopA - 1; q > 0; --q) {
+                                            if (best[q] < best[q - 1]) {
+                                                const uint64_t t = best[q];
+                                                best[q] = best[q - 1];
+                                                best[q - 1] = t;
+                                            }
                                         }
+                                        if (best[kTopA - 1] != ~0ull)
+                                            thr = key_to_float_asc((uint32_t)(best[kTopA - 1] >> 32));
                                     }
-                                    if (best[kTopA - 1] != ~0ull)
-                                        thr = key_to_float_asc((uint32_t)(best[kTopA - 1] >> 32));
                                 }
                             }
                         }
