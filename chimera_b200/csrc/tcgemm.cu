@@ -720,10 +720,10 @@ static ProbePlan probe_plan(int64_t rows, int64_t nc, int nprobe) {
     p.nc = nc;
     p.nprobe = nprobe;
     p.kc = std::min<int64_t>(nc, std::min(512, nprobe + 64));
-    // a prefix sample of nc / 16 centroids, at most 65,536 (at least 4 kc); a
+    // a prefix sample of nc / 32 centroids, at most 65,536 (at least 4 kc); a
     // larger sample costs more in the threshold pass (its dists are written
     // out and selected per row) than it saves in the re-rank
-    p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, std::min<int64_t>(nc / 16, 65536)));
+    p.prefix = (int)std::min<int64_t>(nc, std::max<int64_t>(4 * p.kc, std::min<int64_t>(nc / 32, 65536)));
     p.prefix = (int)std::min<int64_t>(nc, ((p.prefix + kTN - 1) / kTN) * kTN);
     // the threshold is the kthr-th smallest prefix dist, kthr chosen so that
     // about 4 kc centroids pass the filter: enough for the re-rank's kc + 1
