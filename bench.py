@@ -118,10 +118,10 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows), "source": "nvml" if self._nv else "nvidia-smi"}
 
 
-# DRAM bytes per unit of work of the dominant kernel, from the ncu capture in
-# profiles/stage1_bound_refine_c3s_b32.md (c3s corpus, 32 queries: the 1-bit
-# tensor-core refinement over token-order codes read + wrote 153.9 MB for
-# 6.30 M refined tokens), scaled here by this run's refined tokens.
+# DRAM bytes per unit of work of the dominant kernel, from one ncu capture of
+# it on the c3s corpus with 32 queries (the 1-bit tensor-core refinement over
+# token-order codes read + wrote 153.9 MB for 6.30 M refined tokens), scaled
+# here by this run's refined tokens.
 NCU_TRAFFIC_PER_UNIT = {"refine_1bit": 24.4}
 
 METRIC = {"c3": "QPS at Recall@100 (C3 passage corpus)", "c4": "QPS at Recall@100 (C4 long-document corpus)",
