@@ -21,7 +21,7 @@
 // certificate over the 32 candidates.
 //
 // GEMM kernel: one CTA = 128 query rows x a range of 128-centroid tiles.
-// One warp issues TMA loads (A once, B through a 3- or 4-stage ring), one
+// One warp issues TMA loads (A once, B through a 4-stage ring), one
 // owns TMEM and issues tcgen05.mma (M=128, N=128, K=16 x 8) into one TMEM
 // accumulator per epilogue group, and the epilogue groups (four warps each,
 // warps 0 .. 4 G - 1, so that warp % 4 is the TMEM lane quarter) drain the
