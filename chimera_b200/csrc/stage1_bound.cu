@@ -732,6 +732,17 @@ size_t bound_bytes(const chm_index* idx, int nq, int nprobe, int k_refine) {
     return s.s.off;
 }
 
+// SMs of the current device (148 on B200 when none is visible).
+static int bound_sms() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                   cudaSuccess || sms <= 0) {
+        (void)cudaGetLastError();
+        return 148;
+    }
+    return sms;
+}
+
 // The dense-bound pass over `nq` queries.  need_fb[q] = 1 marks the queries
 // the hash-table path must redo; the others have their refined list written.
 chm_status bound_run(const chm_index* idx, int nq, const float* lut, const float* cb1, const uint32_t* labels,
@@ -783,9 +794,23 @@ chm_status bound_run(const chm_index* idx, int nq, const float* lut, const float
         const size_t ex_smem = (size_t)kQ * kLutPerQ * 4 + (size_t)kMapSlots * 8 + kBxWarps * 32 * 4 + kQ * 4;
         CHM_CUDA(cudaFuncSetAttribute(bound_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)ex_smem));
-        // one resident CTA per SM; about two waves over the batch
-        const int gx = (int)std::max<int64_t>(1, std::min<int64_t>((k + kBxWarps - 1) / kBxWarps,
-                                                                   (2 * 148 + nq - 1) / nq));
+        // One resident CTA per SM.  The CTAs per query (gx) minimise the
+        // waves times a CTA's time, setup (the LUTs and the cluster map, about
+        // 0.4% of one query's work) plus 1/gx of the query's candidates: at 128
+        // queries gx = 8 fills 6.9 waves of 148 (gx = 3 left 40% of the SMs idle
+        // in its third wave).
+        const int sms = bound_sms();
+        const int gmax = (int)std::max<int64_t>(1, std::min<int64_t>(1024, (k + kBxWarps - 1) / kBxWarps));
+        int gx = 1;
+        double best = 1e300;
+        for (int g = 1; g <= gmax; ++g) {
+            const double waves = (double)(((int64_t)nq * g + sms - 1) / sms);
+            const double cost = waves * (0.004 + 1.0 / g);
+            if (cost < best - 1e-9) {
+                best = cost;
+                gx = g;
+            }
+        }
         bound_exact_kernel<<<dim3((unsigned)gx, (unsigned)nq), kBxWarps * 32, ex_smem, st>>>(x);
         CHM_TRY(launch_status("bound_exact_kernel"));
         int fsort = 1;
